@@ -1,0 +1,369 @@
+#!/usr/bin/env python3
+"""LSSA-B8 contract attention on B200 -- benchmark (one JSON line on rank 0).
+
+Workload (BASELINE.json configs[1] = config 2): Llama-3.1-8B-shaped causal GQA prefill, B=4,
+32 query / 8 kv heads, dh 128, T 2048, bf16 inputs N(0,1) from seed (1% of K channels x8),
+sink off.  One step = one full drop-in prefill (PREP quantisers + the tcgen05 prefill kernel)
+over inputs resident in HBM.  L2 is flushed (a 512 MB write) before every timed step, outside
+the timed events.  Also measured: config 3 split-KV decode (KV lattice GB/s), the end-to-end
+public-API call with pinned host buffers, the dominant kernel's roofline, clocks, and the CPU
+oracle port on the host cores.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+N > 1 (torchrun): weak scaling -- each rank runs its own config-2 job (rank-specific seed);
+value = all ranks' ops / max-over-ranks time; the NCCL all-gather of the outputs is timed
+separately ("gather").  --impl reference: the reference algorithm's CPU implementation (the
+oracle port; the reference's own code is Python that cannot run outside its checkout) on the
+host cores, rank 0 only.
+"""
+import argparse
+import hashlib
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "LSSA-B8 attn: prefill % int8 MMA peak; decode KV GB/s; 0 bit diffs vs ref"
+CFG = dict(B=4, H=32, KVH=8, dh=128, T=2048, outliers=0.01)
+DEC = dict(B=32, H=32, KVH=8, dh=128, L=8192, nsplit=16)
+
+
+def prefill_ops(B, H, T, dh):
+    """Algorithmic int8 ops: 4*dh per visible (row, key) pair (QK^T and PV, 2 ops per MAC)."""
+    return 4 * dh * B * H * T * (T + 1) // 2
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return dict(hbm=float(d["hbm_gbs"]), bf16=float(d["bf16_tflops"]), bf16_sust=float(d["bf16_tflops_sustained"]),
+                    src="measured")
+    return dict(hbm=6650.0, bf16=1590.0, bf16_sust=1400.0, src="fallback")
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region (clocks, throttle reasons)."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), "--query-gpu=" + self.Q,
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in getattr(self, "lines", []):
+            f = [x.strip() for x in l.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def sha(a):
+    import numpy as np
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+def golden_cfg2():
+    p = os.path.join(ROOT, "tests", "golden", "golden.json")
+    if not os.path.exists(p):
+        return None
+    with open(p) as f:
+        return json.load(f).get("cfg2")
+
+
+def run_gpu(args):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from lockstep_b200 import attention as A
+    from lockstep_b200 import decode as D
+    from lockstep_b200 import workloads as W
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    peaks = measured_peaks()
+    int8_peak = 2.0 * peaks["bf16"]            # dense int8 = 2x dense bf16 on B200
+    # ---------------------------------------------------------------- inputs (HBM resident)
+    seed = rank
+    q, k, v = W.prefill_inputs(CFG["B"], CFG["H"], CFG["KVH"], CFG["T"], CFG["dh"], outliers=CFG["outliers"], seed=seed)
+    qh = torch.from_numpy(q).to(torch.bfloat16).pin_memory()
+    kh = torch.from_numpy(k).to(torch.bfloat16).pin_memory()
+    vh = torch.from_numpy(v).to(torch.bfloat16).pin_memory()
+    qd, kd, vd = qh.to(dev), kh.to(dev), vh.to(dev)
+    out = torch.empty((CFG["B"], CFG["T"], CFG["H"], CFG["dh"]), dtype=torch.bfloat16, device=dev)
+    flush = torch.empty(512 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    ops = prefill_ops(CFG["B"], CFG["H"], CFG["T"], CFG["dh"])
+
+    def step():
+        A.prefill(qd, kd, vd, out=out, check=False)
+
+    # correctness of this very workload: digests vs the reference's recorded output (rank 0 seed)
+    step()
+    torch.cuda.synchronize()
+    A.check_device_errors(dev)
+    bit_check = None
+    g = golden_cfg2()
+    if g is not None and seed == 0:
+        host = out.cpu().view(torch.int16).numpy().view(np.uint16)
+        bit_check = all(sha(host[b]) == g["b8_per_batch"][b] for b in range(CFG["B"]))
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    with Clocks(local) as clk:
+        for i in range(args.steps):
+            flush.fill_(float(i))                    # L2 flush, outside the timed events
+            evs[i][0].record()
+            step()
+            evs[i][1].record()
+        torch.cuda.synchronize()
+    barrier()
+    step_ms = [a.elapsed_time(b) for a, b in evs]
+    t_ms = sum(step_ms) / len(step_ms)
+    if world > 1:
+        tt = torch.tensor([t_ms], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t_ms = float(tt.item())
+    value = world * ops / (t_ms * 1e-3) / 1e12          # TOPS, whole job
+
+    # ---------------------------------------------------------------- dominant kernel alone
+    Tp = A.tpad(CFG["T"])
+    q8, eq = A.quant_rows(qd)
+    k8, ek, _ = A.quant_blocks(kd, 0)
+    v8, ev, _ = A.quant_blocks(vd, 0)
+    kern_ms = []
+    for i in range(args.steps + args.warmup):
+        flush.fill_(float(i))
+        a_, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a_.record()
+        A.prefill_lattice(q8, eq, k8, ek, v8, ev, None, CFG["T"], out=out)
+        b_.record()
+        torch.cuda.synchronize()
+        if i >= args.warmup:
+            kern_ms.append(a_.elapsed_time(b_))
+    kms = sum(kern_ms) / len(kern_ms)
+    achieved = ops / (kms * 1e-3) / 1e12
+    roofline = {"bound": "tensor", "kernel": "prefill_kernel<128,false,bf16>", "achieved": round(achieved, 2),
+                "peak": round(int8_peak, 1), "unit": "TOPS", "frac": round(achieved / int8_peak, 4),
+                "peak_source": "2 x %s bf16 dense (cuBLAS burst %.1f TF/s), int8 dense rate = 2x bf16 on B200"
+                               % (peaks["src"], peaks["bf16"]),
+                "traffic": None, "kernel_ms": round(kms, 4), "algorithmic_ops_per_launch": ops}
+
+    # ---------------------------------------------------------------- end to end (public API)
+    qo = torch.empty_like(out, device="cpu").pin_memory()
+    e2e_ms = []
+    stream = torch.cuda.current_stream()
+    for i in range(args.warmup + args.steps):
+        flush.fill_(float(i))
+        a_, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a_.record()
+        qd.copy_(qh, non_blocking=True)
+        kd.copy_(kh, non_blocking=True)
+        vd.copy_(vh, non_blocking=True)
+        A.prefill(qd, kd, vd, out=out, check=False)
+        qo.copy_(out, non_blocking=True)
+        b_.record()
+        stream.synchronize()
+        if i >= args.warmup:
+            e2e_ms.append(a_.elapsed_time(b_))
+    e2e = sum(e2e_ms) / len(e2e_ms)
+    if world > 1:
+        tt = torch.tensor([e2e], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e2e = float(tt.item())
+    h2d = (qh.numel() + kh.numel() + vh.numel()) * 2
+    d2h = out.numel() * 2
+
+    # ---------------------------------------------------------------- decode (config 3)
+    dq, dk, dv = W.decode_inputs(DEC["B"], DEC["H"], DEC["KVH"], DEC["L"], DEC["dh"], seed=seed)
+    dqd = torch.from_numpy(dq).to(torch.bfloat16).to(dev)
+    kv = D.contiguous_kv(torch.from_numpy(dk).to(torch.bfloat16).to(dev),
+                         torch.from_numpy(dv).to(torch.bfloat16).to(dev), sink=False)
+    del dk, dv
+    dout = torch.empty((DEC["B"], DEC["H"], DEC["dh"]), dtype=torch.bfloat16, device=dev)
+    split = DEC["L"] // 128 // DEC["nsplit"]
+    for _ in range(args.warmup):
+        D.decode(dqd, kv, split_blocks=split, out=dout, check=False)
+    dec_ms = []
+    for i in range(args.steps):
+        flush.fill_(float(i))
+        a_, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a_.record()
+        D.decode(dqd, kv, split_blocks=split, out=dout, check=False)
+        b_.record()
+        torch.cuda.synchronize()
+        dec_ms.append(a_.elapsed_time(b_))
+    dms = sum(dec_ms) / len(dec_ms)
+    lattice_bytes = DEC["B"] * DEC["KVH"] * DEC["L"] * DEC["dh"] * 2
+    dec_gbs = lattice_bytes / (dms * 1e-3) / 1e9
+    A.check_device_errors(dev)
+    decode = {"config": "cfg3 B32 H32/KVH8 dh128 L8192, 16 splits, sink off", "ms_per_step": round(dms, 4),
+              "kv_gbps": round(dec_gbs, 1), "frac_hbm": round(dec_gbs / peaks["hbm"], 4),
+              "hbm_peak_gbps": peaks["hbm"], "algorithmic_bytes": lattice_bytes}
+
+    gather = None
+    if world > 1:
+        bufs = [torch.empty_like(out) for _ in range(world)]
+        barrier()
+        a_, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a_.record()
+        for _ in range(args.steps):
+            dist.all_gather(bufs, out)
+        b_.record()
+        torch.cuda.synchronize()
+        gms = a_.elapsed_time(b_) / args.steps
+        tt = torch.tensor([gms], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        gather = {"ms_per_step": round(float(tt.item()), 4), "bytes_per_rank": out.numel() * 2}
+        del bufs
+
+    launches_per_step = 4                          # quant_rows, quant_blocks x2, prefill_kernel
+    line = {
+        "metric": METRIC, "value": round(value, 3), "unit": "TOPS", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(t_ms, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8 (bf16 in/out, int32 accumulate, binary32 fold)", "data": "synthetic",
+        "config": {"workload": "cfg2 causal GQA prefill (Llama-3.1-8B shape)", "B": CFG["B"], "H": CFG["H"],
+                   "KVH": CFG["KVH"], "dh": CFG["dh"], "T": CFG["T"], "sink": False, "outliers": "1% K channels x8",
+                   "l2": "flushed (512 MB write) before each timed step", "parallelism": "dp%d (independent jobs)" % world},
+        "prefill_frac_int8_peak": round(value / world / int8_peak, 4),
+        "bit_exact_vs_reference": bit_check,
+        "roofline": roofline,
+        "e2e": {"value": round(world * ops / (e2e * 1e-3) / 1e12, 3), "unit": "TOPS", "ms_per_step": round(e2e, 4),
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "api": "lockstep_b200.attention.prefill (pinned host q/k/v -> device -> host out)"},
+        "decode": decode,
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clk.summary(),
+    }
+    if gather:
+        line["gather"] = gather
+    if rank == 0 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(sample_batches=1)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def cpu_baseline(sample_batches=1):
+    """The oracle port (plain C, OpenMP over (head, row)) on all host cores, on a bounded
+    sample of the config-2 workload: the first `sample_batches` batch elements (all heads)."""
+    import numpy as np
+    import oracle as O
+    from lockstep_b200 import workloads as W
+    q, k, v = W.prefill_inputs(CFG["B"], CFG["H"], CFG["KVH"], CFG["T"], CFG["dh"], outliers=CFG["outliers"], seed=0)
+    nt = os.cpu_count() or 1
+    t0 = time.time()
+    for b in range(sample_batches):
+        O.attention(q[b], k[b], v[b], nthreads=nt)
+    dt = time.time() - t0
+    ops = prefill_ops(sample_batches, CFG["H"], CFG["T"], CFG["dh"])
+    return {"value": round(ops / dt / 1e12, 5), "unit": "TOPS", "cores": nt, "kind": "port",
+            "sample": "%d of %d batch elements of cfg2 (all 32 heads, T=2048), PREP + fold, %.1f s"
+                      % (sample_batches, CFG["B"], dt)}
+
+
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import oracle as O
+    O.build()
+    times, cb = [], None
+    for i in range(args.warmup + args.steps):
+        t0 = time.time()
+        cb = cpu_baseline(sample_batches=1)
+        if i >= args.warmup:
+            times.append(time.time() - t0)
+    ops = prefill_ops(1, CFG["H"], CFG["T"], CFG["dh"])
+    ms = sum(times) / len(times) * 1e3
+    val = ops / (ms * 1e-3) / 1e12
+    cb["value"] = round(val, 5)
+    line = {"impl": "reference", "metric": METRIC, "value": round(val, 5), "unit": "TOPS", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 2), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8 (int32/int64 integer chain, binary32 fold)",
+            "data": "synthetic",
+            "config": {"workload": "cfg2 causal GQA prefill (Llama-3.1-8B shape)", "B": CFG["B"], "H": CFG["H"],
+                       "KVH": CFG["KVH"], "dh": CFG["dh"], "T": CFG["T"],
+                       "sample_per_step": "1 batch element (all heads)"},
+            "cpu_baseline": cb,
+            "e2e": {"value": round(val, 5), "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "note": "the reference's CPU path is Python inside its checkout; its algorithm runs here as the "
+                    "C oracle port (bit-identical to it on the committed golden fixtures)"}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_gpu(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,127 @@
+/*
+ * lssab8.h -- C ABI of liblssab8_b200.so: LSSA-B8 / B9.1 contract attention on B200 (sm_100a).
+ *
+ * Plain pointers and sizes only.  All device pointers live on the CUDA device that is current
+ * when the call is made; every call is asynchronous on `stream` (a cudaStream_t, NULL = the
+ * legacy default stream) and never allocates device memory: buffers, including workspaces,
+ * belong to the caller.  Every entry point returns 0 on success or a LSSAB8_E* code; no C++
+ * exception crosses the ABI.  Calls on different streams are independent (thread-safe per
+ * stream); the device error word is per device.
+ *
+ * Reference interfaces replaced (paths inside the reference project):
+ *   reference/lssab8_torch.py:103-272  make_lssab8_long_attn(...) -> attn(module, q, k, v, mask)
+ *   reference/lssab8_torch.py:275-281  make_lssab8_attn
+ *   reference/lssab9_torch.py:68-327   make_lssab9_long_attn(..., sink_alone=True)
+ *   reference/lssab8_golden.py:341-346 lssab8_attention;  :200-338 lssab8_core
+ *   reference/lssab8_golden.py:350-394 lssab8_row_segments (split-KV decode structure)
+ *   reference/lssab_golden.py:214-235  lssab_quantize (PREP);  reference/t10_attn.py:40-48 quant_rows;
+ *   reference/lssab_torch.py:62-85     quant_pow2_blocks;  reference/lssab9_torch.py:46-65,121-132
+ *
+ * Strides are in ELEMENTS (not bytes), int64[4] unless stated.
+ * dtype codes: 0 = float32, 1 = float16, 2 = bfloat16.
+ */
+#ifndef LSSAB8_H
+#define LSSAB8_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  LSSAB8_OK = 0,
+  LSSAB8_EARG = 1,          /* bad shape, stride, dtype or null pointer                      */
+  LSSAB8_EUNSUPPORTED = 2,  /* a contract-valid input these kernels do not cover (e.g. dh)    */
+  LSSAB8_ECUDA = 3,         /* a CUDA runtime/driver call failed                              */
+  LSSAB8_EWORKSPACE = 4,    /* the caller's workspace is smaller than *_workspace_size()      */
+  LSSAB8_EDEVICE = 5        /* the device error word is nonzero (lssab8_device_errors)        */
+};
+
+/* device error bits (OR-accumulated by kernels; read with lssab8_device_errors) */
+enum {
+  LSSAB8_DEV_EV_RANGE = 1,  /* e_v outside [-32, 40]: reference/lssab9_torch.py:158 assert    */
+  LSSAB8_DEV_TIMEOUT = 2,   /* a bounded pipeline wait gave up                                */
+  LSSAB8_DEV_BAD_PAGE = 4   /* a block-table entry outside [0, num_pages)                     */
+};
+
+/* Library identity: writes "lssab8-b200 <version> T2=<sha256 of the T2 csv>" (NUL-terminated)
+ * into buf.  The digest is recomputed from the table compiled into the device code, so it
+ * pins the constants (reference/lssab8_golden.py:117-128).  Returns LSSAB8_EARG if buflen is
+ * too small (needs 128 bytes). */
+int lssab8_version(char* buf, int buflen);
+
+/* Human-readable text for a status code. */
+const char* lssab8_strerror(int code);
+
+/* Synchronise `stream`, store the current device's error word in *bits, clear it if `clear`. */
+int lssab8_device_errors(int clear, void* stream, int* bits);
+
+/* ---------------------------------------------------------------- PREP (P1 / P2 / P3) */
+
+/* P1: per-(row) pow2 quantiser.  x [B, H, T, dh] (strides xs) -> q8 [B, H, Tpad, dh] int8 and
+ * eq [B, H, Tpad] int32, rows >= T zero.  reference/t10_attn.py:40-48. */
+int lssab8_quant_rows(const void* x, int dtype, int B, int H, int T, int dh, const int64_t* xs, int Tpad,
+                      int8_t* q8, int32_t* eq, void* stream);
+
+/* P2/P3: per-(128-key block, kv head) quantiser.  x [B, KVH, T, dh] -> x8 [B, KVH, Tpad, dh],
+ * e [B, KVH, ceil(T/128)], e0 [B, KVH] (mode 2 only).  mode 0 = B8 grid
+ * (reference/lssab_torch.py:62-85), 1 = B9 value grid (reference/lssab9_torch.py:46-65,158),
+ * 2 = B9.1 sink_alone value grid (reference/lssab9_torch.py:124-132). */
+int lssab8_quant_blocks(const void* x, int dtype, int B, int KVH, int T, int dh, const int64_t* xs, int Tpad,
+                        int mode, int8_t* x8, int32_t* e, int32_t* e0, void* stream);
+
+/* --------------------------------------------------------------------------- prefill */
+
+/* Causal GQA prefill on a prepared lattice (the output of the two quantisers with
+ * Tpad = 128*ceil(T/128)).  out[b, t, h, c] at out + b*os[0] + t*os[1] + h*os[2] + c*os[3] in
+ * out_dtype.  ev0 = NULL: sink off (B8); non-NULL: B9.1 sink_alone.  dh in {64, 128}.
+ * The fold of reference/lssab8_torch.py:164-271 / reference/lssab9_torch.py:176-326. */
+int lssab8_prefill_lattice(const int8_t* q8, const int32_t* eq, const int8_t* k8, const int32_t* ek,
+                           const int8_t* v8, const int32_t* ev, const int32_t* ev0, int B, int H, int KVH, int T,
+                           int dh, int Tpad, void* out, int out_dtype, const int64_t* os, void* stream);
+
+/* Bytes of workspace lssab8_prefill needs for this shape. */
+size_t lssab8_prefill_workspace_size(int B, int H, int KVH, int T, int dh);
+
+/* The whole drop-in: PREP + prefill.  q [B, H, T, dh], k/v [B, KVH, T, dh] in `dtype` with
+ * strides qs/ks/vs; out as in lssab8_prefill_lattice.  sink = 0: LSSA-B8
+ * (reference/lssab8_torch.py:134-271 per batch element); sink = 1: LSSA-B9.1 sink_alone
+ * (reference/lssab9_torch.py:109-326 with sink_alone=True). */
+int lssab8_prefill(const void* q, const void* k, const void* v, int dtype, int B, int H, int KVH, int T, int dh,
+                   const int64_t* qs, const int64_t* ks, const int64_t* vs, int sink, void* out, int out_dtype,
+                   const int64_t* os, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------- decode */
+
+/* Paged int8 lattice writer.  Sequence b has seq_lens[b] tokens; token t, kv head g, channel c
+ * of K is read at k + seq_off[b] + t*st + g*sg + c*sc (same for v).  Pages hold 16 keys:
+ * k8p [num_pages, KVH, 16, dh], v8p [num_pages, KVH, dh, 16] (values transposed per page);
+ * block_table [B, max_pages] maps logical page -> physical page.  ek/ev [B, KVH, max_blocks]
+ * int32 per logical 128-key block, ev0 [B, KVH] (sink only; may be NULL when sink = 0).
+ * Block exponents cover the block's present rows only (reference/lssab_torch.py:62-85). */
+int lssab8_decode_prep_kv(const void* k, const void* v, int dtype, int B, int KVH, int dh, const int32_t* seq_lens,
+                          const int64_t* seq_off, int64_t st, int64_t sg, int64_t sc, const int32_t* block_table,
+                          int max_pages, int max_blocks, int num_pages, int sink, int8_t* k8p, int8_t* v8p,
+                          int32_t* ek, int32_t* ev, int32_t* ev0, void* stream);
+
+/* Bytes of workspace lssab8_decode needs. */
+size_t lssab8_decode_workspace_size(int B, int H, int KVH, int dh, int max_blocks);
+
+/* Split-KV decode: one new query row per sequence, q [B, H, dh] (strides qs[0..2]), attending to
+ * all seq_lens[b] keys of the lattice (the new token's own key is the last one).  Each split of
+ * split_blocks 128-key blocks emits exact block partials; the last split to finish refolds
+ * them in ascending order (reference/lssab8_golden.py:350-394).  Equals row L-1 of the prefill
+ * bit for bit (reference/lssab8_selftest.py:320-336).  out[b, h, c] at out + b*os[0] + h*os[1]
+ * + c*os[2].  H/KVH <= 8, dh in {64, 128}. */
+int lssab8_decode(const void* q, int dtype, const int64_t* qs, int B, int H, int KVH, int dh, const int32_t* seq_lens,
+                  const int32_t* block_table, int max_pages, int num_pages, const int8_t* k8p, const int8_t* v8p,
+                  const int32_t* ek, const int32_t* ev, const int32_t* ev0, int max_blocks, int split_blocks, int sink,
+                  void* out, int out_dtype, const int64_t* os, void* workspace, size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LSSAB8_H */

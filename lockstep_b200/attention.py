@@ -1,0 +1,142 @@
+"""Host layer over the C ABI: device buffers, streams and error checks for the prefill path.
+
+PyTorch is used only for device memory and the current CUDA stream; every computation runs in
+liblssab8_b200.so.  Tensors must be CUDA tensors of one floating dtype (float32 / float16 /
+bfloat16); anything else raises -- there is no CPU path.
+"""
+import torch
+
+from . import _lib
+
+_DT = {torch.float32: _lib.DT_F32, torch.float16: _lib.DT_F16, torch.bfloat16: _lib.DT_BF16}
+KB = 128
+
+
+def dtype_code(dt):
+    try:
+        return _DT[dt]
+    except KeyError:
+        raise TypeError("LSSA-B8 kernels take float32, float16 or bfloat16 tensors, got %s" % dt) from None
+
+
+def _stream_handle(device):
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _require_cuda(*ts):
+    for t in ts:
+        if not isinstance(t, torch.Tensor) or t.device.type != "cuda":
+            raise ValueError("LSSA-B8 on B200 needs CUDA tensors (no CPU fallback exists)")
+    dev = ts[0].device
+    if any(t.device != dev for t in ts):
+        raise ValueError("all tensors must be on the same CUDA device")
+    return dev
+
+
+def tpad(T):
+    return ((T + KB - 1) // KB) * KB
+
+
+def check_device_errors(device=None):
+    """Raise if a kernel on this device set the device error word (then clear it).
+
+    e_v outside [-32, 40] raises AssertionError, mirroring the reference's assert
+    (reference/lssab9_torch.py:158); other bits raise RuntimeError."""
+    with torch.cuda.device(device):
+        bits = _lib.device_errors(_stream_handle(device), clear=True)
+    if bits & _lib.DEV_EV_RANGE:
+        raise AssertionError("e_v outside the contract clamp")
+    if bits:
+        raise RuntimeError("LSSA-B8 device error bits 0x%x (timeout=2, bad page=4)" % bits)
+
+
+_WS = {}
+
+
+def workspace(device, nbytes):
+    """A cached uint8 device buffer of at least nbytes (grown, never shrunk)."""
+    key = (device.type, device.index)
+    buf = _WS.get(key)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=device)
+        _WS[key] = buf
+    return buf
+
+
+def quant_rows(x, Tpad=None):
+    """P1 on the device: x [B, H, T, dh] -> (q8 int8 [B, H, Tpad, dh], eq int32 [B, H, Tpad])."""
+    dev = _require_cuda(x)
+    B, H, T, dh = x.shape
+    Tp = tpad(T) if Tpad is None else Tpad
+    q8 = torch.empty((B, H, Tp, dh), dtype=torch.int8, device=dev)
+    eq = torch.empty((B, H, Tp), dtype=torch.int32, device=dev)
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().lssab8_quant_rows(x.data_ptr(), dtype_code(x.dtype), B, H, T, dh, _lib.i64x(x.stride()),
+                                                 Tp, q8.data_ptr(), eq.data_ptr(), _stream_handle(dev)),
+                   "lssab8_quant_rows")
+    return q8, eq
+
+
+def quant_blocks(x, mode=0):
+    """P2/P3 on the device: x [B, KVH, T, dh] -> (x8 [B, KVH, Tpad, dh], e [B, KVH, nblk], e0 [B, KVH]).
+    mode 0 = B8 grid, 1 = B9 value grid, 2 = B9.1 sink_alone value grid."""
+    dev = _require_cuda(x)
+    B, KVH, T, dh = x.shape
+    Tp = tpad(T)
+    x8 = torch.empty((B, KVH, Tp, dh), dtype=torch.int8, device=dev)
+    e = torch.empty((B, KVH, Tp // KB), dtype=torch.int32, device=dev)
+    e0 = torch.zeros((B, KVH), dtype=torch.int32, device=dev)
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().lssab8_quant_blocks(x.data_ptr(), dtype_code(x.dtype), B, KVH, T, dh,
+                                                   _lib.i64x(x.stride()), Tp, int(mode), x8.data_ptr(), e.data_ptr(),
+                                                   e0.data_ptr(), _stream_handle(dev)),
+                   "lssab8_quant_blocks")
+    return x8, e, e0
+
+
+def prefill_lattice(q8, eq, k8, ek, v8, ev, ev0, T, out=None, out_dtype=torch.bfloat16):
+    """Prefill on a prepared lattice; returns out [B, T, H, dh] (or writes `out`)."""
+    dev = _require_cuda(q8, eq, k8, ek, v8, ev)
+    B, H, Tp, dh = q8.shape
+    KVH = k8.shape[1]
+    if out is None:
+        out = torch.empty((B, T, H, dh), dtype=out_dtype, device=dev)
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().lssab8_prefill_lattice(
+            q8.data_ptr(), eq.data_ptr(), k8.data_ptr(), ek.data_ptr(), v8.data_ptr(), ev.data_ptr(),
+            None if ev0 is None else ev0.data_ptr(), B, H, KVH, T, dh, Tp, out.data_ptr(), dtype_code(out.dtype),
+            _lib.i64x(out.stride()), _stream_handle(dev)), "lssab8_prefill_lattice")
+    return out
+
+
+def prefill(query, key, value, sink=False, out=None, out_dtype=None, check=True):
+    """Batched LSSA-B8 (sink=False) / B9.1 sink_alone (sink=True) causal GQA prefill.
+
+    query [B, H, T, dh], key/value [B, KVH, T, dh] (any strides, one dtype) -> out [B, T, H, dh]
+    in out_dtype (default query.dtype).  Each batch element is the reference drop-in's function
+    (reference/lssab8_torch.py:134-271, reference/lssab9_torch.py:109-326)."""
+    dev = _require_cuda(query, key, value)
+    if not (query.dtype == key.dtype == value.dtype):
+        raise TypeError("query, key and value must share one dtype")
+    B, H, T, dh = query.shape
+    if key.dim() != 4 or key.shape[0] != B or key.shape[2] != T or key.shape[3] != dh or value.shape != key.shape:
+        raise ValueError("key/value must be [B, KVH, T, dh] matching query [B, H, T, dh]")
+    KVH = key.shape[1]
+    if H % KVH:
+        raise ValueError("query heads must be a multiple of kv heads")
+    if out is None:
+        out = torch.empty((B, T, H, dh), dtype=out_dtype or query.dtype, device=dev)
+    L = _lib.load()
+    nbytes = L.lssab8_prefill_workspace_size(B, H, KVH, T, dh)
+    if nbytes == 0:
+        raise ValueError("unsupported prefill shape")
+    ws = workspace(dev, nbytes)
+    with torch.cuda.device(dev):
+        _lib.check(L.lssab8_prefill(query.data_ptr(), key.data_ptr(), value.data_ptr(), dtype_code(query.dtype), B, H,
+                                    KVH, T, dh, _lib.i64x(query.stride()), _lib.i64x(key.stride()),
+                                    _lib.i64x(value.stride()), int(bool(sink)), out.data_ptr(), dtype_code(out.dtype),
+                                    _lib.i64x(out.stride()), ws.data_ptr(), ws.numel(), _stream_handle(dev)),
+                   "lssab8_prefill")
+    if check:
+        check_device_errors(dev)
+    return out

@@ -1,0 +1,478 @@
+// C ABI of liblssab8_b200.so (declarations and contracts: include/lssab8.h).
+//
+// Host-side responsibilities: argument validation (every error is a status code, never an
+// exception), TMA tensor-map encoding, workspace carving, kernel instantiation by
+// (head dim, sink, output dtype), and the per-device error word.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/lssab8.h"
+#include "common.cuh"
+#include "prep.cuh"
+#include "prefill.cuh"
+#include "decode.cuh"
+
+using namespace lssab8;
+
+namespace {
+
+constexpr const char* kVersion = "0.1.0";
+
+// ------------------------------------------------------------------ device error word
+__device__ int g_dev_err;
+
+struct DevState {
+  int* err = nullptr;
+  bool prefill_attr_set = false;
+};
+std::mutex g_mu;
+DevState g_dev[64];
+
+int dev_state(DevState** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return kErrCuda;
+  std::lock_guard<std::mutex> lk(g_mu);
+  DevState& st = g_dev[dev];
+  if (!st.err) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_dev_err) != cudaSuccess) return kErrCuda;
+    st.err = static_cast<int*>(p);
+  }
+  *out = &st;
+  return kOk;
+}
+
+// ------------------------------------------------------------------ TMA encode (driver API)
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+int get_encode() {
+  static std::once_flag once;
+  static int rc = kOk;
+  std::call_once(once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !fn) {
+      rc = kErrCuda;
+      return;
+    }
+    g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  return rc;
+}
+
+// rows x dh int8 matrix, box 128 rows x dh, swizzle = dh bytes
+int make_tmap(CUtensorMap* tm, const void* base, long long rows, int dh) {
+  if (get_encode() != kOk) return kErrCuda;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) return kErrArg;
+  cuuint64_t dims[2] = {(cuuint64_t)dh, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)dh};
+  cuuint32_t box[2] = {(cuuint32_t)dh, 128};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        dh == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? kOk : kErrCuda;
+}
+
+inline int cuda_rc(cudaError_t e) { return e == cudaSuccess ? kOk : kErrCuda; }
+inline int launch_rc() { return cuda_rc(cudaGetLastError()); }
+
+uint32_t gbase_of(int dh) {
+  // round(2^26 / (sqrt(dh) ln 2)) with round-half-even, as Python's round() on the double
+  // (reference/lssab_golden.py:161).
+  double x = std::ldexp(1.0, kBHI) / (std::sqrt((double)dh) * std::log(2.0));
+  return (uint32_t)std::nearbyint(x);
+}
+
+inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+inline int tpad_of(int T) { return ((T + 127) / 128) * 128; }
+
+// ------------------------------------------------------------------ sha256 (FIPS 180-4)
+struct Sha256 {
+  uint32_t h[8] = {0x6a09e667, 0xbb67ae85, 0x3c6ef372, 0xa54ff53a, 0x510e527f, 0x9b05688c, 0x1f83d9ab, 0x5be0cd19};
+  uint8_t buf[64];
+  uint64_t len = 0;
+  size_t n = 0;
+  static uint32_t rotr(uint32_t x, int r) { return (x >> r) | (x << (32 - r)); }
+  void block(const uint8_t* p) {
+    static const uint32_t K[64] = {
+        0x428a2f98, 0x71374491, 0xb5c0fbcf, 0xe9b5dba5, 0x3956c25b, 0x59f111f1, 0x923f82a4, 0xab1c5ed5, 0xd807aa98,
+        0x12835b01, 0x243185be, 0x550c7dc3, 0x72be5d74, 0x80deb1fe, 0x9bdc06a7, 0xc19bf174, 0xe49b69c1, 0xefbe4786,
+        0x0fc19dc6, 0x240ca1cc, 0x2de92c6f, 0x4a7484aa, 0x5cb0a9dc, 0x76f988da, 0x983e5152, 0xa831c66d, 0xb00327c8,
+        0xbf597fc7, 0xc6e00bf3, 0xd5a79147, 0x06ca6351, 0x14292967, 0x27b70a85, 0x2e1b2138, 0x4d2c6dfc, 0x53380d13,
+        0x650a7354, 0x766a0abb, 0x81c2c92e, 0x92722c85, 0xa2bfe8a1, 0xa81a664b, 0xc24b8b70, 0xc76c51a3, 0xd192e819,
+        0xd6990624, 0xf40e3585, 0x106aa070, 0x19a4c116, 0x1e376c08, 0x2748774c, 0x34b0bcb5, 0x391c0cb3, 0x4ed8aa4a,
+        0x5b9cca4f, 0x682e6ff3, 0x748f82ee, 0x78a5636f, 0x84c87814, 0x8cc70208, 0x90befffa, 0xa4506ceb, 0xbef9a3f7,
+        0xc67178f2};
+    uint32_t w[64];
+    for (int i = 0; i < 16; ++i) w[i] = (uint32_t)p[4 * i] << 24 | (uint32_t)p[4 * i + 1] << 16 | (uint32_t)p[4 * i + 2] << 8 | p[4 * i + 3];
+    for (int i = 16; i < 64; ++i) {
+      uint32_t s0 = rotr(w[i - 15], 7) ^ rotr(w[i - 15], 18) ^ (w[i - 15] >> 3);
+      uint32_t s1 = rotr(w[i - 2], 17) ^ rotr(w[i - 2], 19) ^ (w[i - 2] >> 10);
+      w[i] = w[i - 16] + s0 + w[i - 7] + s1;
+    }
+    uint32_t a = h[0], b = h[1], c = h[2], d = h[3], e = h[4], f = h[5], g = h[6], hh = h[7];
+    for (int i = 0; i < 64; ++i) {
+      uint32_t S1 = rotr(e, 6) ^ rotr(e, 11) ^ rotr(e, 25);
+      uint32_t ch = (e & f) ^ (~e & g);
+      uint32_t t1 = hh + S1 + ch + K[i] + w[i];
+      uint32_t S0 = rotr(a, 2) ^ rotr(a, 13) ^ rotr(a, 22);
+      uint32_t mj = (a & b) ^ (a & c) ^ (b & c);
+      uint32_t t2 = S0 + mj;
+      hh = g; g = f; f = e; e = d + t1; d = c; c = b; b = a; a = t1 + t2;
+    }
+    h[0] += a; h[1] += b; h[2] += c; h[3] += d; h[4] += e; h[5] += f; h[6] += g; h[7] += hh;
+  }
+  void update(const void* data, size_t m) {
+    const uint8_t* p = static_cast<const uint8_t*>(data);
+    len += m;
+    while (m--) {
+      buf[n++] = *p++;
+      if (n == 64) { block(buf); n = 0; }
+    }
+  }
+  void final(char* hex) {
+    uint64_t bits = len * 8;
+    uint8_t pad = 0x80;
+    update(&pad, 1);
+    uint8_t z = 0;
+    while (n != 56) update(&z, 1);
+    uint8_t lb[8];
+    for (int i = 0; i < 8; ++i) lb[i] = (uint8_t)(bits >> (56 - 8 * i));
+    for (int i = 0; i < 8; ++i) { buf[n++] = lb[i]; }
+    block(buf);
+    for (int i = 0; i < 8; ++i) std::snprintf(hex + 8 * i, 9, "%08x", h[i]);
+  }
+};
+
+const uint8_t kT2Host[kTabLive] = {
+#include "t2_table.inc"
+};
+
+// ------------------------------------------------------------------ kernel dispatch helpers
+template <typename F>
+int with_in_dtype(int dtype, F&& f) {
+  switch (dtype) {
+    case kF32: return f((const float*)nullptr);
+    case kF16: return f((const __half*)nullptr);
+    case kBF16: return f((const __nv_bfloat16*)nullptr);
+    default: return kErrArg;
+  }
+}
+
+template <int DH, bool SINK, typename OutT>
+int launch_prefill_t(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const PrefillArgs& a,
+                     cudaStream_t st) {
+  using L = PrefillSmem<DH>;
+  const int multi = a.nblk > kSEG;
+  // at least ~116 KB so only one CTA (and one 512-column TMEM allocation) lands on an SM
+  int smem = (multi ? L::kBytesMulti : L::kBytesSingle) + 1024;
+  if (smem < 116 * 1024) smem = 116 * 1024;
+  auto kfn = prefill_kernel<DH, SINK, OutT>;
+  static int set_bytes[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && set_bytes[dev] < smem) {
+    if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytesMulti + 1024) != cudaSuccess)
+      return kErrCuda;
+    set_bytes[dev] = L::kBytesMulti + 1024;
+  }
+  dim3 grid(a.Tpad / 128, a.H, a.B);
+  kfn<<<grid, 448, smem, st>>>(tq, tk, tv, a, multi);
+  return launch_rc();
+}
+
+template <int DH, bool SINK>
+int launch_prefill_out(int out_dtype, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                       const PrefillArgs& a, cudaStream_t st) {
+  switch (out_dtype) {
+    case kF32: return launch_prefill_t<DH, SINK, float>(tq, tk, tv, a, st);
+    case kF16: return launch_prefill_t<DH, SINK, __half>(tq, tk, tv, a, st);
+    case kBF16: return launch_prefill_t<DH, SINK, __nv_bfloat16>(tq, tk, tv, a, st);
+    default: return kErrArg;
+  }
+}
+
+template <int DH, bool SINK, typename OutT>
+int launch_decode_t(const DecodeArgs& a, int max_splits, cudaStream_t st) {
+  using L = DecodeSmem<DH>;
+  const int smem = L::kBytes + 128;
+  auto kfn = decode_kernel<DH, SINK, OutT>;
+  if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return kErrCuda;
+  dim3 grid(max_splits, a.KVH, a.B);
+  kfn<<<grid, 128, smem, st>>>(a);
+  return launch_rc();
+}
+
+template <int DH, bool SINK>
+int launch_decode_out(int out_dtype, const DecodeArgs& a, int max_splits, cudaStream_t st) {
+  switch (out_dtype) {
+    case kF32: return launch_decode_t<DH, SINK, float>(a, max_splits, st);
+    case kF16: return launch_decode_t<DH, SINK, __half>(a, max_splits, st);
+    case kBF16: return launch_decode_t<DH, SINK, __nv_bfloat16>(a, max_splits, st);
+    default: return kErrArg;
+  }
+}
+
+bool strides_ok(const int64_t* s, int n) {
+  if (!s) return false;
+  for (int i = 0; i < n; ++i) if (s[i] < 0) return false;
+  return true;
+}
+
+struct PrefillWs {
+  size_t q8, eq, k8, ek, v8, ev, ev0, total;
+};
+
+PrefillWs prefill_ws(int B, int H, int KVH, int T, int dh) {
+  PrefillWs w{};
+  const size_t Tpad = (size_t)tpad_of(T), nblk = Tpad / 128;
+  size_t o = 0;
+  w.q8 = o; o += align256((size_t)B * H * Tpad * dh);
+  w.eq = o; o += align256((size_t)B * H * Tpad * 4);
+  w.k8 = o; o += align256((size_t)B * KVH * Tpad * dh);
+  w.ek = o; o += align256((size_t)B * KVH * nblk * 4);
+  w.v8 = o; o += align256((size_t)B * KVH * Tpad * dh);
+  w.ev = o; o += align256((size_t)B * KVH * nblk * 4);
+  w.ev0 = o; o += align256((size_t)B * KVH * 4);
+  w.total = o + 256;     // slack for aligning the caller's base
+  return w;
+}
+
+struct DecodeWs {
+  size_t q8, eq, partA, partM, tickets, total;
+};
+
+DecodeWs decode_ws(int B, int H, int KVH, int dh, int max_blocks) {
+  DecodeWs w{};
+  const int gq = H / KVH;
+  size_t o = 0;
+  w.q8 = o; o += align256((size_t)B * H * dh);
+  w.eq = o; o += align256((size_t)B * H * 4);
+  w.partA = o; o += align256((size_t)B * KVH * max_blocks * gq * dh * 4);
+  w.partM = o; o += align256((size_t)B * KVH * max_blocks * gq * 16);
+  w.tickets = o; o += align256((size_t)B * KVH * 4);
+  w.total = o + 256;
+  return w;
+}
+
+bool shape_ok(int B, int H, int KVH, int T, int dh) {
+  return B > 0 && H > 0 && KVH > 0 && T > 0 && dh > 0 && H % KVH == 0 && dh <= 256 && dh % 32 == 0 &&
+         (long long)T <= (1ll << 24);
+}
+
+}  // namespace
+
+// ========================================================================== extern "C"
+extern "C" {
+
+int lssab8_version(char* buf, int buflen) {
+  if (!buf || buflen < 128) return kErrArg;
+  Sha256 s;
+  char num[8];
+  for (int k = 0; k < 17 * 128; ++k) {
+    int v = k < kTabLive ? kT2Host[k] : 0;
+    int n = std::snprintf(num, sizeof num, k ? ",%d" : "%d", v);
+    s.update(num, (size_t)n);
+  }
+  char hex[65];
+  s.final(hex);
+  std::snprintf(buf, (size_t)buflen, "lssab8-b200 %s T2=%s", kVersion, hex);
+  return kOk;
+}
+
+const char* lssab8_strerror(int code) {
+  switch (code) {
+    case kOk: return "ok";
+    case kErrArg: return "invalid argument (shape, stride, dtype or pointer)";
+    case kErrUnsupported: return "unsupported by the B200 kernels (head dim / group size)";
+    case kErrCuda: return "CUDA error";
+    case kErrWorkspace: return "workspace too small";
+    case kErrDevice: return "device error word set";
+    default: return "unknown status";
+  }
+}
+
+int lssab8_device_errors(int clear, void* stream, int* bits) {
+  if (!bits) return kErrArg;
+  DevState* st = nullptr;
+  int rc = dev_state(&st);
+  if (rc) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int host = 0;
+  if (cudaMemcpyAsync(&host, st->err, sizeof(int), cudaMemcpyDeviceToHost, s) != cudaSuccess) return kErrCuda;
+  if (cudaStreamSynchronize(s) != cudaSuccess) return kErrCuda;
+  *bits = host;
+  if (clear && host) {
+    if (cudaMemsetAsync(st->err, 0, sizeof(int), s) != cudaSuccess) return kErrCuda;
+    if (cudaStreamSynchronize(s) != cudaSuccess) return kErrCuda;
+  }
+  return kOk;
+}
+
+int lssab8_quant_rows(const void* x, int dtype, int B, int H, int T, int dh, const int64_t* xs, int Tpad,
+                      int8_t* q8, int32_t* eq, void* stream) {
+  if (!x || !q8 || !eq || !shape_ok(B, H, H, T, dh) || Tpad < T || !strides_ok(xs, 4)) return kErrArg;
+  Strides4 s{xs[0], xs[1], xs[2], xs[3]};
+  const long long rows = (long long)B * H * Tpad;
+  const int grid = (int)((rows + 7) / 8);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return with_in_dtype(dtype, [&](auto tag) {
+    using InT = std::remove_const_t<std::remove_pointer_t<decltype(tag)>>;
+    quant_rows_kernel<InT><<<grid, 256, 0, st>>>(static_cast<const InT*>(x), s, B, H, T, dh, Tpad, q8, eq);
+    return launch_rc();
+  });
+}
+
+int lssab8_quant_blocks(const void* x, int dtype, int B, int KVH, int T, int dh, const int64_t* xs, int Tpad,
+                        int mode, int8_t* x8, int32_t* e, int32_t* e0, void* stream) {
+  if (!x || !x8 || !e || !shape_ok(B, KVH, KVH, T, dh) || Tpad < tpad_of(T) || !strides_ok(xs, 4) || mode < 0 ||
+      mode > 2 || (mode == 2 && !e0))
+    return kErrArg;
+  DevState* ds = nullptr;
+  int rc = dev_state(&ds);
+  if (rc) return rc;
+  Strides4 s{xs[0], xs[1], xs[2], xs[3]};
+  dim3 grid((T + 127) / 128, KVH, B);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return with_in_dtype(dtype, [&](auto tag) {
+    using InT = std::remove_const_t<std::remove_pointer_t<decltype(tag)>>;
+    quant_blocks_kernel<InT><<<grid, 256, 0, st>>>(static_cast<const InT*>(x), s, B, KVH, T, dh, Tpad, mode, x8, e, e0,
+                                                   ds->err);
+    return launch_rc();
+  });
+}
+
+int lssab8_prefill_lattice(const int8_t* q8, const int32_t* eq, const int8_t* k8, const int32_t* ek,
+                           const int8_t* v8, const int32_t* ev, const int32_t* ev0, int B, int H, int KVH, int T,
+                           int dh, int Tpad, void* out, int out_dtype, const int64_t* os, void* stream) {
+  if (!q8 || !eq || !k8 || !ek || !v8 || !ev || !out || !shape_ok(B, H, KVH, T, dh) || Tpad != tpad_of(T) ||
+      !strides_ok(os, 4))
+    return kErrArg;
+  if (dh != 64 && dh != 128) return kErrUnsupported;
+  DevState* ds = nullptr;
+  int rc = dev_state(&ds);
+  if (rc) return rc;
+  CUtensorMap tq, tk, tv;
+  if ((rc = make_tmap(&tq, q8, (long long)B * H * Tpad, dh))) return rc;
+  if ((rc = make_tmap(&tk, k8, (long long)B * KVH * Tpad, dh))) return rc;
+  if ((rc = make_tmap(&tv, v8, (long long)B * KVH * Tpad, dh))) return rc;
+  PrefillArgs a{};
+  a.B = B; a.H = H; a.KVH = KVH; a.T = T; a.dh = dh; a.Tpad = Tpad; a.nblk = Tpad / 128; a.group = H / KVH;
+  a.eq = eq; a.ek = ek; a.ev = ev; a.ev0 = ev0; a.v8 = v8;
+  a.out = out; a.os0 = os[0]; a.os1 = os[1]; a.os2 = os[2]; a.os3 = os[3]; a.out_dtype = out_dtype;
+  a.gbase = gbase_of(dh);
+  a.err = ds->err;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool sink = ev0 != nullptr;
+  if (dh == 128) return sink ? launch_prefill_out<128, true>(out_dtype, tq, tk, tv, a, st)
+                             : launch_prefill_out<128, false>(out_dtype, tq, tk, tv, a, st);
+  return sink ? launch_prefill_out<64, true>(out_dtype, tq, tk, tv, a, st)
+              : launch_prefill_out<64, false>(out_dtype, tq, tk, tv, a, st);
+}
+
+size_t lssab8_prefill_workspace_size(int B, int H, int KVH, int T, int dh) {
+  if (!shape_ok(B, H, KVH, T, dh)) return 0;
+  return prefill_ws(B, H, KVH, T, dh).total;
+}
+
+int lssab8_prefill(const void* q, const void* k, const void* v, int dtype, int B, int H, int KVH, int T, int dh,
+                   const int64_t* qs, const int64_t* ks, const int64_t* vs, int sink, void* out, int out_dtype,
+                   const int64_t* os, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!q || !k || !v || !out || !workspace || !shape_ok(B, H, KVH, T, dh)) return kErrArg;
+  if (dh != 64 && dh != 128) return kErrUnsupported;
+  const PrefillWs w = prefill_ws(B, H, KVH, T, dh);
+  if (workspace_bytes < w.total) return kErrWorkspace;
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(workspace) + 255) & ~uintptr_t(255));
+  const int Tpad = tpad_of(T);
+  int8_t* q8 = reinterpret_cast<int8_t*>(base + w.q8);
+  int32_t* eq = reinterpret_cast<int32_t*>(base + w.eq);
+  int8_t* k8 = reinterpret_cast<int8_t*>(base + w.k8);
+  int32_t* ek = reinterpret_cast<int32_t*>(base + w.ek);
+  int8_t* v8 = reinterpret_cast<int8_t*>(base + w.v8);
+  int32_t* ev = reinterpret_cast<int32_t*>(base + w.ev);
+  int32_t* ev0 = reinterpret_cast<int32_t*>(base + w.ev0);
+  int rc;
+  if ((rc = lssab8_quant_rows(q, dtype, B, H, T, dh, qs, Tpad, q8, eq, stream))) return rc;
+  if ((rc = lssab8_quant_blocks(k, dtype, B, KVH, T, dh, ks, Tpad, 0, k8, ek, nullptr, stream))) return rc;
+  const int vmode = sink ? (T > 1 ? 2 : 1) : 0;
+  if ((rc = lssab8_quant_blocks(v, dtype, B, KVH, T, dh, vs, Tpad, vmode, v8, ev, ev0, stream))) return rc;
+  return lssab8_prefill_lattice(q8, eq, k8, ek, v8, ev, (sink && T > 1) ? ev0 : nullptr, B, H, KVH, T, dh, Tpad, out,
+                                out_dtype, os, stream);
+}
+
+int lssab8_decode_prep_kv(const void* k, const void* v, int dtype, int B, int KVH, int dh, const int32_t* seq_lens,
+                          const int64_t* seq_off, int64_t st, int64_t sg, int64_t sc, const int32_t* block_table,
+                          int max_pages, int max_blocks, int num_pages, int sink, int8_t* k8p, int8_t* v8p,
+                          int32_t* ek, int32_t* ev, int32_t* ev0, void* stream) {
+  if (!k || !v || !seq_lens || !seq_off || !block_table || !k8p || !v8p || !ek || !ev || (sink && !ev0) || B <= 0 ||
+      KVH <= 0 || dh <= 0 || dh > 256 || max_pages <= 0 || max_blocks <= 0 || num_pages <= 0 || st < 0 || sg < 0 ||
+      sc < 0 || max_pages < max_blocks * 8 - 7)
+    return kErrArg;
+  DevState* ds = nullptr;
+  int rc = dev_state(&ds);
+  if (rc) return rc;
+  dim3 grid(max_blocks, KVH, B);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int vmode = sink ? 2 : 0;
+  return with_in_dtype(dtype, [&](auto tag) {
+    using InT = std::remove_const_t<std::remove_pointer_t<decltype(tag)>>;
+    decode_prep_kernel<InT><<<grid, 256, 0, s>>>(static_cast<const InT*>(k), static_cast<const InT*>(v),
+                                                 reinterpret_cast<const long long*>(seq_off), st, sg, sc, B, KVH, dh,
+                                                 seq_lens, block_table, max_pages, max_blocks, num_pages, vmode, k8p,
+                                                 v8p, ek, ev, ev0, ds->err);
+    return launch_rc();
+  });
+}
+
+size_t lssab8_decode_workspace_size(int B, int H, int KVH, int dh, int max_blocks) {
+  if (B <= 0 || H <= 0 || KVH <= 0 || H % KVH || dh <= 0 || max_blocks <= 0) return 0;
+  return decode_ws(B, H, KVH, dh, max_blocks).total;
+}
+
+int lssab8_decode(const void* q, int dtype, const int64_t* qs, int B, int H, int KVH, int dh, const int32_t* seq_lens,
+                  const int32_t* block_table, int max_pages, int num_pages, const int8_t* k8p, const int8_t* v8p,
+                  const int32_t* ek, const int32_t* ev, const int32_t* ev0, int max_blocks, int split_blocks, int sink,
+                  void* out, int out_dtype, const int64_t* os, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!q || !seq_lens || !block_table || !k8p || !v8p || !ek || !ev || (sink && !ev0) || !out || !workspace ||
+      !strides_ok(qs, 3) || !strides_ok(os, 3) || B <= 0 || H <= 0 || KVH <= 0 || H % KVH || max_blocks <= 0 ||
+      split_blocks <= 0 || max_pages <= 0 || num_pages <= 0)
+    return kErrArg;
+  if ((dh != 64 && dh != 128) || H / KVH > 8) return kErrUnsupported;
+  const DecodeWs w = decode_ws(B, H, KVH, dh, max_blocks);
+  if (workspace_bytes < w.total) return kErrWorkspace;
+  DevState* ds = nullptr;
+  int rc = dev_state(&ds);
+  if (rc) return rc;
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(workspace) + 255) & ~uintptr_t(255));
+  int8_t* q8 = reinterpret_cast<int8_t*>(base + w.q8);
+  int32_t* eq = reinterpret_cast<int32_t*>(base + w.eq);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t q4[4] = {qs[0], qs[1], 0, qs[2]};
+  if ((rc = lssab8_quant_rows(q, dtype, B, H, 1, dh, q4, 1, q8, eq, stream))) return rc;
+  if (cudaMemsetAsync(base + w.tickets, 0, (size_t)B * KVH * 4, s) != cudaSuccess) return kErrCuda;
+  DecodeArgs a{};
+  a.B = B; a.H = H; a.KVH = KVH; a.dh = dh; a.group = H / KVH; a.max_blocks = max_blocks; a.max_pages = max_pages;
+  a.split_blocks = split_blocks; a.num_pages = num_pages; a.seq_lens = seq_lens; a.block_table = block_table;
+  a.k8p = k8p; a.v8p = v8p; a.ek = ek; a.ev = ev; a.ev0 = sink ? ev0 : nullptr; a.q8 = q8; a.eq = eq;
+  a.partA = reinterpret_cast<int32_t*>(base + w.partA);
+  a.partM = reinterpret_cast<int4*>(base + w.partM);
+  a.tickets = reinterpret_cast<unsigned int*>(base + w.tickets);
+  a.out = out; a.os0 = os[0]; a.os1 = os[1]; a.os2 = os[2];
+  a.gbase = gbase_of(dh);
+  a.err = ds->err;
+  const int max_splits = (max_blocks + split_blocks - 1) / split_blocks;
+  if (dh == 128) return sink ? launch_decode_out<128, true>(out_dtype, a, max_splits, s)
+                             : launch_decode_out<128, false>(out_dtype, a, max_splits, s);
+  return sink ? launch_decode_out<64, true>(out_dtype, a, max_splits, s)
+              : launch_decode_out<64, false>(out_dtype, a, max_splits, s);
+}
+
+}  // extern "C"

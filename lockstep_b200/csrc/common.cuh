@@ -1,0 +1,188 @@
+// LSSA-B8 / B9.1 contract attention for sm_100a -- shared device definitions.
+//
+// Contract constants (docs/contract/BLOCK_EXPONENT_VARIANT.md B8.0; reference/lssab8_golden.py:54-74).
+// Every helper here is exact: integer arithmetic, or a single IEEE binary32 RNE operation on
+// exactly representable operands.  The library is built with -ftz=false -prec-div=true
+// -prec-sqrt=true -fmad=false so no compiler contraction or flush can change a rounding.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+namespace lssab8 {
+
+constexpr int kBHI = 26;          // one doubling = 2^26 in the chain
+constexpr int kKB = 128;          // key block (absolute positions)
+constexpr int kSEG = 32;          // fold segment, in blocks
+constexpr int kSWIN = 32;         // exact-skip window, in doublings
+constexpr int kWLOC = 9;          // block-local weight window, in doublings
+constexpr int kNIDX = 7;          // index bits per doubling
+constexpr int kTabLive = kWLOC << kNIDX;      // 1152 live T2 entries
+constexpr int kTabPad = 8192;                  // zero-padded: a 32-bit d indexes it as d >> 19
+constexpr int kIdxShift = kBHI - kNIDX;        // 19
+
+// status / device error bits (the device error word is OR-accumulated)
+enum : int {
+  kOk = 0,
+  kErrArg = 1,            // bad shape / stride / dtype / null pointer
+  kErrUnsupported = 2,    // valid contract input the kernels do not cover (e.g. dh not 64/128)
+  kErrCuda = 3,           // CUDA runtime error
+  kErrWorkspace = 4,      // caller workspace too small
+  kErrDevice = 5,         // the device error word is nonzero (see kDev*)
+};
+enum : int {
+  kDevEvRange = 1,        // e_v outside [-32, 40] (reference/lssab9_torch.py:158)
+  kDevTimeout = 2,        // a bounded wait gave up (pipeline stalled)
+  kDevBadPage = 4,        // block table entry out of range
+};
+
+// dtype codes used across the C ABI
+enum : int { kF32 = 0, kF16 = 1, kBF16 = 2 };
+
+template <int Dt> struct Elem;
+template <> struct Elem<kF32> { using T = float; };
+template <> struct Elem<kF16> { using T = __half; };
+template <> struct Elem<kBF16> { using T = __nv_bfloat16; };
+
+__device__ __forceinline__ float to_f32(float x) { return x; }
+__device__ __forceinline__ float to_f32(__half x) { return __half2float(x); }
+__device__ __forceinline__ float to_f32(__nv_bfloat16 x) { return __bfloat162float(x); }
+
+template <typename T> __device__ __forceinline__ T from_f32(float x);
+template <> __device__ __forceinline__ float from_f32<float>(float x) { return x; }
+template <> __device__ __forceinline__ __half from_f32<__half>(float x) { return __float2half_rn(x); }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
+
+// --------------------------------------------------------------------------------- PREP
+// The clip-safe pow2 exponent of an amax m >= 0 (reference/contract_common.py:80-90,
+// reference/lssab_torch.py:62-85): e = 7 - E(frexp), 0 for m == 0, minus one when
+// m * 2^e > 127, clamped to [-32, hi].  With m = (1+f) 2^(be-127): e = 133 - be and
+// m * 2^e = 64 (1+f) > 127  <=>  mantissa field > 0x7E0000.  Subnormal m gives e >= 132, which
+// the clamp maps to hi, exactly as the reference's clamp does.
+__device__ __forceinline__ int pow2_exponent(float m, int hi) {
+  if (m == 0.0f) return 0;
+  uint32_t u = __float_as_uint(m);
+  int be = (int)(u >> 23) & 0xFF;
+  int e = 133 - be - (int)((u & 0x7FFFFFu) > 0x7E0000u);
+  e = e < -32 ? -32 : e;
+  return e > hi ? hi : e;
+}
+
+// 2^e as an exact binary32, e in [-126, 127].
+__device__ __forceinline__ float pow2f(int e) { return __uint_as_float((uint32_t)(e + 127) << 23); }
+
+// q = clamp(rint(x * 2^e), -127, 127): rint is round-half-even; x * 2^e is exact unless it
+// is subnormal, in which case it rounds to zero either way.
+__device__ __forceinline__ int quant8(float x, float sc) {
+  float y = rintf(__fmul_rn(x, sc));
+  y = fminf(fmaxf(y, -127.0f), 127.0f);
+  return (int)y;
+}
+
+// ---------------------------------------------------------------------------------- FOLD
+// G = g_fold(dh, clamp(sh, -7, 23)) in [1, 2^30] (reference/lssab_golden.py:158-168).
+__device__ __forceinline__ uint32_t g_fold(uint32_t base, int sh) {
+  sh = sh < -7 ? -7 : (sh > 23 ? 23 : sh);
+  uint64_t G;
+  if (sh >= 0) G = ((uint64_t)base + (sh > 0 ? (1ull << (sh - 1)) : 0ull)) >> sh;
+  else G = (uint64_t)base << (-sh);
+  G = G < 1 ? 1 : G;
+  return (uint32_t)(G > (1ull << 30) ? (1ull << 30) : G);
+}
+
+// The contract rescale: exponent-field subtraction, +0.0 when the input is zero/subnormal or
+// the result's biased exponent would be < 1 (reference/lssab8_golden.py:150-168).  D >= 0.
+__device__ __forceinline__ float rescale(float x, int D) {
+  uint32_t u = __float_as_uint(x);
+  int e = (int)(u >> 23) & 0xFF;
+  int ne = e - D;
+  return (e >= 1 && ne >= 1) ? __uint_as_float((u & 0x807FFFFFu) | ((uint32_t)ne << 23)) : 0.0f;
+}
+
+// One fold term: fl(O + f32(A) * 2^esc).  f32(A) is exact (|A| < 2^24) and so is the product
+// (its exponent stays normal), so this is one RNE addition.
+__device__ __forceinline__ float fold_term(float O, int A, float sc) {
+  return __fadd_rn(O, __fmul_rn(__int2float_rn(A), sc));
+}
+
+// least multiple of 2^26 >= m*G, returned as NB / 2^26 (|NB| < 2^52, so it fits in int32).
+__device__ __forceinline__ int nb_of(int m, uint32_t G) {
+  long long sg = (long long)m * (long long)G;
+  return (int)((sg + ((1ll << kBHI) - 1)) >> kBHI);
+}
+
+// ------------------------------------------------------------------ bounded waits + PTX
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("{\n .reg .b64 st;\n mbarrier.arrive.shared::cta.b64 st, [%0];\n}" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("{\n .reg .b64 st;\n mbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n}"
+               ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+               : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+  return ok != 0;
+}
+
+// Bounded wait on an mbarrier phase.  Gives up after ~2 s of wall time or as soon as another
+// role of the CTA has raised *abort; on giving up it records kDevTimeout in *err and returns
+// false so the caller can unwind without hanging the GPU.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int* err) {
+  if (mbar_try(bar, parity)) return true;
+  uint64_t t0 = globaltimer();
+  for (uint32_t it = 0;; ++it) {
+    if (mbar_try(bar, parity)) return true;
+    if ((it & 255u) == 255u) {
+      if (*abort) return false;
+      if (globaltimer() - t0 > 2000000000ull) {
+        *abort = 1;
+        if (err) atomicOr(err, kDevTimeout);
+        return false;
+      }
+    }
+  }
+}
+
+// Warp-uniform form of mbar_wait for warps that next issue .sync.aligned instructions
+// (tcgen05.ld): lane 0 does the bounded wait, the verdict is broadcast, and on success every
+// lane observes the completed phase itself (it cannot advance again before this warp arrives
+// on the matching release barrier), which gives each lane the acquire ordering.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort, int* err) {
+  int ok = 0;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, abort, err) ? 1 : 0;
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  if (ok) {
+    // completes on the first try by the argument above; bounded all the same
+    uint32_t it = 0;
+    while (!mbar_try(bar, parity) && ++it < (1u << 22)) {
+    }
+    if (it >= (1u << 22)) {
+      *abort = 1;
+      if (err) atomicOr(err, kDevTimeout);
+      ok = 0;
+    }
+  }
+  ok = __all_sync(0xffffffffu, ok);
+  return ok != 0;
+}
+
+}  // namespace lssab8

@@ -1,0 +1,380 @@
+// LSSA-B8 split-KV decode on sm_100a (HBM-bound byte/integer work).
+//
+// The KV cache is a PAGED int8 lattice (16-key pages; a contiguous cache is the identity page
+// table):
+//   k8p [P, KVH, 16, dh]  key rows of a page, one kv head contiguous (2 KB at dh 128)
+//   v8p [P, KVH, dh, 16]  the page's values TRANSPOSED (channel-major), so 4 consecutive keys
+//                         of one channel are one 32-bit word for dp4a
+//   ek, ev [B, KVH, max_blocks] int32 per logical 128-key block; ev0 [B, KVH] (B9.1 sink)
+//
+// One CTA = (split, kv head, sequence): the split's 128-key blocks stream through a 2-stage
+// shared-memory ring with cp.async.bulk (16 page copies of 2 KB per block), the GQA group's
+// query rows sit in shared memory, and for each block the CTA computes the EXACT integer block
+// partials of every head of the group (docs/contract/BLOCK_EXPONENT_VARIANT.md B8.4):
+//   S (int32, dp4a), block max, NB_b, the 32-bit chain and T2 gather, l_b, A_b = eh . v8
+// and writes (A_b, NB_b, l_b, eh0) to the workspace.  A split below segment granularity may only
+// exchange exact block partials (reference/lssab8_golden.py:350-394); the LAST CTA of a
+// (sequence, kv head) to finish (an atomic ticket, no waiting) refolds all blocks in ascending
+// order with the two-level committed-order fold and writes the output rows.
+#pragma once
+#include "common.cuh"
+#include "prefill.cuh"   // PTX wrappers, T2 table
+
+namespace lssab8 {
+
+struct DecodeArgs {
+  int B, H, KVH, dh, group;          // group = H / KVH (<= 8)
+  int max_blocks;                     // exponent / partial array extent per (b, g)
+  int max_pages;                      // block_table row length
+  int split_blocks;                   // blocks per split
+  int num_pages;                      // physical pool size (for bounds checks)
+  const int32_t* seq_lens;            // [B]
+  const int32_t* block_table;         // [B, max_pages]
+  const int8_t* k8p;                  // [P, KVH, 16, dh]
+  const int8_t* v8p;                  // [P, KVH, dh, 16]
+  const int32_t* ek;                  // [B, KVH, max_blocks]
+  const int32_t* ev;
+  const int32_t* ev0;                 // [B, KVH] or nullptr (sink off)
+  const int8_t* q8;                   // [B, H, dh]
+  const int32_t* eq;                  // [B, H]
+  int32_t* partA;                     // [B, KVH, max_blocks, group, dh]
+  int4* partM;                        // [B, KVH, max_blocks, group] {nb, l_b, eh0, 0}
+  unsigned int* tickets;              // [B, KVH], zero before the launch
+  void* out; long long os0, os1, os2; // out[b, h, c]
+  uint32_t gbase;
+  int* err;
+};
+
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ uint32_t dp4a_us(uint32_t a_u8x4, uint32_t b_s8x4, uint32_t c) {
+  uint32_t d;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a_u8x4), "r"(b_s8x4), "r"(c));
+  return d;
+}
+
+template <int DH>
+struct DecodeSmem {
+  static constexpr int kPage = 16 * DH;                 // bytes of one page, one kv head
+  static constexpr int kStage = 2 * 8 * kPage;          // K block + V block
+  static constexpr int kK = 0;                          // stage s: K at s*kStage, V at s*kStage + 8*kPage
+  static constexpr int kTab = 2 * kStage;
+  static constexpr int kQ = kTab + kTabPad;             // [8][DH] int8
+  static constexpr int kEh = kQ + 8 * DH;               // [8][128] u8
+  static constexpr int kRed = kEh + 8 * 128;            // 80 ints: max[4][8], l_b[4][8], eh0[8], nb[8]
+  static constexpr int kBar = kRed + 384;
+  static constexpr int kBytes = kBar + 64;
+};
+
+template <int DH, bool SINK, typename OutT>
+__global__ void __launch_bounds__(128)
+decode_kernel(const DecodeArgs p) {
+  using L = DecodeSmem<DH>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((128u - (smem_u32(smem_raw) & 127u)) & 127u);        // 128-B aligned, still __shared__
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
+  uint8_t* tab = smem + L::kTab;
+  int8_t* sq = reinterpret_cast<int8_t*>(smem + L::kQ);
+  uint8_t* seh = smem + L::kEh;
+  int* red = reinterpret_cast<int*>(smem + L::kRed);
+  __shared__ int s_last;
+  __shared__ int s_abort;
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int split = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+  const int gq = p.group;
+  const int L_len = p.seq_lens[b];
+  const int nblk = (L_len + kKB - 1) / kKB;
+  const int nsplit = (nblk + p.split_blocks - 1) / p.split_blocks;
+  if (L_len <= 0 || split >= nsplit) return;
+  if (nblk > p.max_blocks || (L_len + 15) / 16 > p.max_pages) {   // lattice arrays too short
+    if (tid == 0) atomicOr(p.err, kDevBadPage);
+    return;
+  }
+  const int blo = split * p.split_blocks;
+  const int bhi = min(nblk, blo + p.split_blocks);
+  const long long bg = (long long)b * p.KVH + g;
+  const int32_t* bt = p.block_table + (long long)b * p.max_pages;
+
+  for (int i = tid; i < kTabPad; i += blockDim.x) tab[i] = (i < kTabLive) ? kT2Live[i] : 0;
+  for (int i = tid; i < gq * DH; i += blockDim.x) sq[i] = p.q8[((long long)b * p.H + g * gq) * DH + i];
+  if (tid == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    s_abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+
+  // issue the page copies of logical block blk into stage s (thread 0 only)
+  auto issue = [&](int blk, int s) {
+    uint8_t* kdst = smem + s * L::kStage;
+    uint8_t* vdst = kdst + 8 * L::kPage;
+    const int pg0 = blk * 8;
+    const int npg = min(8, (L_len - blk * kKB + 15) / 16);
+    mbar_expect_tx(&bars[s], (uint32_t)(2 * npg * L::kPage));
+    for (int i = 0; i < npg; ++i) {
+      int pg = bt[pg0 + i];
+      if (pg < 0 || pg >= p.num_pages) { atomicOr(p.err, kDevBadPage); pg = 0; }
+      const long long off = ((long long)pg * p.KVH + g) * L::kPage;
+      bulk_g2s(kdst + i * L::kPage, p.k8p + off, L::kPage, &bars[s]);
+      bulk_g2s(vdst + i * L::kPage, p.v8p + off, L::kPage, &bars[s]);
+    }
+  };
+  if (tid == 0) {
+    issue(blo, 0);
+    if (blo + 1 < bhi) issue(blo + 1, 1);
+  }
+
+  for (int blk = blo; blk < bhi; ++blk) {
+    const int j = blk - blo;
+    const int s = j & 1;
+    const uint32_t ph = (j >> 1) & 1;
+    if (!mbar_wait(&bars[s], ph, &s_abort, p.err)) break;
+    const uint8_t* kblk = smem + s * L::kStage;
+    const uint8_t* vblk = kblk + 8 * L::kPage;
+    const int nkeys = min(kKB, L_len - blk * kKB);
+    // ---- scores: thread t = key t, every head of the group
+    int S[8];
+#pragma unroll
+    for (int hh = 0; hh < 8; ++hh) S[hh] = 0;
+    if (tid < nkeys) {
+      const uint8_t* krow = kblk + tid * DH;
+#pragma unroll
+      for (int k = 0; k < DH / 16; ++k) {
+        const int ch = (k + tid) & (DH / 16 - 1);            // rotate chunks: conflict-free
+        const uint4 kw = *reinterpret_cast<const uint4*>(krow + ch * 16);
+#pragma unroll
+        for (int hh = 0; hh < 8; ++hh) {
+          if (hh < gq) {
+            const uint4 qw = *reinterpret_cast<const uint4*>(sq + hh * DH + ch * 16);
+            S[hh] = __dp4a((int)kw.x, (int)qw.x, S[hh]);
+            S[hh] = __dp4a((int)kw.y, (int)qw.y, S[hh]);
+            S[hh] = __dp4a((int)kw.z, (int)qw.z, S[hh]);
+            S[hh] = __dp4a((int)kw.w, (int)qw.w, S[hh]);
+          }
+        }
+      }
+    } else {
+#pragma unroll
+      for (int hh = 0; hh < 8; ++hh) S[hh] = INT32_MIN;     // keys past the sequence end
+    }
+    // ---- block max per head (exact, order-free)
+#pragma unroll
+    for (int hh = 0; hh < 8; ++hh) {
+      if (hh < gq) {
+        int m = S[hh];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if (lane == 0) red[warp * 8 + hh] = m;
+      }
+    }
+    __syncthreads();
+    // ---- chain: eh for (head, key t), l_b per head
+    const int ekb = p.ek[bg * p.max_blocks + blk];
+#pragma unroll
+    for (int hh = 0; hh < 8; ++hh) {
+      if (hh < gq) {
+        const int m = max(max(red[hh], red[8 + hh]), max(red[16 + hh], red[24 + hh]));
+        const uint32_t G = g_fold(p.gbase, p.eq[(long long)b * p.H + g * gq + hh] + ekb);
+        const int nbv = nb_of(m, G);
+        const uint32_t NBlo = (uint32_t)nbv << kBHI;
+        const int dm = 1 << max(0, 30 - (31 - __clz((int)G)));
+        const int sc = max(S[hh], m - dm);
+        const uint32_t d = NBlo + (uint32_t)sc * (0u - G);
+        uint32_t e = tab[d >> kIdxShift];
+        int lbw = (int)e;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) lbw += __shfl_xor_sync(0xffffffffu, lbw, o);
+        if (lane == 0) red[32 + warp * 8 + hh] = lbw;      // second reduction area
+        if (SINK && blk == 0 && tid == 0 && L_len > 1) {
+          red[64 + hh] = (int)e;                          // eh0, kept out of the PV product
+          e = 0;
+        }
+        seh[hh * 128 + tid] = (uint8_t)e;
+        if (tid == 0) red[72 + hh] = nbv;
+      }
+    }
+    __syncthreads();
+    // ---- PV: thread c = channel, A[hh] = sum_k eh[hh][k] * v8[k][c] (exact int32)
+    if (tid < DH) {
+      int A[8];
+#pragma unroll
+      for (int hh = 0; hh < 8; ++hh) A[hh] = 0;
+      const int npg = (nkeys + 15) / 16;
+#pragma unroll 1
+      for (int i = 0; i < 8; ++i) {
+        const int pgi = (i + tid) & 7;                       // rotate pages: conflict-free
+        if (pgi >= npg) continue;
+        const uint4 vw = *reinterpret_cast<const uint4*>(vblk + pgi * L::kPage + tid * 16);
+#pragma unroll
+        for (int hh = 0; hh < 8; ++hh) {
+          if (hh < gq) {
+            const uint4 ew = *reinterpret_cast<const uint4*>(seh + hh * 128 + pgi * 16);
+            uint32_t a = (uint32_t)A[hh];
+            a = dp4a_us(ew.x, vw.x, a);
+            a = dp4a_us(ew.y, vw.y, a);
+            a = dp4a_us(ew.z, vw.z, a);
+            a = dp4a_us(ew.w, vw.w, a);
+            A[hh] = (int)a;
+          }
+        }
+      }
+      int32_t* dstA = p.partA + ((bg * p.max_blocks + blk) * gq) * DH;
+#pragma unroll
+      for (int hh = 0; hh < 8; ++hh) if (hh < gq) dstA[hh * DH + tid] = A[hh];
+    }
+    if (tid < gq) {
+      const int hh = tid;
+      const int lb = red[32 + hh] + red[40 + hh] + red[48 + hh] + red[56 + hh];
+      const int e0 = (SINK && blk == 0 && L_len > 1) ? red[64 + hh] : 0;
+      p.partM[(bg * p.max_blocks + blk) * gq + hh] = make_int4(red[72 + hh], lb, e0, 0);
+    }
+    __syncthreads();                                         // stage s and red/seh are free
+    if (tid == 0 && blk + 2 < bhi) issue(blk + 2, s);
+  }
+
+  // ---- ticket: the last split of this (sequence, kv head) merges, in ascending block order
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    const unsigned int t = atomicAdd(&p.tickets[bg], 1u);
+    s_last = (t == (unsigned int)(nsplit - 1));
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  if (tid == 0) p.tickets[bg] = 0u;                          // ready for the next launch
+  if (tid >= DH) return;
+  const int c = tid;
+  const int evs0 = SINK ? p.ev0[bg] : 0;
+  int v0c = 0;
+  if (SINK && L_len > 1) {
+    const int pg = bt[0];
+    v0c = (int)p.v8p[((long long)pg * p.KVH + g) * L::kPage + c * 16 + 0];
+  }
+  for (int hh = 0; hh < gq; ++hh) {
+    float Orow = 0.0f, lrow = 0.0f;
+    int nbrow = 0;
+    bool have_row = false;
+    for (int s0 = 0; s0 < nblk; s0 += kSEG) {
+      float O = 0.0f, lseg = 0.0f;
+      int nbrun = 0;
+      bool have = false;
+      const int s1 = min(nblk, s0 + kSEG);
+      for (int blk = s0; blk < s1; ++blk) {
+        const int4 m4 = __ldcg(&p.partM[(bg * p.max_blocks + blk) * gq + hh]);
+        const int A = __ldcg(&p.partA[((bg * p.max_blocks + blk) * gq + hh) * DH + c]);
+        if (!have) { nbrun = m4.x; have = true; }
+        const int D = m4.x - nbrun;
+        int sg = 0;
+        if (D > 0) { O = rescale(O, D); lseg = rescale(lseg, D); nbrun = m4.x; }
+        else sg = -D;
+        if (sg > kSWIN) continue;
+        if (SINK && blk == 0 && L_len > 1) O = fold_term(O, m4.z * v0c, pow2f(-(sg + evs0)));
+        O = fold_term(O, A, pow2f(-(sg + p.ev[bg * p.max_blocks + blk])));
+        lseg = fold_term(lseg, m4.y, pow2f(-sg));
+      }
+      if (!have) continue;
+      if (!have_row) { nbrow = nbrun; have_row = true; }
+      const int D2 = nbrun - nbrow;
+      int s2 = 0;
+      if (D2 > 0) { Orow = rescale(Orow, D2); lrow = rescale(lrow, D2); nbrow = nbrun; }
+      else s2 = -D2;
+      if (s2 > kSWIN) continue;
+      Orow = __fadd_rn(Orow, rescale(O, s2));
+      lrow = __fadd_rn(lrow, rescale(lseg, s2));
+    }
+    const float y = (lrow != 0.0f) ? __fdiv_rn(Orow, lrow) : 0.0f;
+    OutT* dst = reinterpret_cast<OutT*>(p.out) + b * p.os0 + (long long)(g * gq + hh) * p.os1 + c * p.os2;
+    *dst = from_f32<OutT>(y);
+  }
+}
+
+// Decode lattice writer: quantise a sequence's K and V (bf16/f16/f32, any strides) into the
+// paged lattice.  One CTA per (logical block, kv head, sequence); the block exponent is over
+// the block's present rows (reference/lssab_torch.py:62-85); with the sink on, key 0 is
+// quantised alone and block 0's value exponent covers keys 1.. (reference/lssab9_torch.py:124-132).
+// Source element (b, t, g, c) is at src + seq_off[b] + t*st + g*sg + c*sc.
+template <typename InT>
+__global__ void __launch_bounds__(256)
+decode_prep_kernel(const InT* __restrict__ ksrc, const InT* __restrict__ vsrc, const long long* __restrict__ seq_off,
+                   long long st, long long sg, long long sc, int B, int KVH, int dh, const int32_t* __restrict__ seq_lens,
+                   const int32_t* __restrict__ block_table, int max_pages, int max_blocks, int num_pages, int vmode,
+                   int8_t* __restrict__ k8p, int8_t* __restrict__ v8p, int32_t* __restrict__ ek, int32_t* __restrict__ ev,
+                   int32_t* __restrict__ ev0, int* __restrict__ err) {
+  const int blk = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+  const int L_len = seq_lens[b];
+  const int nblk = (L_len + kKB - 1) / kKB;
+  if (blk >= nblk) return;
+  if (nblk > max_blocks || (L_len + 15) / 16 > max_pages) {        // lattice arrays too short
+    if (threadIdx.x == 0) atomicOr(err, kDevBadPage);
+    return;
+  }
+  const int lo = blk * kKB, hi = min(L_len, lo + kKB);
+  const int n = (hi - lo) * dh;
+  __shared__ float red[4][8];
+  const long long base = seq_off[b] + g * sg;
+  const int32_t* bt = block_table + (long long)b * max_pages;
+  for (int which = 0; which < 2; ++which) {
+    const InT* src = (which == 0) ? ksrc : vsrc;
+    const int mode = (which == 0) ? 0 : vmode;
+    const bool split0 = (mode == 2) && (blk == 0) && (L_len > 1);
+    float m = 0.0f, m0 = 0.0f;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      const int r = lo + i / dh, c = i % dh;
+      const float a = fabsf(to_f32(src[base + (long long)r * st + (long long)c * sc]));
+      if (split0 && r == 0) m0 = fmaxf(m0, a); else m = fmaxf(m, a);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, o));
+    }
+    if ((threadIdx.x & 31) == 0) { red[which * 2][threadIdx.x >> 5] = m; red[which * 2 + 1][threadIdx.x >> 5] = m0; }
+    __syncthreads();
+    m = 0.0f; m0 = 0.0f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) { m = fmaxf(m, red[which * 2][w]); m0 = fmaxf(m0, red[which * 2 + 1][w]); }
+    const int e = pow2_exponent(m, mode == 0 ? 40 : 48);
+    const int ez = split0 ? pow2_exponent(m0, 48) : e;
+    const float scl = pow2f(e), scl0 = pow2f(ez);
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      const int r = lo + i / dh, c = i % dh;
+      const float x = to_f32(src[base + (long long)r * st + (long long)c * sc]);
+      const int q = quant8(x, (split0 && r == 0) ? scl0 : scl);
+      int pg = bt[r >> 4];
+      if (pg < 0 || pg >= num_pages) { atomicOr(err, kDevBadPage); continue; }
+      const long long pbase = ((long long)pg * KVH + g) * 16 * dh;
+      if (which == 0) k8p[pbase + (r & 15) * dh + c] = (int8_t)q;
+      else v8p[pbase + c * 16 + (r & 15)] = (int8_t)q;
+    }
+    // zero the unused rows of the last page so the bulk copies read defined bytes
+    if (blk == nblk - 1 && (hi & 15)) {
+      int pg = bt[(hi - 1) >> 4];
+      if (pg >= 0 && pg < num_pages) {
+        const long long pbase = ((long long)pg * KVH + g) * 16 * dh;
+        const int nz = (16 - (hi & 15)) * dh;
+        for (int i = threadIdx.x; i < nz; i += blockDim.x) {
+          const int rr = (hi & 15) + i / dh, c = i % dh;
+          if (which == 0) k8p[pbase + rr * dh + c] = 0;
+          else v8p[pbase + c * 16 + rr] = 0;
+        }
+      }
+    }
+    if (threadIdx.x == 0) {
+      const long long o = ((long long)b * KVH + g) * max_blocks + blk;
+      if (which == 0) ek[o] = e;
+      else {
+        ev[o] = e;
+        if (mode == 2 && blk == 0) ev0[(long long)b * KVH + g] = ez;
+        if (mode != 0 && (e < -32 || e > 40)) atomicOr(err, kDevEvRange);
+      }
+    }
+    __syncthreads();
+  }
+}
+
+}  // namespace lssab8

@@ -1,0 +1,114 @@
+// PREP kernels: the LSSA-B8 quantisers (P1 query rows, P2 K/V 128-key blocks, P3 the B9.1
+// sink value grid).  Memory-bound byte work: one warp per query row, one CTA per
+// (batch, kv head, key block).  Max reductions are exact and order-free, so warp shuffles
+// are used freely; nothing here rounds except rint(x * 2^e), which is exact-or-zero.
+#pragma once
+#include "common.cuh"
+
+namespace lssab8 {
+
+struct Strides4 { long long s0, s1, s2, s3; };
+
+// P1 (reference/t10_attn.py:40-48; golden reference/lssab_golden.py:228-229).
+// x [B, H, T, dh] (any strides) -> q8 [B, H, Tpad, dh] int8, eq [B, H, Tpad] int32.
+// Rows t in [T, Tpad) are written as zeros (they are padding for the 128-row TMA tiles).
+template <typename InT>
+__global__ void __launch_bounds__(256)
+quant_rows_kernel(const InT* __restrict__ x, Strides4 xs, int B, int H, int T, int dh, int Tpad,
+                  int8_t* __restrict__ q8, int32_t* __restrict__ eq) {
+  const int warps = blockDim.x >> 5;
+  const long long row = (long long)blockIdx.x * warps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  const long long nrows = (long long)B * H * Tpad;
+  if (row >= nrows) return;
+  const int t = (int)(row % Tpad);
+  const long long bh = row / Tpad;
+  const int h = (int)(bh % H), b = (int)(bh / H);
+  int8_t* dst = q8 + row * dh;
+  if (t >= T) {
+    for (int c = lane; c < dh; c += 32) dst[c] = 0;
+    if (lane == 0) eq[row] = 0;
+    return;
+  }
+  const InT* src = x + b * xs.s0 + h * xs.s1 + (long long)t * xs.s2;
+  constexpr int kMaxPer = 8;                  // dh <= 256
+  float v[kMaxPer];
+  float m = 0.0f;
+#pragma unroll
+  for (int i = 0; i < kMaxPer; ++i) {
+    int c = lane + 32 * i;
+    v[i] = (c < dh) ? to_f32(src[(long long)c * xs.s3]) : 0.0f;
+    m = fmaxf(m, fabsf(v[i]));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  const int e = pow2_exponent(m, 40);
+  const float sc = pow2f(e);
+#pragma unroll
+  for (int i = 0; i < kMaxPer; ++i) {
+    int c = lane + 32 * i;
+    if (c < dh) dst[c] = (int8_t)quant8(v[i], sc);
+  }
+  if (lane == 0) eq[row] = e;
+}
+
+// P2/P3 (reference/lssab_torch.py:62-85; reference/lssab9_torch.py:46-65,121-132,158).
+// One CTA per (key block, kv head, batch).  x [B, KVH, T, dh] -> x8 [B, KVH, Tpad, dh],
+// e [B, KVH, nblk], e0 [B, KVH] (sink mode only).
+//   mode 0: B8 grid, exponent clamp [-32, 40]
+//   mode 1: B9 value grid, clamp [-32, 48], then e outside [-32, 40] sets kDevEvRange
+//   mode 2: B9.1 sink_alone: as mode 1, and when T > 1 key 0 is quantised alone (e0) while
+//           block 0's exponent covers keys 1 .. min(KB, T)-1.
+template <typename InT>
+__global__ void __launch_bounds__(256)
+quant_blocks_kernel(const InT* __restrict__ x, Strides4 xs, int B, int KVH, int T, int dh, int Tpad,
+                    int mode, int8_t* __restrict__ x8, int32_t* __restrict__ eblk, int32_t* __restrict__ e0,
+                    int* __restrict__ err) {
+  const int blk = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+  const int nblk = (T + kKB - 1) / kKB;
+  const int lo = blk * kKB;
+  const int hi = min(T, lo + kKB);
+  const InT* src = x + b * xs.s0 + g * xs.s1;
+  int8_t* dst = x8 + ((long long)(b * KVH + g) * Tpad) * dh;
+  const bool split0 = (mode == 2) && (blk == 0) && (T > 1);
+  __shared__ float red[2][8];
+  // pass 1: amax over the block's present rows (and key 0 alone when split0)
+  float m = 0.0f, m0 = 0.0f;
+  const int n = (hi - lo) * dh;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    int r = lo + i / dh, c = i % dh;
+    float a = fabsf(to_f32(src[(long long)r * xs.s2 + (long long)c * xs.s3]));
+    if (split0 && r == 0) m0 = fmaxf(m0, a); else m = fmaxf(m, a);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, o));
+  }
+  if ((threadIdx.x & 31) == 0) { red[0][threadIdx.x >> 5] = m; red[1][threadIdx.x >> 5] = m0; }
+  __syncthreads();
+  m = 0.0f; m0 = 0.0f;
+  for (int w = 0; w < (int)(blockDim.x >> 5); ++w) { m = fmaxf(m, red[0][w]); m0 = fmaxf(m0, red[1][w]); }
+  const int hic = (mode == 0) ? 40 : 48;
+  const int e = pow2_exponent(m, hic);
+  const int ez = split0 ? pow2_exponent(m0, 48) : e;
+  const float sc = pow2f(e), sc0 = pow2f(ez);
+  // pass 2: quantise (re-reading the block keeps registers free; it is L2/L1 resident)
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    int r = lo + i / dh, c = i % dh;
+    float v = to_f32(src[(long long)r * xs.s2 + (long long)c * xs.s3]);
+    dst[(long long)r * dh + c] = (int8_t)quant8(v, (split0 && r == 0) ? sc0 : sc);
+  }
+  // zero the padding rows of the last block
+  if (blk == nblk - 1) {
+    const int npad = (Tpad - hi) * dh;
+    for (int i = threadIdx.x; i < npad; i += blockDim.x) dst[(long long)hi * dh + i] = 0;
+  }
+  if (threadIdx.x == 0) {
+    eblk[(long long)(b * KVH + g) * nblk + blk] = e;
+    if (mode == 2 && blk == 0) e0[b * KVH + g] = ez;
+    if (mode != 0 && (e < -32 || e > 40)) atomicOr(err, kDevEvRange);
+  }
+}
+
+}  // namespace lssab8

@@ -1,0 +1,89 @@
+"""Drop-in for reference/lssab8_torch.py: the LSSA-B8 eager-attention replacement on B200.
+
+Same entry points, arguments, return value and asserts as the reference module
+(reference/lssab8_torch.py:103-310); the arithmetic runs in liblssab8_b200.so (tcgen05 int8 MMA
+prefill, sm_100a) and is bit-identical to the reference's.
+
+  make_lssab8_long_attn(...) -> attn(module, query, key, value, attention_mask, ...) -> (out, None)
+      query [1, H, T, dh], key/value [1, KVH, T, dh] CUDA tensors (float32/float16/bfloat16,
+      contiguous or not); out [1, T, H, dh] in query.dtype, contiguous.  Batch must be 1
+      (AssertionError, like the reference); lockstep_b200.attention.prefill is the batched form.
+  make_lssab8_attn, ARM_SPECS, build_arm8: as in the reference.
+
+Parameters the reference calls SCHEDULE (head_chunk, qblk, kblk; gate S10) and `skip` (exact,
+gate S6) are accepted and do not change a bit.  Contract parameters must be the contract's
+values (kb=128, bhi=26, n=7, w_loc=9, weight="rn", s_win=32, seg_keys=4096, qexp="row",
+clamp_sh=True): other arms of the reference (L8-RN-W8, L8-TR, L8-RN-n8, L8-RN-KB64, L16) are
+research controls with no B200 kernel and raise NotImplementedError, as does a key offset `mu`.
+"""
+from . import attention as _A
+
+BHI = 26
+KB = 128
+SEG_KEYS = 32 * 128
+S_WIN = 32
+W_LOC = 9
+NIDX = 7
+NB_SENT = -(1 << 58)
+
+
+def _contract_check(kb, bhi, n, w_loc, weight, s_win, seg_keys, mu, qexp, clamp_sh):
+    assert n <= bhi and qexp in ("row", "head")
+    assert seg_keys % kb == 0, "a segment must be a whole number of blocks"
+    if mu is not None:
+        raise NotImplementedError("key offset mu: not built for B200 yet")
+    if (kb, bhi, n, w_loc, weight, s_win, seg_keys, qexp, bool(clamp_sh)) != (KB, BHI, NIDX, W_LOC, "rn", S_WIN,
+                                                                               SEG_KEYS, "row", True):
+        raise NotImplementedError("only the LSSA-B8 contract arm (L8 = L8-RN-W9) has a B200 kernel")
+
+
+def _attn_closure(sink):
+    def attn(module, query, key, value, attention_mask, *args, **kw):
+        Bsz, H, T, dh = query.shape
+        assert Bsz == 1, "B=1 windows only"
+        out = _A.prefill(query, key, value, sink=sink, out_dtype=query.dtype)
+        return out, None
+    return attn
+
+
+def make_lssab8_long_attn(kb=KB, bhi=BHI, n=NIDX, w_loc=W_LOC, weight="rn", s_win=S_WIN,
+                          seg_keys=SEG_KEYS, head_chunk=7, qblk=1024, kblk=8192, mu=None,
+                          qexp="row", clamp_sh=True, stats=None, skip=True):
+    """eager_attention_forward replacement implementing LSSA-B8 (reference/lssab8_torch.py:103-272).
+
+    `stats` (the reference's debug counters) is not collected by the kernels and stays untouched."""
+    _contract_check(kb, bhi, n, w_loc, weight, s_win, seg_keys, mu, qexp, clamp_sh)
+    return _attn_closure(sink=False)
+
+
+def make_lssab8_attn(kb=KB, bhi=BHI, n=NIDX, w_loc=W_LOC, weight="rn", head_chunk=16,
+                     mu=None, qexp="row", stats=None, **kw):
+    """Short-context entry point (reference/lssab8_torch.py:275-281): the same function."""
+    return make_lssab8_long_attn(kb=kb, bhi=bhi, n=n, w_loc=w_loc, weight=weight,
+                                 head_chunk=head_chunk, qblk=1 << 20, kblk=1 << 20,
+                                 mu=mu, qexp=qexp, stats=stats, **kw)
+
+
+ARM_SPECS = {
+    "L8":          dict(kb=128, n=7, w_loc=9, weight="rn"),
+    "L8-RN-W9":    dict(kb=128, n=7, w_loc=9, weight="rn"),
+    "L8-RN-W8":    dict(kb=128, n=7, w_loc=8, weight="rn"),
+    "L8-TR":       dict(kb=128, n=7, w_loc=9, weight="tr"),
+    "L8-RN-n8":    dict(kb=128, n=8, w_loc=9, weight="rn"),
+    "L8-RN-KB64":  dict(kb=64,  n=7, w_loc=9, weight="rn"),
+    "L16":         dict(kb=128, n=13, w_loc=16, weight="l16"),
+}
+
+
+def build_arm8(name, bhi=BHI, head_chunk=7, mu=None, qblk=1024, kblk=8192, stats=None,
+               long=True, qexp="row"):
+    """Return an eager_attention_forward for an LSSA-B8 arm, or None if `name` is not one
+    (reference/lssab8_torch.py:296-310).  Control arms raise NotImplementedError."""
+    spec = ARM_SPECS.get(name)
+    if spec is None:
+        return None
+    sk = dict(spec)
+    if long:
+        return make_lssab8_long_attn(head_chunk=head_chunk, qblk=qblk, kblk=kblk, mu=mu,
+                                     bhi=bhi, stats=stats, qexp=qexp, **sk)
+    return make_lssab8_attn(head_chunk=head_chunk, mu=mu, bhi=bhi, stats=stats, qexp=qexp, **sk)

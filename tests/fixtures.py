@@ -1,0 +1,142 @@
+"""Test fixtures that restate the reference selftest's case generators.
+
+Each generator draws exactly the arrays the reference selftest draws
+(``reference/lssab8_selftest.py:157-241``, ``reference/lssab9_selftest.py:44-48``), so the
+reference's own outputs on them -- recorded as digests in ``tests/golden/`` by
+``tests/golden/make_golden.py`` -- pin the oracle and the CUDA path.  ``make_golden.py``
+asserts that these constructors reproduce the reference's arrays bit for bit before it
+records anything.
+"""
+import numpy as np
+
+KB = 128
+BHI = 26
+
+
+def g_base(dh=128):
+    import math
+    return round((2.0 ** BHI) / (math.sqrt(dh) * math.log(2.0)))
+
+
+def qk_from_scores(S, dh=128, pin_block=KB):
+    """One query row and T keys whose quantisation is the identity (e_q = e_k = 0) and whose
+    int8 scores equal S [1, T] exactly (construction of reference/lssab_selftest.py:25-41):
+    q = [64, 1, ..., 1, 0]; key j = [a_j, r_j, 0, ..., 0] with S_j = 64 a_j + r_j; one key per
+    block carries 127 in the channel q zeroes, pinning the block amax to 127."""
+    Tq, Tk = S.shape
+    assert Tq == 1
+    q = np.zeros((1, 1, dh), np.float32)
+    q[0, 0, 0] = 64.0
+    q[0, 0, 1:dh - 1] = 1.0
+    k = np.zeros((1, Tk, dh), np.float32)
+    a = np.clip(np.round(S[0] / 64.0), -127, 127)
+    r = S[0] - 64 * a
+    assert np.abs(r).max() <= 127
+    k[0, :, 0] = a
+    k[0, :, 1] = r
+    for b in range(0, Tk, pin_block):
+        k[0, b, dh - 1] = 127.0
+    return q, k
+
+
+def random_cases():
+    cs = []
+    for T in (256, 320, 512, 1000, 1024, 2048):
+        for (H, KVH) in ((1, 1), (4, 2), (7, 1)):
+            g = np.random.RandomState(1000 + T + H)
+            cs.append(dict(tag="rand_T%d_H%dx%d" % (T, H, KVH),
+                           q=g.standard_normal((H, T, 128)).astype(np.float32),
+                           k=g.standard_normal((KVH, T, 128)).astype(np.float32),
+                           v=g.standard_normal((KVH, T, 128)).astype(np.float32)))
+    return cs
+
+
+def jump_cases():
+    cs = []
+    G = g_base(128)
+    for jump in (50, 126, 127, 200, 400):
+        dS = int(round(jump * (1 << BHI) / G))
+        for T in (512, 1024):
+            S = np.zeros((1, T), np.int64)
+            for b in range(T // KB):
+                S[0, b * KB:(b + 1) * KB] = (b % 2) * dS - np.arange(KB) % 37
+            S = np.clip(S, -8255, 8255)
+            q1, k1 = qk_from_scores(S)
+            q = np.zeros((1, T, 128), np.float32)
+            q[0] = q1[0, 0][None, :]
+            g = np.random.RandomState(7 * T + jump)
+            v = (g.standard_normal((1, T, 128)) * 8).astype(np.float32)
+            cs.append(dict(tag="jump%d_T%d" % (jump, T), q=q, k=k1, v=v))
+    return cs
+
+
+def ftz_cases():
+    cs = []
+    for sp in (0, 8, 16, 24, 32, 40):
+        T = 512
+        g = np.random.RandomState(555 + sp)
+        v = g.standard_normal((1, T, 128)).astype(np.float32)
+        for b in range(0, T, KB):
+            v[:, b:b + KB] *= np.float32(2.0 ** (-(b // KB) * sp))
+        cs.append(dict(tag="ftz_evladder_%d" % sp,
+                       q=g.standard_normal((2, T, 128)).astype(np.float32),
+                       k=g.standard_normal((1, T, 128)).astype(np.float32), v=v))
+    T = 384
+    g = np.random.RandomState(99)
+    v = g.standard_normal((1, T, 128)).astype(np.float32)
+    v[:, :KB] *= np.float32(2.0 ** 30)
+    v[:, KB:2 * KB] *= np.float32(2.0 ** -30)
+    cs.append(dict(tag="ftz_extreme_v", q=g.standard_normal((2, T, 128)).astype(np.float32),
+                   k=g.standard_normal((1, T, 128)).astype(np.float32), v=v))
+    return cs
+
+
+def degenerate_cases():
+    cs = []
+    for T in (1, 2, 128, 129, 130, 255, 257, 384):
+        g = np.random.RandomState(31 * T)
+        cs.append(dict(tag="deg_T%d" % T,
+                       q=g.standard_normal((2, T, 128)).astype(np.float32),
+                       k=g.standard_normal((1, T, 128)).astype(np.float32),
+                       v=g.standard_normal((1, T, 128)).astype(np.float32)))
+    for val in (0, 137, -55):
+        T = 256
+        S = np.full((1, T), val, np.int64)
+        q1, k1 = qk_from_scores(S)
+        q = np.zeros((1, T, 128), np.float32)
+        q[0] = q1[0, 0][None, :]
+        g = np.random.RandomState(abs(val) + 5)
+        cs.append(dict(tag="ties_%d" % val, q=q, k=k1,
+                       v=g.standard_normal((1, T, 128)).astype(np.float32)))
+    T = 512
+    S = np.random.RandomState(3).randint(-20, 20, size=(1, T)).astype(np.int64)
+    S[0, KB:2 * KB] = -8000
+    S[0, T - 1] = 300
+    q1, k1 = qk_from_scores(S)
+    q = np.zeros((1, T, 128), np.float32)
+    q[0] = q1[0, 0][None, :]
+    cs.append(dict(tag="dead_block", q=q, k=k1,
+                   v=np.random.RandomState(4).standard_normal((1, T, 128)).astype(np.float32)))
+    return cs
+
+
+def sink300_cases():
+    """reference/lssab9_selftest.py:44-48: key 0's value x300."""
+    rng = np.random.default_rng(9)
+    cs = []
+    for T in (1, 2, 128, 129, 300):
+        q = rng.standard_normal((4, T, 128)).astype(np.float32)
+        k = rng.standard_normal((2, T, 128)).astype(np.float32)
+        v = rng.standard_normal((2, T, 128)).astype(np.float32)
+        v[:, 0] *= 300.0
+        cs.append(dict(tag="sink300_T%d" % T, q=q, k=k, v=v))
+    return cs
+
+
+def all_cases():
+    return random_cases() + jump_cases() + ftz_cases() + degenerate_cases()
+
+
+def digest(a):
+    import hashlib
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
