@@ -62,8 +62,9 @@ class Clocks:
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), "--query-gpu=" + self.Q,
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            time.sleep(1.5)                      # nvidia-smi start-up: sample from the first timed step on
         except OSError:
             self.proc = None
         return self
@@ -164,7 +165,8 @@ def run_gpu(args):
         step()
     barrier()
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    with Clocks(local) as clk:
+    clk = Clocks(local).__enter__()
+    if True:
         for i in range(args.steps):
             flush.fill_(float(i))                    # L2 flush, outside the timed events
             evs[i][0].record()
@@ -250,6 +252,7 @@ def run_gpu(args):
     dms = sum(dec_ms) / len(dec_ms)
     lattice_bytes = DEC["B"] * DEC["KVH"] * DEC["L"] * DEC["dh"] * 2
     dec_gbs = lattice_bytes / (dms * 1e-3) / 1e9
+    clk.__exit__(None, None, None)
     A.check_device_errors(dev)
     decode = {"config": "cfg3 B32 H32/KVH8 dh128 L8192, 16 splits, sink off", "ms_per_step": round(dms, 4),
               "kv_gbps": round(dec_gbs, 1), "frac_hbm": round(dec_gbs / peaks["hbm"], 4),
@@ -352,7 +355,7 @@ def run_reference(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
