@@ -295,7 +295,7 @@ def run_gpu(args):
     if gather:
         line["gather"] = gather
     if rank == 0 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(sample_batches=1)
+        line["cpu_baseline"] = cpu_baseline(sample_batches=CFG["B"])
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -175,17 +175,11 @@ int launch_prefill_t(const CUtensorMap& tq, const CUtensorMap& tk, const CUtenso
   // at least ~116 KB so only one CTA (and one 512-column TMEM allocation) lands on an SM
   int smem = (multi ? L::kBytesMulti : L::kBytesSingle) + 1024;
   if (smem < 116 * 1024) smem = 116 * 1024;
-  auto kfn = prefill_kernel<DH, SINK, OutT>;
-  static int set_bytes[64] = {0};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && set_bytes[dev] < smem) {
-    if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytesMulti + 1024) != cudaSuccess)
-      return kErrCuda;
-    set_bytes[dev] = L::kBytesMulti + 1024;
-  }
+  auto kfn = multi ? prefill_kernel<DH, SINK, OutT, true> : prefill_kernel<DH, SINK, OutT, false>;
+  if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytesMulti + 1024) != cudaSuccess)
+    return kErrCuda;
   dim3 grid(a.Tpad / 128, a.H, a.B);
-  kfn<<<grid, 448, smem, st>>>(tq, tk, tv, a, multi);
+  kfn<<<grid, 448, smem, st>>>(tq, tk, tv, a);
   return launch_rc();
 }
 

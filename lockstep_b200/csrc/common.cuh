@@ -100,10 +100,19 @@ __device__ __forceinline__ float rescale(float x, int D) {
   return (e >= 1 && ne >= 1) ? __uint_as_float((u & 0x807FFFFFu) | ((uint32_t)ne << 23)) : 0.0f;
 }
 
-// One fold term: fl(O + f32(A) * 2^esc).  f32(A) is exact (|A| < 2^24) and so is the product
-// (its exponent stays normal), so this is one RNE addition.
+// Exact int -> binary32 for |a| < 2^22 without the conversion pipe: the bit pattern a + 0x4B400000
+// is the float 1.5*2^23 + a (its exponent cannot change for |a| < 2^22), and subtracting
+// 1.5*2^23 is exact.  Every integer the fold converts is below 2^22: |A_b| <= 4,145,280,
+// l_b <= 32,640, the sink product eh0*v8 <= 32,385 (docs/contract/BLOCK_EXPONENT_VARIANT.md B8.4).
+__device__ __forceinline__ float i2f_small(int a) {
+  return __fsub_rn(__int_as_float(a + 0x4B400000), 12582912.0f);
+}
+
+// One fold term: fl(O + f32(A) * 2^esc).  f32(A) is exact and so is the product (its exponent
+// stays in the normal range, B8.5 "Ranges"), hence RN(A*sc + O) in one fused multiply-add is the
+// same single rounding as the contract's add of the exact product.
 __device__ __forceinline__ float fold_term(float O, int A, float sc) {
-  return __fadd_rn(O, __fmul_rn(__int2float_rn(A), sc));
+  return __fmaf_rn(i2f_small(A), sc, O);
 }
 
 // least multiple of 2^26 >= m*G, returned as NB / 2^26 (|NB| < 2^52, so it fits in int32).
@@ -143,6 +152,15 @@ __device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait that may suspend the thread for up to ~20 us while the phase is incomplete, so a
+// waiting warp issues a handful of instructions instead of spinning.
+__device__ __forceinline__ bool mbar_try_suspend(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}"
+               : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity), "r"(20000u) : "memory");
+  return ok != 0;
+}
+
 // Bounded wait on an mbarrier phase.  Gives up after ~2 s of wall time or as soon as another
 // role of the CTA has raised *abort; on giving up it records kDevTimeout in *err and returns
 // false so the caller can unwind without hanging the GPU.
@@ -150,8 +168,8 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   if (mbar_try(bar, parity)) return true;
   uint64_t t0 = globaltimer();
   for (uint32_t it = 0;; ++it) {
-    if (mbar_try(bar, parity)) return true;
-    if ((it & 255u) == 255u) {
+    if (mbar_try_suspend(bar, parity)) return true;
+    if ((it & 15u) == 15u) {
       if (*abort) return false;
       if (globaltimer() - t0 > 2000000000ull) {
         *abort = 1;

@@ -137,10 +137,11 @@ enum BarId : int {
   kBarPFull = 13, kBarPEmpty = 15, kBarAFull = 17, kBarAEmpty = 19, kBarIFull = 21, kBarIEmpty = 23
 };
 
-template <int DH, bool SINK, typename OutT>
+template <int DH, bool SINK, typename OutT, bool MULTI>
 __global__ void __launch_bounds__(448, 1)
 prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-               const __grid_constant__ CUtensorMap tm_v, const PrefillArgs p, const int multi_seg) {
+               const __grid_constant__ CUtensorMap tm_v, const PrefillArgs p) {
+  constexpr bool multi_seg = MULTI;    // rows spanning more than one 32-block segment
   using L = PrefillSmem<DH>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);   // 1024-B aligned, still __shared__
@@ -181,7 +182,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(tmem_slot)) : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
-  if (multi_seg) {
+  if constexpr (MULTI) {
     for (int i = threadIdx.x; i < DH * 128; i += blockDim.x) orow[i] = 0.0f;
   }
   tc_fence_before();
@@ -385,7 +386,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
       tc_fence_before();
       mbar_arrive(&bars[kBarAEmpty + s]);
       const bool seg_end = ((j + 1) % kSEG == 0) || (j == nb - 1);
-      if (seg_end && multi_seg) {
+      if (MULTI && seg_end) {
         // segment -> row: the same three rules (reference/lssab8_golden.py:317-331)
         if (!have_row) { nbrow = nbrun; have_row = true; }
         const int D2 = nbrun - nbrow;
@@ -412,7 +413,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
     // ---- epilogue: out = O_row / l_row (one RN division), l_row == 0 -> 0
     const int i = tile * 128 + r;
     if (ok && i < p.T) {
-      if (!multi_seg) {
+      if constexpr (!MULTI) {
         // a single segment: O_row = 0 + rescale(O_seg, 0), l_row likewise
 #pragma unroll
         for (int c = 0; c < HD; ++c) O[c] = rescale(O[c], 0);
