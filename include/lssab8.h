@@ -36,8 +36,13 @@ enum {
   LSSAB8_EUNSUPPORTED = 2,  /* a contract-valid input these kernels do not cover (e.g. dh)    */
   LSSAB8_ECUDA = 3,         /* a CUDA runtime/driver call failed                              */
   LSSAB8_EWORKSPACE = 4,    /* the caller's workspace is smaller than *_workspace_size()      */
-  LSSAB8_EDEVICE = 5        /* the device error word is nonzero (lssab8_device_errors)        */
+  LSSAB8_EDEVICE = 5,       /* the device error word is nonzero (lssab8_device_errors)        */
+  LSSAB8_ESCRATCH = 6       /* lssab8_decode_noalloc: the problem needs more scratch than the
+                               library's fixed buffer (LSSAB8_NOALLOC_SCRATCH_BYTES)            */
 };
+
+/* Size of the fixed device scratch buffer behind lssab8_decode_noalloc (48 MiB). */
+#define LSSAB8_NOALLOC_SCRATCH_BYTES (48u << 20)
 
 /* device error bits (OR-accumulated by kernels; read with lssab8_device_errors) */
 enum {
@@ -119,6 +124,27 @@ int lssab8_decode(const void* q, int dtype, const int64_t* qs, int B, int H, int
                   const int32_t* block_table, int max_pages, int num_pages, const int8_t* k8p, const int8_t* v8p,
                   const int32_t* ek, const int32_t* ev, const int32_t* ev0, int max_blocks, int split_blocks, int sink,
                   void* out, int out_dtype, const int64_t* os, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Allocation-free decode.  No counterpart in the reference: it exists for hosts that cannot
+ * hand this library a workspace.  Some engines plan all device memory up front and give each
+ * attention call only its inputs and outputs; some plugin hosts own every device allocation and
+ * expose no allocator to the plugin.  Such callers cannot call cudaMalloc for the split-KV
+ * partials that lssab8_decode needs, so this entry point takes the same arguments as
+ * lssab8_decode minus the workspace and uses a fixed scratch buffer of
+ * LSSAB8_NOALLOC_SCRATCH_BYTES that the library holds in device memory on every GPU it is loaded
+ * on, until the process exits.  It allocates nothing.
+ *   - The problem's scratch need is lssab8_decode_workspace_size(B, H, KVH, dh, max_blocks); if it
+ *     exceeds the buffer the call returns LSSAB8_ESCRATCH and launches nothing.
+ *   - The first call on a device looks up the buffer's device address for that device (with
+ *     that device current); make that first call before any stream capture.
+ *   - Every call on a device shares the one buffer: calls that can overlap on the GPU (other
+ *     streams, other host threads) race and corrupt each other's results; serialise them.
+ * Results are bit-identical to lssab8_decode's. */
+int lssab8_decode_noalloc(const void* q, int dtype, const int64_t* qs, int B, int H, int KVH, int dh,
+                          const int32_t* seq_lens, const int32_t* block_table, int max_pages, int num_pages,
+                          const int8_t* k8p, const int8_t* v8p, const int32_t* ek, const int32_t* ev,
+                          const int32_t* ev0, int max_blocks, int split_blocks, int sink, void* out, int out_dtype,
+                          const int64_t* os, void* stream);
 
 #ifdef __cplusplus
 }

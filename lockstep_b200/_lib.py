@@ -18,6 +18,7 @@ SYMBOLS = (
     "lssab8_quant_rows", "lssab8_quant_blocks",
     "lssab8_prefill_lattice", "lssab8_prefill_workspace_size", "lssab8_prefill",
     "lssab8_decode_prep_kv", "lssab8_decode_workspace_size", "lssab8_decode",
+    "lssab8_decode_noalloc",
 )
 
 _lib = None
@@ -53,6 +54,7 @@ def load():
     L.lssab8_decode_workspace_size.argtypes = [I] * 5
     L.lssab8_decode_workspace_size.restype = SZ
     L.lssab8_decode.argtypes = [P, I, PI64, I, I, I, I, P, P, I, I, P, P, P, P, P, I, I, I, P, I, PI64, P, SZ, P]
+    L.lssab8_decode_noalloc.argtypes = [P, I, PI64, I, I, I, I, P, P, I, I, P, P, P, P, P, I, I, I, P, I, PI64, P]
     for name in SYMBOLS:
         getattr(L, name).restype = getattr(L, name).restype or I
     _lib = L

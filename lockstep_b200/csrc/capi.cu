@@ -290,6 +290,7 @@ const char* lssab8_strerror(int code) {
     case kErrCuda: return "CUDA error";
     case kErrWorkspace: return "workspace too small";
     case kErrDevice: return "device error word set";
+    case LSSAB8_ESCRATCH: return "problem needs more scratch than the fixed no-alloc buffer";
     default: return "unknown status";
   }
 }
@@ -451,6 +452,72 @@ int lssab8_decode(const void* q, int dtype, const int64_t* qs, int B, int H, int
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int64_t q4[4] = {qs[0], qs[1], 0, qs[2]};
   if ((rc = lssab8_quant_rows(q, dtype, B, H, 1, dh, q4, 1, q8, eq, stream))) return rc;
+  if (cudaMemsetAsync(base + w.tickets, 0, (size_t)B * KVH * 4, s) != cudaSuccess) return kErrCuda;
+  DecodeArgs a{};
+  a.B = B; a.H = H; a.KVH = KVH; a.dh = dh; a.group = H / KVH; a.max_blocks = max_blocks; a.max_pages = max_pages;
+  a.split_blocks = split_blocks; a.num_pages = num_pages; a.seq_lens = seq_lens; a.block_table = block_table;
+  a.k8p = k8p; a.v8p = v8p; a.ek = ek; a.ev = ev; a.ev0 = sink ? ev0 : nullptr; a.q8 = q8; a.eq = eq;
+  a.partA = reinterpret_cast<int32_t*>(base + w.partA);
+  a.partM = reinterpret_cast<int4*>(base + w.partM);
+  a.tickets = reinterpret_cast<unsigned int*>(base + w.tickets);
+  a.out = out; a.os0 = os[0]; a.os1 = os[1]; a.os2 = os[2];
+  a.gbase = gbase_of(dh);
+  a.err = ds->err;
+  const int max_splits = (max_blocks + split_blocks - 1) / split_blocks;
+  if (dh == 128) return sink ? launch_decode_out<128, true>(out_dtype, a, max_splits, s)
+                             : launch_decode_out<128, false>(out_dtype, a, max_splits, s);
+  return sink ? launch_decode_out<64, true>(out_dtype, a, max_splits, s)
+              : launch_decode_out<64, false>(out_dtype, a, max_splits, s);
+}
+
+// ------------------------------------------------------------ allocation-free decode
+// The fixed scratch of lssab8_decode_noalloc (see include/lssab8.h): a file-scope device array.
+// In host code its name is only a host-side stand-in, never a device address; the device address
+// is looked up once per device with cudaGetSymbolAddress, with that device current.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[LSSAB8_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[64] = {nullptr};
+
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return kErrCuda;
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) return kErrCuda;
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return kOk;
+}
+}  // namespace
+
+int lssab8_decode_noalloc(const void* q, int dtype, const int64_t* qs, int B, int H, int KVH, int dh,
+                          const int32_t* seq_lens, const int32_t* block_table, int max_pages, int num_pages,
+                          const int8_t* k8p, const int8_t* v8p, const int32_t* ek, const int32_t* ev,
+                          const int32_t* ev0, int max_blocks, int split_blocks, int sink, void* out, int out_dtype,
+                          const int64_t* os, void* stream) {
+  if (!q || !seq_lens || !block_table || !k8p || !v8p || !ek || !ev || (sink && !ev0) || !out ||
+      !strides_ok(qs, 3) || !strides_ok(os, 3) || B <= 0 || H <= 0 || KVH <= 0 || H % KVH || max_blocks <= 0 ||
+      split_blocks <= 0 || max_pages <= 0 || num_pages <= 0)
+    return kErrArg;
+  if ((dh != 64 && dh != 128) || H / KVH > 8) return kErrUnsupported;
+  const DecodeWs w = decode_ws(B, H, KVH, dh, max_blocks);
+  if (w.total - 256 > (size_t)LSSAB8_NOALLOC_SCRATCH_BYTES) return LSSAB8_ESCRATCH;   // base is 256-aligned
+  void* scratch = nullptr;
+  int rc = noalloc_scratch(&scratch);
+  if (rc) return rc;
+  DevState* ds = nullptr;
+  if ((rc = dev_state(&ds))) return rc;
+  uint8_t* base = static_cast<uint8_t*>(scratch);
+  int8_t* q8 = reinterpret_cast<int8_t*>(base + w.q8);
+  int32_t* eq = reinterpret_cast<int32_t*>(base + w.eq);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t q4[4] = {qs[0], qs[1], 0, qs[2]};
+  if ((rc = lssab8_quant_rows(q, dtype, B, H, 1, dh, q4, 1, q8, eq, stream))) return rc;
+  // the tickets must start at zero; the buffer keeps whatever the previous call left
   if (cudaMemsetAsync(base + w.tickets, 0, (size_t)B * KVH * 4, s) != cudaSuccess) return kErrCuda;
   DecodeArgs a{};
   a.B = B; a.H = H; a.KVH = KVH; a.dh = dh; a.group = H / KVH; a.max_blocks = max_blocks; a.max_pages = max_pages;
