@@ -82,10 +82,13 @@ int lssab8_quant_blocks(const void* x, int dtype, int B, int KVH, int T, int dh,
 /* Causal GQA prefill on a prepared lattice (the output of the two quantisers with
  * Tpad = 128*ceil(T/128)).  out[b, t, h, c] at out + b*os[0] + t*os[1] + h*os[2] + c*os[3] in
  * out_dtype.  ev0 = NULL: sink off (B8); non-NULL: B9.1 sink_alone.  dh in {64, 128}.
+ * orow_scratch: B*H*Tpad*dh floats of caller memory, needed when Tpad > 4096 (rows spanning more
+ * than one 32-block fold segment keep their row accumulator there); may be NULL otherwise.
  * The fold of reference/lssab8_torch.py:164-271 / reference/lssab9_torch.py:176-326. */
 int lssab8_prefill_lattice(const int8_t* q8, const int32_t* eq, const int8_t* k8, const int32_t* ek,
                            const int8_t* v8, const int32_t* ev, const int32_t* ev0, int B, int H, int KVH, int T,
-                           int dh, int Tpad, void* out, int out_dtype, const int64_t* os, void* stream);
+                           int dh, int Tpad, float* orow_scratch, void* out, int out_dtype, const int64_t* os,
+                           void* stream);
 
 /* Bytes of workspace lssab8_prefill needs for this shape. */
 size_t lssab8_prefill_workspace_size(int B, int H, int KVH, int T, int dh);

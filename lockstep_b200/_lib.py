@@ -46,7 +46,7 @@ def load():
     L.lssab8_device_errors.argtypes = [I, P, ctypes.POINTER(I)]
     L.lssab8_quant_rows.argtypes = [P, I, I, I, I, I, PI64, I, P, P, P]
     L.lssab8_quant_blocks.argtypes = [P, I, I, I, I, I, PI64, I, I, P, P, P, P]
-    L.lssab8_prefill_lattice.argtypes = [P] * 7 + [I] * 6 + [P, I, PI64, P]
+    L.lssab8_prefill_lattice.argtypes = [P] * 7 + [I] * 6 + [P, P, I, PI64, P]
     L.lssab8_prefill_workspace_size.argtypes = [I] * 5
     L.lssab8_prefill_workspace_size.restype = SZ
     L.lssab8_prefill.argtypes = [P, P, P, I, I, I, I, I, I, PI64, PI64, PI64, I, P, I, PI64, P, SZ, P]

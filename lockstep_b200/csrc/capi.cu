@@ -172,14 +172,14 @@ int launch_prefill_t(const CUtensorMap& tq, const CUtensorMap& tk, const CUtenso
                      cudaStream_t st) {
   using L = PrefillSmem<DH>;
   const int multi = a.nblk > kSEG;
+  if (multi && !a.orow) return kErrWorkspace;
   // at least ~116 KB so only one CTA (and one 512-column TMEM allocation) lands on an SM
-  int smem = (multi ? L::kBytesMulti : L::kBytesSingle) + 1024;
+  int smem = L::kBytes + 1024;
   if (smem < 116 * 1024) smem = 116 * 1024;
   auto kfn = multi ? prefill_kernel<DH, SINK, OutT, true> : prefill_kernel<DH, SINK, OutT, false>;
-  if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytesMulti + 1024) != cudaSuccess)
-    return kErrCuda;
+  if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return kErrCuda;
   dim3 grid(a.Tpad / 128, a.H, a.B);
-  kfn<<<grid, 448, smem, st>>>(tq, tk, tv, a);
+  kfn<<<grid, PrefillShape<DH>::kThreads, smem, st>>>(tq, tk, tv, a);
   return launch_rc();
 }
 
@@ -222,7 +222,7 @@ bool strides_ok(const int64_t* s, int n) {
 }
 
 struct PrefillWs {
-  size_t q8, eq, k8, ek, v8, ev, ev0, total;
+  size_t q8, eq, k8, ek, v8, ev, ev0, orow, total;
 };
 
 PrefillWs prefill_ws(int B, int H, int KVH, int T, int dh) {
@@ -236,6 +236,8 @@ PrefillWs prefill_ws(int B, int H, int KVH, int T, int dh) {
   w.v8 = o; o += align256((size_t)B * KVH * Tpad * dh);
   w.ev = o; o += align256((size_t)B * KVH * nblk * 4);
   w.ev0 = o; o += align256((size_t)B * KVH * 4);
+  w.orow = o;            // rows spanning more than one 32-block segment keep O_row here
+  if (nblk > (size_t)kSEG) o += align256((size_t)B * H * Tpad * dh * 4);
   w.total = o + 256;     // slack for aligning the caller's base
   return w;
 }
@@ -347,7 +349,8 @@ int lssab8_quant_blocks(const void* x, int dtype, int B, int KVH, int T, int dh,
 
 int lssab8_prefill_lattice(const int8_t* q8, const int32_t* eq, const int8_t* k8, const int32_t* ek,
                            const int8_t* v8, const int32_t* ev, const int32_t* ev0, int B, int H, int KVH, int T,
-                           int dh, int Tpad, void* out, int out_dtype, const int64_t* os, void* stream) {
+                           int dh, int Tpad, float* orow_scratch, void* out, int out_dtype, const int64_t* os,
+                           void* stream) {
   if (!q8 || !eq || !k8 || !ek || !v8 || !ev || !out || !shape_ok(B, H, KVH, T, dh) || Tpad != tpad_of(T) ||
       !strides_ok(os, 4))
     return kErrArg;
@@ -363,6 +366,7 @@ int lssab8_prefill_lattice(const int8_t* q8, const int32_t* eq, const int8_t* k8
   a.B = B; a.H = H; a.KVH = KVH; a.T = T; a.dh = dh; a.Tpad = Tpad; a.nblk = Tpad / 128; a.group = H / KVH;
   a.eq = eq; a.ek = ek; a.ev = ev; a.ev0 = ev0; a.v8 = v8;
   a.out = out; a.os0 = os[0]; a.os1 = os[1]; a.os2 = os[2]; a.os3 = os[3]; a.out_dtype = out_dtype;
+  a.orow = orow_scratch;
   a.gbase = gbase_of(dh);
   a.err = ds->err;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -399,8 +403,9 @@ int lssab8_prefill(const void* q, const void* k, const void* v, int dtype, int B
   if ((rc = lssab8_quant_blocks(k, dtype, B, KVH, T, dh, ks, Tpad, 0, k8, ek, nullptr, stream))) return rc;
   const int vmode = sink ? (T > 1 ? 2 : 1) : 0;
   if ((rc = lssab8_quant_blocks(v, dtype, B, KVH, T, dh, vs, Tpad, vmode, v8, ev, ev0, stream))) return rc;
-  return lssab8_prefill_lattice(q8, eq, k8, ek, v8, ev, (sink && T > 1) ? ev0 : nullptr, B, H, KVH, T, dh, Tpad, out,
-                                out_dtype, os, stream);
+  float* orow = (Tpad / 128 > kSEG) ? reinterpret_cast<float*>(base + w.orow) : nullptr;
+  return lssab8_prefill_lattice(q8, eq, k8, ek, v8, ev, (sink && T > 1) ? ev0 : nullptr, B, H, KVH, T, dh, Tpad,
+                                orow, out, out_dtype, os, stream);
 }
 
 int lssab8_decode_prep_kv(const void* k, const void* v, int dtype, int B, int KVH, int dh, const int32_t* seq_lens,

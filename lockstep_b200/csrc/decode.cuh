@@ -17,8 +17,7 @@
 // (sequence, kv head) to finish (an atomic ticket, no waiting) refolds all blocks in ascending
 // order with the two-level committed-order fold and writes the output rows.
 #pragma once
-#include "common.cuh"
-#include "prefill.cuh"   // PTX wrappers, T2 table
+#include "tcgen05.cuh"
 
 namespace lssab8 {
 
@@ -44,11 +43,6 @@ struct DecodeArgs {
   uint32_t gbase;
   int* err;
 };
-
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-               ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar)) : "memory");
-}
 
 __device__ __forceinline__ uint32_t dp4a_us(uint32_t a_u8x4, uint32_t b_s8x4, uint32_t c) {
   uint32_t d;

@@ -10,15 +10,23 @@
 //                 S_b  = Q8 . K8_b^T   tcgen05.mma kind::i8, s8 x s8 -> s32, M=128 N=128 K=dh
 //                 A_b  = P_b . V8_b    tcgen05.mma kind::i8, u8 x s8 -> s32, M=128 N=dh K=128
 //               S and A are double-buffered in TMEM (4 x 128 columns = all 512).
-//   warps 2-5   "chain" warps, one query row per thread (TMEM lane = row): block max of S,
-//               G, NB, the 32-bit chain d = NB - max(S, m - dm) * G (mod 2^32), the T2 gather
-//               from an 8 KB zero-padded shared table, l_b = sum eh, and the u8 P row written
-//               to shared memory in the SW128 K-major layout the PV MMA reads.
-//   warps 6-13  "fold" warps, two threads per row (each owns dh/2 channels): the
-//               committed-order binary32 fold of (NB_b, l_b, A_b) into O (registers), the
-//               segment -> row fold at 32-block boundaries (O_row in shared memory when a row
-//               spans > 1 segment), and the epilogue fl(O / l) -> output dtype.  Both threads
-//               of a row run the same scalar recurrence on (NB, l) and disjoint channels.
+//   warps 2-9   "chain" warps, two threads per query row (TMEM lane = row, 64 keys each):
+//               exact block max (the two halves meet through shared memory and a named
+//               barrier), G, NB, the 32-bit chain d = NB - max(S, m - dm) * G (mod 2^32), the T2
+//               gather from a lane-replicated shared table (at most 2-way bank conflicts),
+//               l_b = sum eh, and the u8 P half-row written in the SW128 K-major layout the
+//               PV MMA reads.
+//   warps 10..  "fold" warps, dh/32 threads per row (each owns 32 channels): the
+//               committed-order binary32 fold of (NB_b, l_b, A_b) into O (registers, paired
+//               f32x2 arithmetic), the segment -> row fold at 32-block boundaries (O_row in a
+//               workspace buffer when a row spans > 1 segment), and the epilogue
+//               fl(O / l) -> output dtype.  The threads of a row run the same scalar
+//               recurrence on (NB, l) over disjoint channels.
+//
+// The A accumulators are pre-loaded with the bit pattern 0x4B400000 (the float 1.5 * 2^23) and
+// the PV MMA accumulates onto it, so a fold thread reads 1.5 * 2^23 + A_b as a float: one
+// subtraction recovers A_b exactly (|A_b| < 2^22) and one fused multiply-add folds it (exact
+// product, one rounding).  The fold thread writes the bias back after reading.
 //
 // Exactness: S and A_b are exact integer sums (any MMA order); everything after them is the
 // contract's integer chain and a fixed sequence of RN binary32 operations per row
@@ -26,8 +34,7 @@
 // (reference/lssab9_torch.py:276-304): key 0's weight is removed from block 0's P operand
 // (l_b keeps it) and its product eh0 * v8[0] is folded first with e_v0.
 #pragma once
-#include <cuda.h>
-#include "common.cuh"
+#include "tcgen05.cuh"
 
 namespace lssab8 {
 
@@ -41,75 +48,23 @@ struct PrefillArgs {
   void* out;            // output, element strides below
   long long os0, os1, os2, os3;   // out[b, t, h, c]
   int out_dtype;
+  float* orow;          // [B, H, Tpad, dh] f32: O_row of rows spanning > 1 segment (else unused)
   uint32_t gbase;
   int* err;
 };
 
-// -------------------------------------------------------------------------- PTX wrappers
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, int x, int y, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
-      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(smem_u32(bar))
-      : "memory");
-}
-
-// UMMA shared-memory descriptor (sm_100 layout: start>>4 [0,14), LBO>>4 [16,30), SBO>>4 [32,46),
-// version 1 at bit 46, swizzle mode [61,64): 2 = 128B, 4 = 64B).
-__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo, uint32_t swz) {
-  return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
-         ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | ((uint64_t)swz << 61);
-}
-
-// Instruction descriptor, kind::i8: D s32 (bits 4-5 = 2), A/B format 1 = s8, 0 = u8
-// (bits 7-9, 10-12), A/B major 0 = K, 1 = MN (bits 15, 16), N>>3 (bits 17-22), M>>4 (24-28).
-__host__ __device__ constexpr uint32_t idesc_i8(int a_signed, int b_signed, int b_mn_major, int M, int N) {
-  return (2u << 4) | ((uint32_t)a_signed << 7) | ((uint32_t)b_signed << 10) | ((uint32_t)b_mn_major << 16) |
-         ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
-}
-
-__device__ __forceinline__ void umma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}\n"
-      ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc) : "memory");
-}
-
-__device__ __forceinline__ void umma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
-               ::"r"(smem_u32(bar)) : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-
-// 32 lanes x 32 consecutive 32-bit columns: thread i of the warp receives lane (base lane + i).
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
-      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-}
-
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-}
-
-__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
-  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
-}
-
-__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-
 // ------------------------------------------------------------------------ smem layout
+constexpr int kTabCopies = 16;                                // T2 copies, one per lane of a half-warp
+constexpr int kTabEntries = kTabLive + 1;                     // index 1152 (T2 = 0) absorbs clamped d
+constexpr uint32_t kDClamp = (uint32_t)kTabLive << kIdxShift; // min(d, 1152 << 19) -> index <= 1152
+constexpr uint32_t kMagicBits = 0x4B400000u;                  // 1.5 * 2^23
+// warps: 0 TMA, 1 MMA, 2-9 chain (2 per row), then dh/32 fold warps per row quarter (32 channels each)
+template <int DH> struct PrefillShape {
+  static constexpr int kFoldSplit = DH / 32;                // fold threads per row
+  static constexpr int kFoldWarps = 4 * kFoldSplit;
+  static constexpr int kThreads = 32 * (10 + kFoldWarps);   // 832 at dh 128, 576 at dh 64
+};
+
 template <int DH>
 struct PrefillSmem {
   static constexpr int kTile = 128 * DH;                 // one Q/K/V tile, bytes
@@ -117,19 +72,13 @@ struct PrefillSmem {
   static constexpr int kK = kTile;                       // 2 stages
   static constexpr int kV = 3 * kTile;                   // 2 stages
   static constexpr int kP = 5 * kTile;                   // 2 x 16 KB, SW128 K-major u8
-  static constexpr int kTab = kP + 2 * 16384;            // 8 KB zero-padded T2
-  static constexpr int kInfo = kTab + kTabPad;           // 2 x 128 x int4
-  static constexpr int kV0 = kInfo + 2 * 128 * 16;       // key 0's int8 value row (sink)
+  static constexpr int kTab = kP + 2 * 16384;            // 1153 entries x 16 copies x u32
+  static constexpr int kInfo = kTab + kTabEntries * kTabCopies * 4;   // 2 x 128 x {nb, lb0, eh0, lb1}
+  static constexpr int kPmax = kInfo + 2 * 128 * 16;     // 2 parities x 2 halves x 128 rows
+  static constexpr int kV0 = kPmax + 2 * 2 * 128 * 4;    // key 0's int8 value row (sink)
   static constexpr int kBar = kV0 + 256;                 // mbarriers
-  static constexpr int kNumBars = 25;
   static constexpr int kMisc = kBar + 256;               // tmem base, abort flag
-  static constexpr int kORow = kMisc + 64;               // [DH][128] f32 (multi-segment rows)
-  static constexpr int kBytesSingle = kORow;
-  static constexpr int kBytesMulti = kORow + DH * 128 * 4;
-};
-
-__device__ const uint8_t kT2Live[kTabLive] = {
-#include "t2_table.inc"
+  static constexpr int kBytes = kMisc + 64;
 };
 
 enum BarId : int {
@@ -137,21 +86,40 @@ enum BarId : int {
   kBarPFull = 13, kBarPEmpty = 15, kBarAFull = 17, kBarAEmpty = 19, kBarIFull = 21, kBarIEmpty = 23
 };
 
+// store one output row slice of n channels (n a multiple of 8), vectorised when contiguous
+template <typename OutT, int N>
+__device__ __forceinline__ void store_row(OutT* dst, long long os3, const float* y) {
+  if (os3 == 1 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+    constexpr int kPer = 16 / sizeof(OutT);
+#pragma unroll
+    for (int c = 0; c < N; c += kPer) {
+      union { uint4 u; OutT e[kPer]; } pk;
+#pragma unroll
+      for (int t = 0; t < kPer; ++t) pk.e[t] = from_f32<OutT>(y[c + t]);
+      *reinterpret_cast<uint4*>(dst + c) = pk.u;
+    }
+  } else {
+#pragma unroll
+    for (int c = 0; c < N; ++c) dst[c * os3] = from_f32<OutT>(y[c]);
+  }
+}
+
 template <int DH, bool SINK, typename OutT, bool MULTI>
-__global__ void __launch_bounds__(448, 1)
+__global__ void __launch_bounds__(PrefillShape<DH>::kThreads, 1)
 prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                const __grid_constant__ CUtensorMap tm_v, const PrefillArgs p) {
-  constexpr bool multi_seg = MULTI;    // rows spanning more than one 32-block segment
   using L = PrefillSmem<DH>;
+  constexpr int HD = 32;                               // channels per fold thread
+  constexpr int kFoldThreads = 32 * PrefillShape<DH>::kFoldWarps;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);   // 1024-B aligned, still __shared__
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kMisc + 8);
-  uint8_t* tab = smem + L::kTab;
-  int4* info = reinterpret_cast<int4*>(smem + L::kInfo);
+  const uint8_t* tab = smem + L::kTab;
+  int* info = reinterpret_cast<int*>(smem + L::kInfo);
+  int* pmax = reinterpret_cast<int*>(smem + L::kPmax);
   int8_t* v0row = reinterpret_cast<int8_t*>(smem + L::kV0);
-  float* orow = reinterpret_cast<float*>(smem + L::kORow);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ntile = gridDim.x;
@@ -162,18 +130,24 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
   const int qrow0 = (b * p.H + h) * p.Tpad + tile * 128;
   const int krow0 = (b * p.KVH + g) * p.Tpad;
 
-  // ---- setup: table, barriers, TMEM
-  for (int i = threadIdx.x; i < kTabPad; i += blockDim.x) tab[i] = (i < kTabLive) ? kT2Live[i] : 0;
+  // ---- setup: T2 copies, barriers, TMEM
+  {
+    uint32_t* tw = reinterpret_cast<uint32_t*>(smem + L::kTab);
+    for (int i = threadIdx.x; i < kTabEntries * kTabCopies; i += blockDim.x) {
+      const int k = i / kTabCopies;
+      tw[i] = (k < kTabLive) ? (uint32_t)kT2Live[k] : 0u;
+    }
+  }
   if (SINK && threadIdx.x < DH) v0row[threadIdx.x] = p.v8[(long long)krow0 * DH + threadIdx.x];
   if (threadIdx.x == 0) {
     mbar_init(&bars[kBarQ], 1);
     for (int s = 0; s < 2; ++s) {
-      mbar_init(&bars[kBarKFull + s], 1);  mbar_init(&bars[kBarKEmpty + s], 1);
-      mbar_init(&bars[kBarVFull + s], 1);  mbar_init(&bars[kBarVEmpty + s], 1);
-      mbar_init(&bars[kBarSFull + s], 1);  mbar_init(&bars[kBarSEmpty + s], 128);
-      mbar_init(&bars[kBarPFull + s], 128); mbar_init(&bars[kBarPEmpty + s], 1);
-      mbar_init(&bars[kBarAFull + s], 1);  mbar_init(&bars[kBarAEmpty + s], 256);
-      mbar_init(&bars[kBarIFull + s], 128); mbar_init(&bars[kBarIEmpty + s], 256);
+      mbar_init(&bars[kBarKFull + s], 1);   mbar_init(&bars[kBarKEmpty + s], 1);
+      mbar_init(&bars[kBarVFull + s], 1);   mbar_init(&bars[kBarVEmpty + s], 1);
+      mbar_init(&bars[kBarSFull + s], 1);   mbar_init(&bars[kBarSEmpty + s], 256);
+      mbar_init(&bars[kBarPFull + s], 256); mbar_init(&bars[kBarPEmpty + s], 1);
+      mbar_init(&bars[kBarAFull + s], 1);   mbar_init(&bars[kBarAEmpty + s], kFoldThreads);
+      mbar_init(&bars[kBarIFull + s], 256); mbar_init(&bars[kBarIEmpty + s], kFoldThreads);
     }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -182,13 +156,21 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(tmem_slot)) : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
-  if constexpr (MULTI) {
-    for (int i = threadIdx.x; i < DH * 128; i += blockDim.x) orow[i] = 0.0f;
-  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  if (warp >= 10) {                                  // fold warps: bias both A accumulators
+    const uint32_t ab = tmem + ((uint32_t)((warp & 3) * 32) << 16) + 256 + ((warp - 10) >> 2) * HD;   // (fold warps)
+#pragma unroll
+    for (int s = 0; s < 2; ++s)
+#pragma unroll
+      for (int cc = 0; cc < HD / 16; ++cc) tmem_fill16(ab + s * 128 + cc * 16, kMagicBits);
+    tc_wait_st();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
 
   if (warp == 0) {
     // ================================================================ TMA producer
@@ -245,20 +227,23 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
           // A = P (K-major SW128, 32 keys = 32 bytes per step); B = V (MN-major: 32 keys =
-          // 4 groups of 8 rows per step; LBO = MN-atom stride (one atom), SBO = 8-row stride)
+          // 4 groups of 8 rows per step; LBO = MN-atom stride (one atom), SBO = 8-row stride).
+          // Every step accumulates: the accumulator starts at the 1.5 * 2^23 bias.
           umma_i8(tmem + 256 + s * 128, umma_desc(sp + kk * 32, 16, 1024, 2),
-                  umma_desc(sv + kk * 32 * DH, L::kTile, kRowGroup, kSwz), idesc_pv, kk > 0);
+                  umma_desc(sv + kk * 32 * DH, L::kTile, kRowGroup, kSwz), idesc_pv, 1u);
         }
         umma_commit(&bars[kBarAFull + s]);
         umma_commit(&bars[kBarVEmpty + s]);
         umma_commit(&bars[kBarPEmpty + s]);
       }
     }
-  } else if (warp < 6) {
+  } else if (warp < 10) {
     // ================================================================ chain warps
     const int q4 = warp & 3;
+    const int kh = (warp - 2) >> 2;                    // key half: keys [64 kh, 64 kh + 64)
     const int r = q4 * 32 + lane;
     const uint32_t lanebase = (uint32_t)(q4 * 32) << 16;
+    const uint32_t lane4 = (uint32_t)(lane & 15) << 2;
     const int eqr = p.eq[(long long)qrow0 + r];
     const int32_t* ekg = p.ek + (long long)(b * p.KVH + g) * p.nblk;
     const uint32_t prow = (uint32_t)((r >> 3) * 1024 + (r & 7) * 128);
@@ -268,21 +253,26 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
       if (!mbar_wait_warp(&bars[kBarSFull + s], ph, abort_flag, p.err)) break;
       tc_fence_after();
       const bool diag = (j == tile);                     // key c of the diagonal block visible iff c <= r
-      const uint32_t sbase = tmem + lanebase + s * 128;
-      // pass 1: exact block max over the visible keys (32 TMEM columns at a time)
+      const uint32_t sbase = tmem + lanebase + s * 128 + kh * 64;
+      // pass 1: exact max over this thread's visible keys, then over the row
       int m = INT32_MIN;
 #pragma unroll 1
       for (int cc = 0; cc < 4; ++cc) {
-        uint32_t v[32];
-        tmem_ld32(sbase + cc * 32, v);
+        uint32_t v[16];
+        tmem_ld16(sbase + cc * 16, v);
         tc_wait_ld();
+        if (diag) {
 #pragma unroll
-        for (int c = 0; c < 32; ++c) if (diag && cc * 32 + c > r) v[c] = 0x80000000u;
-        int m2 = (int)v[0];
+          for (int c = 0; c < 16; ++c) if (kh * 64 + cc * 16 + c > r) v[c] = 0x80000000u;
+        }
+        int m2 = __vimax3_s32((int)v[0], (int)v[1], (int)v[2]);
 #pragma unroll
-        for (int c = 1; c < 31; c += 2) m2 = __vimax3_s32(m2, (int)v[c], (int)v[c + 1]);
-        m = __vimax3_s32(m, m2, (int)v[31]);
+        for (int c = 3; c < 15; c += 2) m2 = __vimax3_s32(m2, (int)v[c], (int)v[c + 1]);
+        m = __vimax3_s32(m, m2, (int)v[15]);
       }
+      pmax[(s * 2 + kh) * 128 + r] = m;
+      named_bar_sync(1, 256);
+      m = max(pmax[(s * 2) * 128 + r], pmax[(s * 2 + 1) * 128 + r]);
       const uint32_t G = g_fold(p.gbase, eqr + ekg[j]);
       const int nbv = nb_of(m, G);
       const uint32_t NBlo = (uint32_t)nbv << kBHI;
@@ -293,63 +283,66 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
       if (!mbar_wait_warp(&bars[kBarPEmpty + s], ph ^ 1, abort_flag, p.err)) break;
       const uint32_t pbase = smem_u32(smem + L::kP + s * 16384) + prow;
       uint32_t lb = 0, eh0 = 0;
-      // pass 2: the chain and the u8 P row (two 16-key chunks per 32 columns)
+      // pass 2: the chain and the u8 P half-row (one 16-key chunk per 16 columns)
 #pragma unroll 1
       for (int cc = 0; cc < 4; ++cc) {
-        uint32_t v[32];
-        tmem_ld32(sbase + cc * 32, v);
+        uint32_t v[16];
+        tmem_ld16(sbase + cc * 16, v);
         tc_wait_ld();
+        if (diag) {
 #pragma unroll
-        for (int c = 0; c < 32; ++c) if (diag && cc * 32 + c > r) v[c] = 0x80000000u;
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          uint32_t w[4];
-#pragma unroll
-          for (int qq = 0; qq < 4; ++qq) {
-            uint32_t acc = 0;
-#pragma unroll
-            for (int x = 0; x < 4; ++x) {
-              const int sc = max((int)v[half * 16 + qq * 4 + x], lo);
-              const uint32_t d = NBlo + (uint32_t)sc * negG;   // exact: d < 2^32
-              acc |= (uint32_t)tab[d >> kIdxShift] << (8 * x);
-            }
-            w[qq] = acc;
-            lb = __dp4a(acc, 0x01010101u, lb);
-          }
-          const int chunk = cc * 2 + half;
-          if (SINK && chunk == 0 && j == 0 && p.T > 1) { eh0 = w[0] & 0xFFu; w[0] &= ~0xFFu; }
-          st_shared_v4(pbase + (uint32_t)((chunk ^ (r & 7)) << 4), w[0], w[1], w[2], w[3]);
+          for (int c = 0; c < 16; ++c) if (kh * 64 + cc * 16 + c > r) v[c] = 0x80000000u;
         }
+        uint32_t w[4];
+#pragma unroll
+        for (int qq = 0; qq < 4; ++qq) {
+          uint32_t e[4];
+#pragma unroll
+          for (int x = 0; x < 4; ++x) {
+            const int sc = max((int)v[qq * 4 + x], lo);
+            uint32_t d = NBlo + (uint32_t)sc * negG;       // exact: d < 2^32
+            d = min(d, kDClamp);                           // index <= 1152 (T2 = 0 from 1152 on)
+            e[x] = tab[((d >> (kIdxShift - 6)) & ~63u) | lane4];
+          }
+          w[qq] = __byte_perm(__byte_perm(e[0], e[1], 0x0040), __byte_perm(e[2], e[3], 0x0040), 0x5410);
+          lb = __dp4a(w[qq], 0x01010101u, lb);
+        }
+        const int chunk = kh * 4 + cc;
+        if (SINK && chunk == 0 && j == 0 && p.T > 1) { eh0 = w[0] & 0xFFu; w[0] &= ~0xFFu; }
+        st_shared_v4(pbase + (uint32_t)((chunk ^ (r & 7)) << 4), w[0], w[1], w[2], w[3]);
       }
       tc_fence_before();
       mbar_arrive(&bars[kBarSEmpty + s]);
       fence_async_smem();
       mbar_arrive(&bars[kBarPFull + s]);
       if (!mbar_wait_warp(&bars[kBarIEmpty + s], ph ^ 1, abort_flag, p.err)) break;
-      info[s * 128 + r] = make_int4(nbv, (int)lb, (int)eh0, 0);
+      int* slot = info + (s * 128 + r) * 4;
+      if (kh == 0) { slot[0] = nbv; slot[1] = (int)lb; slot[2] = (int)eh0; }
+      else { slot[3] = (int)lb; }
       mbar_arrive(&bars[kBarIFull + s]);
     }
   } else {
     // ================================================================ fold warps
-    constexpr int HD = DH / 2;                        // channels owned by this thread
     const int q4 = warp & 3;
     const int r = q4 * 32 + lane;
-    const int c0 = (warp >= 10) ? HD : 0;
+    const int c0 = ((warp - 10) >> 2) * HD;            // this thread's 32 channels
     const uint32_t lanebase = (uint32_t)(q4 * 32) << 16;
     const int32_t* evg = p.ev + (long long)(b * p.KVH + g) * p.nblk;
     const int ev0 = SINK ? p.ev0[b * p.KVH + g] : 0;
-    float O[HD];
+    uint64_t O2[HD / 2];                               // O as binary32 pairs
 #pragma unroll
-    for (int c = 0; c < HD; ++c) O[c] = 0.0f;
+    for (int c = 0; c < HD / 2; ++c) O2[c] = 0ull;
+    const uint64_t negM2 = f2_pack(-12582912.0f, -12582912.0f);
     float lseg = 0.0f, lrow = 0.0f;
     int nbrun = 0, nbrow = 0;
     bool have_seg = false, have_row = false;
     bool ok = true;
+    float* orow = MULTI ? p.orow + ((long long)qrow0 + r) * DH + c0 : nullptr;
     for (int j = 0; j < nb; ++j) {
       const int s = j & 1;
       const uint32_t ph = (j >> 1) & 1;
       if (!mbar_wait_warp(&bars[kBarIFull + s], ph, abort_flag, p.err)) { ok = false; break; }
-      const int4 inf = info[s * 128 + r];
+      const int4 inf = *reinterpret_cast<const int4*>(info + (s * 128 + r) * 4);
       mbar_arrive(&bars[kBarIEmpty + s]);
       const int nbb = inf.x;
       if (!have_seg) { nbrun = nbb; have_seg = true; }
@@ -357,7 +350,11 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
       int sg = 0;
       if (D > 0) {
 #pragma unroll
-        for (int c = 0; c < HD; ++c) O[c] = rescale(O[c], D);
+        for (int c = 0; c < HD / 2; ++c) {
+          float lo_, hi_;
+          f2_unpack(O2[c], lo_, hi_);
+          O2[c] = f2_pack(rescale(lo_, D), rescale(hi_, D));
+        }
         lseg = rescale(lseg, D);
         nbrun = nbb;
       } else {
@@ -365,47 +362,73 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
       }
       if (!mbar_wait_warp(&bars[kBarAFull + s], ph, abort_flag, p.err)) { ok = false; break; }
       tc_fence_after();
+      const uint32_t abase = tmem + lanebase + 256 + s * 128 + c0;
       if (sg <= kSWIN) {
         if (SINK && j == 0 && p.T > 1) {
           const float sc0 = pow2f(-(sg + ev0));
-          const int e0w = inf.z;
 #pragma unroll
-          for (int c = 0; c < HD; ++c) O[c] = fold_term(O[c], e0w * (int)v0row[c0 + c], sc0);
+          for (int c = 0; c < HD / 2; ++c) {
+            float lo_, hi_;
+            f2_unpack(O2[c], lo_, hi_);
+            lo_ = fold_term(lo_, inf.z * (int)v0row[c0 + 2 * c], sc0);
+            hi_ = fold_term(hi_, inf.z * (int)v0row[c0 + 2 * c + 1], sc0);
+            O2[c] = f2_pack(lo_, hi_);
+          }
         }
         const float scO = pow2f(-(sg + evg[j]));
+        const uint64_t scO2 = f2_pack(scO, scO);
 #pragma unroll
-        for (int cc = 0; cc < HD / 16; ++cc) {
-          uint32_t a[16];
-          tmem_ld16(tmem + lanebase + 256 + s * 128 + c0 + cc * 16, a);
+        for (int cc = 0; cc < HD / 8; ++cc) {
+          uint32_t a[8];
+          tmem_ld8(abase + cc * 8, a);
           tc_wait_ld();
 #pragma unroll
-          for (int c = 0; c < 16; ++c) O[cc * 16 + c] = fold_term(O[cc * 16 + c], (int)a[c], scO);
+          for (int t = 0; t < 4; ++t) {
+            const uint64_t x = f2_add(f2_pack(__uint_as_float(a[2 * t]), __uint_as_float(a[2 * t + 1])), negM2);
+            O2[cc * 4 + t] = f2_fma(x, scO2, O2[cc * 4 + t]);
+          }
         }
-        lseg = fold_term(lseg, inf.y, pow2f(-sg));
+#pragma unroll
+        for (int cc = 0; cc < HD / 16; ++cc) tmem_fill16(abase + cc * 16, kMagicBits);   // re-bias for the next PV
+        lseg = fold_term(lseg, inf.y + inf.w, pow2f(-sg));
+      } else {
+#pragma unroll
+        for (int cc = 0; cc < HD / 16; ++cc) tmem_fill16(abase + cc * 16, kMagicBits);
       }
+      tc_wait_st();
       tc_fence_before();
       mbar_arrive(&bars[kBarAEmpty + s]);
-      const bool seg_end = ((j + 1) % kSEG == 0) || (j == nb - 1);
-      if (MULTI && seg_end) {
+      if (MULTI && (((j + 1) % kSEG == 0) || (j == nb - 1))) {
         // segment -> row: the same three rules (reference/lssab8_golden.py:317-331)
-        if (!have_row) { nbrow = nbrun; have_row = true; }
-        const int D2 = nbrun - nbrow;
         int s2 = 0;
-        if (D2 > 0) {
-#pragma unroll 8
-          for (int c = c0; c < c0 + HD; ++c) orow[c * 128 + r] = rescale(orow[c * 128 + r], D2);
-          lrow = rescale(lrow, D2);
-          nbrow = nbrun;
+        if (!have_row) {
+          nbrow = nbrun; have_row = true;
+#pragma unroll
+          for (int c = 0; c < HD / 2; ++c) {
+            float lo_, hi_;
+            f2_unpack(O2[c], lo_, hi_);
+            *reinterpret_cast<float2*>(orow + 2 * c) = make_float2(rescale(lo_, 0), rescale(hi_, 0));
+          }
+          lrow = rescale(lseg, 0);
         } else {
-          s2 = -D2;
+          const int D2 = nbrun - nbrow;
+          if (D2 > 0) { lrow = rescale(lrow, D2); nbrow = nbrun; } else { s2 = -D2; }
+#pragma unroll 4
+          for (int c = 0; c < HD / 2; ++c) {
+            float2 o = *reinterpret_cast<const float2*>(orow + 2 * c);
+            if (D2 > 0) { o.x = rescale(o.x, D2); o.y = rescale(o.y, D2); }
+            if (s2 <= kSWIN) {
+              float lo_, hi_;
+              f2_unpack(O2[c], lo_, hi_);
+              o.x = __fadd_rn(o.x, rescale(lo_, s2));
+              o.y = __fadd_rn(o.y, rescale(hi_, s2));
+            }
+            *reinterpret_cast<float2*>(orow + 2 * c) = o;
+          }
+          if (s2 <= kSWIN) lrow = __fadd_rn(lrow, rescale(lseg, s2));
         }
-        if (s2 <= kSWIN) {
 #pragma unroll
-          for (int c = 0; c < HD; ++c) orow[(c0 + c) * 128 + r] = __fadd_rn(orow[(c0 + c) * 128 + r], rescale(O[c], s2));
-          lrow = __fadd_rn(lrow, rescale(lseg, s2));
-        }
-#pragma unroll
-        for (int c = 0; c < HD; ++c) O[c] = 0.0f;
+        for (int c = 0; c < HD / 2; ++c) O2[c] = 0ull;
         lseg = 0.0f;
         have_seg = false;
       }
@@ -413,19 +436,25 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
     // ---- epilogue: out = O_row / l_row (one RN division), l_row == 0 -> 0
     const int i = tile * 128 + r;
     if (ok && i < p.T) {
+      float y[HD];
       if constexpr (!MULTI) {
-        // a single segment: O_row = 0 + rescale(O_seg, 0), l_row likewise
+        lrow = rescale(lseg, 0);                         // a single segment: O_row = 0 + rescale(O_seg, 0)
 #pragma unroll
-        for (int c = 0; c < HD; ++c) O[c] = rescale(O[c], 0);
-        lrow = rescale(lseg, 0);
+        for (int c = 0; c < HD / 2; ++c) {
+          float lo_, hi_;
+          f2_unpack(O2[c], lo_, hi_);
+          y[2 * c] = rescale(lo_, 0);
+          y[2 * c + 1] = rescale(hi_, 0);
+        }
       } else {
 #pragma unroll
-        for (int c = 0; c < HD; ++c) O[c] = orow[(c0 + c) * 128 + r];
+        for (int c = 0; c < HD; ++c) y[c] = orow[c];
       }
-      OutT* dst = reinterpret_cast<OutT*>(p.out) + b * p.os0 + (long long)i * p.os1 + h * p.os2 + c0 * p.os3;
       const bool nz = (lrow != 0.0f);
 #pragma unroll
-      for (int c = 0; c < HD; ++c) dst[c * p.os3] = from_f32<OutT>(nz ? __fdiv_rn(O[c], lrow) : 0.0f);
+      for (int c = 0; c < HD; ++c) y[c] = nz ? __fdiv_rn(y[c], lrow) : 0.0f;
+      OutT* dst = reinterpret_cast<OutT*>(p.out) + b * p.os0 + (long long)i * p.os1 + h * p.os2 + c0 * p.os3;
+      store_row<OutT, HD>(dst, p.os3, y);
     }
   }
 
