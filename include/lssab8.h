@@ -149,6 +149,13 @@ int lssab8_decode_noalloc(const void* q, int dtype, const int64_t* qs, int B, in
                           const int32_t* ev0, int max_blocks, int split_blocks, int sink, void* out, int out_dtype,
                           const int64_t* os, void* stream);
 
+/* ------------------------------------------------------------------------- self-test */
+
+/* Test support, no counterpart in the reference: out[i] = the prefill epilogue's division of
+ * y[i] by l[i] (l[i] != 0), i.e. the correctly rounded binary32 quotient the contract's
+ * fl(O / l) names (reference/lssab8_golden.py:333).  Device pointers, n elements. */
+int lssab8_selftest_div(const float* y, const float* l, long long n, float* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

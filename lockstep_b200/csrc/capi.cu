@@ -8,6 +8,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdio>
+#include <algorithm>
 #include <cstring>
 #include <mutex>
 
@@ -173,13 +174,14 @@ int launch_prefill_t(const CUtensorMap& tq, const CUtensorMap& tk, const CUtenso
   using L = PrefillSmem<DH>;
   const int multi = a.nblk > kSEG;
   if (multi && !a.orow) return kErrWorkspace;
-  // at least ~116 KB so only one CTA (and one 512-column TMEM allocation) lands on an SM
-  int smem = L::kBytes + 1024;
+  // the T2 copies, the aligned tiles; at least ~116 KB so only one CTA (and one 512-column TMEM
+  // allocation) lands on an SM
+  int smem = kTabBytes + 1024 + L::kBytes;
   if (smem < 116 * 1024) smem = 116 * 1024;
   auto kfn = multi ? prefill_kernel<DH, SINK, OutT, true> : prefill_kernel<DH, SINK, OutT, false>;
   if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return kErrCuda;
   dim3 grid(a.Tpad / 128, a.H, a.B);
-  kfn<<<grid, PrefillShape<DH>::kThreads, smem, st>>>(tq, tk, tv, a);
+  kfn<<<grid, kPrefillThreads, smem, st>>>(tq, tk, tv, a);
   return launch_rc();
 }
 
@@ -213,6 +215,15 @@ int launch_decode_out(int out_dtype, const DecodeArgs& a, int max_splits, cudaSt
     case kBF16: return launch_decode_t<DH, SINK, __nv_bfloat16>(a, max_splits, st);
     default: return kErrArg;
   }
+}
+
+// the vectorised quantisers need a contiguous channel dim, dh in {64, 128} and 16-byte aligned
+// rows (base and every stride a multiple of 16 bytes)
+template <typename InT>
+bool vec_ok(const void* x, const Strides4& s, int dh) {
+  const long long e = (long long)sizeof(InT);
+  return (dh == 64 || dh == 128) && s.s3 == 1 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+         (s.s0 * e) % 16 == 0 && (s.s1 * e) % 16 == 0 && (s.s2 * e) % 16 == 0;
 }
 
 bool strides_ok(const int64_t* s, int n) {
@@ -265,6 +276,14 @@ bool shape_ok(int B, int H, int KVH, int T, int dh) {
 }
 
 }  // namespace
+
+// the prefill epilogue's division (div_rn_shared with the row reciprocal), one element per thread
+__global__ void selftest_div_kernel(const float* y, const float* l, long long n, float* out) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const float li = l[i];
+    out[i] = div_rn_shared(y[i], li, __frcp_rn(li));
+  }
+}
 
 // ========================================================================== extern "C"
 extern "C" {
@@ -319,10 +338,18 @@ int lssab8_quant_rows(const void* x, int dtype, int B, int H, int T, int dh, con
   if (!x || !q8 || !eq || !shape_ok(B, H, H, T, dh) || Tpad < T || !strides_ok(xs, 4)) return kErrArg;
   Strides4 s{xs[0], xs[1], xs[2], xs[3]};
   const long long rows = (long long)B * H * Tpad;
-  const int grid = (int)((rows + 7) / 8);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   return with_in_dtype(dtype, [&](auto tag) {
     using InT = std::remove_const_t<std::remove_pointer_t<decltype(tag)>>;
+    if (vec_ok<InT>(x, s, dh)) {
+      constexpr int N = Vec16<InT>::kN;
+      const int rpw = 32 / (dh / N);
+      const int grid = (int)((rows + 8LL * rpw - 1) / (8LL * rpw));
+      if (dh == 128) quant_rows_vec_kernel<InT, 128><<<grid, 256, 0, st>>>(static_cast<const InT*>(x), s, B, H, T, Tpad, q8, eq);
+      else quant_rows_vec_kernel<InT, 64><<<grid, 256, 0, st>>>(static_cast<const InT*>(x), s, B, H, T, Tpad, q8, eq);
+      return launch_rc();
+    }
+    const int grid = (int)((rows + 7) / 8);
     quant_rows_kernel<InT><<<grid, 256, 0, st>>>(static_cast<const InT*>(x), s, B, H, T, dh, Tpad, q8, eq);
     return launch_rc();
   });
@@ -341,6 +368,15 @@ int lssab8_quant_blocks(const void* x, int dtype, int B, int KVH, int T, int dh,
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   return with_in_dtype(dtype, [&](auto tag) {
     using InT = std::remove_const_t<std::remove_pointer_t<decltype(tag)>>;
+    if (vec_ok<InT>(x, s, dh) && Tpad == tpad_of(T)) {
+      if (dh == 128)
+        quant_blocks_vec_kernel<InT, 128><<<grid, 256, 0, st>>>(static_cast<const InT*>(x), s, B, KVH, T, Tpad, mode, x8, e,
+                                                                e0, ds->err);
+      else
+        quant_blocks_vec_kernel<InT, 64><<<grid, 256, 0, st>>>(static_cast<const InT*>(x), s, B, KVH, T, Tpad, mode, x8, e,
+                                                               e0, ds->err);
+      return launch_rc();
+    }
     quant_blocks_kernel<InT><<<grid, 256, 0, st>>>(static_cast<const InT*>(x), s, B, KVH, T, dh, Tpad, mode, x8, e, e0,
                                                    ds->err);
     return launch_rc();
@@ -539,6 +575,14 @@ int lssab8_decode_noalloc(const void* q, int dtype, const int64_t* qs, int B, in
                              : launch_decode_out<128, false>(out_dtype, a, max_splits, s);
   return sink ? launch_decode_out<64, true>(out_dtype, a, max_splits, s)
               : launch_decode_out<64, false>(out_dtype, a, max_splits, s);
+}
+
+int lssab8_selftest_div(const float* y, const float* l, long long n, float* out, void* stream) {
+  if (!y || !l || !out || n < 0) return kErrArg;
+  if (n == 0) return kOk;
+  const int blocks = (int)std::min<long long>((n + 255) / 256, 148LL * 16);
+  selftest_div_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(y, l, n, out);
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
 
 }  // extern "C"

@@ -115,6 +115,28 @@ __device__ __forceinline__ float fold_term(float O, int A, float sc) {
   return __fmaf_rn(i2f_small(A), sc, O);
 }
 
+// RN(y / l) for many y sharing one divisor l, given rl = RN(1 / l) (__frcp_rn, once per row).
+// Markstein's method (P. W. Markstein, "Computation of elementary functions on the IBM RISC
+// System/6000 processor", IBM J. Res. Dev. 34(1), 1990): q0 = RN(y * rl) lies within 1.5 ulp of
+// y / l; one correction q1 = RN(q0 + RN(y - l * q0) * rl) lies within 1 ulp; then the remainder
+// r = y - l * q1 is exact in one fused multiply-add and RN(q1 + r * rl) is the correctly
+// rounded quotient (Markstein's theorem: rl correctly rounded, q1 within 1 ulp).  The argument
+// needs no underflow or overflow in any step, so it is used only for |y|, |l| in
+// [2^-31, 2^32) (quotient and remainder far inside the normal range); any other operand
+// (zero, subnormal, tiny or huge) takes the IEEE division __fdiv_rn.
+__device__ __forceinline__ bool div_window(float x) {
+  return ((__float_as_uint(x) >> 23) & 0xFFu) - 96u <= 62u;   // biased exponent in [96, 158]
+}
+__device__ __noinline__ float div_rn_ieee(float y, float l) { return __fdiv_rn(y, l); }
+__device__ __forceinline__ float div_rn_shared(float y, float l, float rl) {
+  if (div_window(y) && div_window(l)) {
+    const float q0 = __fmul_rn(y, rl);
+    const float q1 = __fmaf_rn(__fmaf_rn(-q0, l, y), rl, q0);
+    return __fmaf_rn(__fmaf_rn(-q1, l, y), rl, q1);
+  }
+  return div_rn_ieee(y, l);                 // rare: kept out of line
+}
+
 // least multiple of 2^26 >= m*G, returned as NB / 2^26 (|NB| < 2^52, so it fits in int32).
 __device__ __forceinline__ int nb_of(int m, uint32_t G) {
   long long sg = (long long)m * (long long)G;
@@ -164,11 +186,19 @@ __device__ __forceinline__ bool mbar_try_suspend(uint64_t* bar, uint32_t parity)
 // Bounded wait on an mbarrier phase.  Gives up after ~2 s of wall time or as soon as another
 // role of the CTA has raised *abort; on giving up it records kDevTimeout in *err and returns
 // false so the caller can unwind without hanging the GPU.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int* err) {
+// sleep_ns > 0 parks the thread between polls: roles that are not on the critical path (the
+// fold warps, the MMA and TMA threads) must not steal issue slots from the warps that are.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int* err,
+                                          uint32_t sleep_ns = 0) {
   if (mbar_try(bar, parity)) return true;
   uint64_t t0 = globaltimer();
   for (uint32_t it = 0;; ++it) {
-    if (mbar_try_suspend(bar, parity)) return true;
+    if (sleep_ns) {
+      __nanosleep(sleep_ns);
+      if (mbar_try(bar, parity)) return true;
+    } else if (mbar_try_suspend(bar, parity)) {
+      return true;
+    }
     if ((it & 15u) == 15u) {
       if (*abort) return false;
       if (globaltimer() - t0 > 2000000000ull) {
@@ -180,13 +210,63 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile("{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+               : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+  return ok != 0;
+}
+
+// Non-blocking poll of an mbarrier phase (no hardware suspension: arrivals made by
+// tcgen05.commit are observed as soon as they land).  Same bounds as mbar_wait.
+__device__ __forceinline__ bool mbar_poll(uint64_t* bar, uint32_t parity, volatile int* abort, int* err) {
+  if (mbar_test(bar, parity)) return true;
+  uint64_t t0 = globaltimer();
+  for (uint32_t it = 0;; ++it) {
+    if (mbar_test(bar, parity)) return true;
+    if ((it & 1023u) == 1023u) {
+      if (*abort) return false;
+      if (globaltimer() - t0 > 2000000000ull) {
+        *abort = 1;
+        if (err) atomicOr(err, kDevTimeout);
+        return false;
+      }
+    }
+  }
+}
+
+// Named barrier with an OR-reduction: every participant gets the same answer, so a group can
+// decide to unwind together (no participant can leave while others wait at a barrier).
+__device__ __forceinline__ bool bar_any(int bar_id, int nthreads, bool pred) {
+  uint32_t r;
+  asm volatile("{\n .reg .pred p, q;\n setp.ne.u32 q, %1, 0;\n barrier.cta.red.or.pred p, %2, %3, q;\n"
+               " selp.u32 %0, 1, 0, p;\n}"
+               : "=r"(r) : "r"((uint32_t)pred), "r"(bar_id), "r"(nthreads) : "memory");
+  return r != 0;
+}
+
+// Group wait: thread `leader` of a group of `nthreads` (whole warps) polls the phase, then the
+// group meets at named barrier `bar_id`, so only one thread spins while the others are parked.
+// The barrier's OR-reduction makes the give-up decision identical for every member; on success
+// each member re-tests the completed phase (it cannot be reused before this group releases it)
+// for its own acquire ordering.
+__device__ __forceinline__ bool group_wait(uint64_t* bar, uint32_t parity, bool leader, int bar_id, int nthreads,
+                                           volatile int* abort, int* err) {
+  bool fail = false;
+  if (leader) fail = !mbar_poll(bar, parity, abort, err);
+  if (bar_any(bar_id, nthreads, fail || *abort != 0)) return false;
+  (void)mbar_test(bar, parity);
+  return true;
+}
+
 // Warp-uniform form of mbar_wait for warps that next issue .sync.aligned instructions
 // (tcgen05.ld): lane 0 does the bounded wait, the verdict is broadcast, and on success every
 // lane observes the completed phase itself (it cannot advance again before this warp arrives
 // on the matching release barrier), which gives each lane the acquire ordering.
-__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort, int* err) {
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort, int* err,
+                                               uint32_t sleep_ns = 0) {
   int ok = 0;
-  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, abort, err) ? 1 : 0;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, abort, err, sleep_ns) ? 1 : 0;
   ok = __shfl_sync(0xffffffffu, ok, 0);
   if (ok) {
     // completes on the first try by the argument above; bounded all the same

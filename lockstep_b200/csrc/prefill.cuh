@@ -9,24 +9,23 @@
 //   warp 1      TMEM owner and MMA issuer (one thread):
 //                 S_b  = Q8 . K8_b^T   tcgen05.mma kind::i8, s8 x s8 -> s32, M=128 N=128 K=dh
 //                 A_b  = P_b . V8_b    tcgen05.mma kind::i8, u8 x s8 -> s32, M=128 N=dh K=128
-//               S and A are double-buffered in TMEM (4 x 128 columns = all 512).
+//               TMEM columns: S double-buffered [0, 256), A [256, 384), O [384, 512).
 //   warps 2-9   "chain" warps, two threads per query row (TMEM lane = row, 64 keys each):
 //               exact block max (the two halves meet through shared memory and a named
 //               barrier), G, NB, the 32-bit chain d = NB - max(S, m - dm) * G (mod 2^32), the T2
 //               gather from a lane-replicated shared table (at most 2-way bank conflicts),
 //               l_b = sum eh, and the u8 P half-row written in the SW128 K-major layout the
 //               PV MMA reads.
-//   warps 10..  "fold" warps, dh/32 threads per row (each owns 32 channels): the
-//               committed-order binary32 fold of (NB_b, l_b, A_b) into O (registers, paired
-//               f32x2 arithmetic), the segment -> row fold at 32-block boundaries (O_row in a
+//   warps 10-13 "fold" warps, one thread per row: the committed-order binary32 fold of
+//               (NB_b, l_b, A_b) into the row's O, which lives in TMEM (paired f32x2
+//               arithmetic), the segment -> row fold at 32-block boundaries (O_row in a
 //               workspace buffer when a row spans > 1 segment), and the epilogue
-//               fl(O / l) -> output dtype.  The threads of a row run the same scalar
-//               recurrence on (NB, l) over disjoint channels.
+//               fl(O / l) -> output dtype.
 //
-// The A accumulators are pre-loaded with the bit pattern 0x4B400000 (the float 1.5 * 2^23) and
-// the PV MMA accumulates onto it, so a fold thread reads 1.5 * 2^23 + A_b as a float: one
-// subtraction recovers A_b exactly (|A_b| < 2^22) and one fused multiply-add folds it (exact
-// product, one rounding).  The fold thread writes the bias back after reading.
+// The A accumulator is pre-loaded with the bit pattern 0x4B400000 (the float 1.5 * 2^23) and
+// the PV MMA accumulates onto it, so the fold reads 1.5 * 2^23 + A_b as a float: one subtraction
+// recovers A_b exactly (|A_b| < 2^22) and one fused multiply-add folds it (exact product, one
+// rounding).  The fold thread writes the bias back after reading.
 //
 // Exactness: S and A_b are exact integer sums (any MMA order); everything after them is the
 // contract's integer chain and a fixed sequence of RN binary32 operations per row
@@ -37,7 +36,6 @@
 #include "tcgen05.cuh"
 
 namespace lssab8 {
-
 struct PrefillArgs {
   int B, H, KVH, T, dh, Tpad, nblk, group;
   const int32_t* eq;    // [B, H, Tpad]
@@ -58,12 +56,9 @@ constexpr int kTabCopies = 16;                                // T2 copies, one 
 constexpr int kTabEntries = kTabLive + 1;                     // index 1152 (T2 = 0) absorbs clamped d
 constexpr uint32_t kDClamp = (uint32_t)kTabLive << kIdxShift; // min(d, 1152 << 19) -> index <= 1152
 constexpr uint32_t kMagicBits = 0x4B400000u;                  // 1.5 * 2^23
-// warps: 0 TMA, 1 MMA, 2-9 chain (2 per row), then dh/32 fold warps per row quarter (32 channels each)
-template <int DH> struct PrefillShape {
-  static constexpr int kFoldSplit = DH / 32;                // fold threads per row
-  static constexpr int kFoldWarps = 4 * kFoldSplit;
-  static constexpr int kThreads = 32 * (10 + kFoldWarps);   // 832 at dh 128, 576 at dh 64
-};
+constexpr int kPrefillThreads = 448;                          // 14 warps: TMA, MMA, 8 chain, 4 fold
+constexpr int kFoldThreads = 128;
+constexpr int kTabBytes = kTabEntries * kTabCopies * 4;       // 73,792 B at the start of dynamic smem
 
 template <int DH>
 struct PrefillSmem {
@@ -72,25 +67,25 @@ struct PrefillSmem {
   static constexpr int kK = kTile;                       // 2 stages
   static constexpr int kV = 3 * kTile;                   // 2 stages
   static constexpr int kP = 5 * kTile;                   // 2 x 16 KB, SW128 K-major u8
-  static constexpr int kTab = kP + 2 * 16384;            // 1153 entries x 16 copies x u32
-  static constexpr int kInfo = kTab + kTabEntries * kTabCopies * 4;   // 2 x 128 x {nb, lb0, eh0, lb1}
+  static constexpr int kInfo = kP + 2 * 16384;           // 2 x 128 x {nb, lb0, eh0, lb1}
   static constexpr int kPmax = kInfo + 2 * 128 * 16;     // 2 parities x 2 halves x 128 rows
   static constexpr int kV0 = kPmax + 2 * 2 * 128 * 4;    // key 0's int8 value row (sink)
-  static constexpr int kBar = kV0 + 256;                 // mbarriers
+  static constexpr int kLrow = kV0 + 256;                // 128 x l_row (binary32) for the epilogue
+  static constexpr int kBar = kLrow + 512;               // mbarriers
   static constexpr int kMisc = kBar + 256;               // tmem base, abort flag
-  static constexpr int kBytes = kMisc + 64;
+  static constexpr int kBytes = kMisc + 64;              // (+ the static T2 table)
 };
 
 enum BarId : int {
   kBarQ = 0, kBarKFull = 1, kBarKEmpty = 3, kBarVFull = 5, kBarVEmpty = 7, kBarSFull = 9, kBarSEmpty = 11,
-  kBarPFull = 13, kBarPEmpty = 15, kBarAFull = 17, kBarAEmpty = 19, kBarIFull = 21, kBarIEmpty = 23
+  kBarPFull = 13, kBarPEmpty = 15, kBarAFull = 17, kBarAEmpty = 18, kBarIFull = 19, kBarIEmpty = 21
 };
 
-// store one output row slice of n channels (n a multiple of 8), vectorised when contiguous
+// store n consecutive channels, vectorised when contiguous and aligned
 template <typename OutT, int N>
-__device__ __forceinline__ void store_row(OutT* dst, long long os3, const float* y) {
+__device__ __forceinline__ void store_chunk(OutT* dst, long long os3, const float* y) {
+  constexpr int kPer = 16 / sizeof(OutT);
   if (os3 == 1 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
-    constexpr int kPer = 16 / sizeof(OutT);
 #pragma unroll
     for (int c = 0; c < N; c += kPer) {
       union { uint4 u; OutT e[kPer]; } pk;
@@ -105,21 +100,24 @@ __device__ __forceinline__ void store_row(OutT* dst, long long os3, const float*
 }
 
 template <int DH, bool SINK, typename OutT, bool MULTI>
-__global__ void __launch_bounds__(PrefillShape<DH>::kThreads, 1)
+__global__ void __launch_bounds__(kPrefillThreads, 1)
 prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                const __grid_constant__ CUtensorMap tm_v, const PrefillArgs p) {
   using L = PrefillSmem<DH>;
-  constexpr int HD = 32;                               // channels per fold thread
-  constexpr int kFoldThreads = 32 * PrefillShape<DH>::kFoldWarps;
+  // Dynamic shared memory starts with T2 in 16 copies per entry (a half-warp's lanes never
+  // share a bank: entry k of copy c is the 32-bit word k * 16 + c); the start of the window is a
+  // link-time constant, so every gather folds the table base into its immediate offset.  The
+  // 1024-byte aligned tiles follow.
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);   // 1024-B aligned, still __shared__
+  uint32_t* s_t2 = reinterpret_cast<uint32_t*>(smem_raw);
+  uint8_t* smem = smem_raw + kTabBytes + ((1024u - (smem_u32(smem_raw + kTabBytes) & 1023u)) & 1023u);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kMisc + 8);
-  const uint8_t* tab = smem + L::kTab;
   int* info = reinterpret_cast<int*>(smem + L::kInfo);
   int* pmax = reinterpret_cast<int*>(smem + L::kPmax);
   int8_t* v0row = reinterpret_cast<int8_t*>(smem + L::kV0);
+  float* lrow_s = reinterpret_cast<float*>(smem + L::kLrow);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ntile = gridDim.x;
@@ -130,15 +128,9 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
   const int qrow0 = (b * p.H + h) * p.Tpad + tile * 128;
   const int krow0 = (b * p.KVH + g) * p.Tpad;
 
-  // ---- setup: T2 copies, barriers, TMEM
-  {
-    uint32_t* tw = reinterpret_cast<uint32_t*>(smem + L::kTab);
-    for (int i = threadIdx.x; i < kTabEntries * kTabCopies; i += blockDim.x) {
-      const int k = i / kTabCopies;
-      tw[i] = (k < kTabLive) ? (uint32_t)kT2Live[k] : 0u;
-    }
-  }
-  if (SINK && threadIdx.x < DH) v0row[threadIdx.x] = p.v8[(long long)krow0 * DH + threadIdx.x];
+  // ---- setup: barriers and the first loads (thread 0 is the TMA producer, so its loads need
+  // no CTA barrier; they overlap the table fill), then T2 copies and TMEM
+  const int npre = min(nb, 2);                       // stages that start empty
   if (threadIdx.x == 0) {
     mbar_init(&bars[kBarQ], 1);
     for (int s = 0; s < 2; ++s) {
@@ -146,12 +138,28 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
       mbar_init(&bars[kBarVFull + s], 1);   mbar_init(&bars[kBarVEmpty + s], 1);
       mbar_init(&bars[kBarSFull + s], 1);   mbar_init(&bars[kBarSEmpty + s], 256);
       mbar_init(&bars[kBarPFull + s], 256); mbar_init(&bars[kBarPEmpty + s], 1);
-      mbar_init(&bars[kBarAFull + s], 1);   mbar_init(&bars[kBarAEmpty + s], kFoldThreads);
       mbar_init(&bars[kBarIFull + s], 256); mbar_init(&bars[kBarIEmpty + s], kFoldThreads);
     }
+    mbar_init(&bars[kBarAFull], 1);
+    mbar_init(&bars[kBarAEmpty], kFoldThreads);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    mbar_expect_tx(&bars[kBarQ], L::kTile);
+    tma_load_2d(smem + L::kQ, &tm_q, 0, qrow0, &bars[kBarQ]);
+    for (int j = 0; j < npre; ++j) {
+      mbar_expect_tx(&bars[kBarKFull + j], L::kTile);
+      tma_load_2d(smem + L::kK + j * L::kTile, &tm_k, 0, krow0 + j * 128, &bars[kBarKFull + j]);
+      mbar_expect_tx(&bars[kBarVFull + j], L::kTile);
+      tma_load_2d(smem + L::kV + j * L::kTile, &tm_v, 0, krow0 + j * 128, &bars[kBarVFull + j]);
+    }
   }
+  for (int k = threadIdx.x; k < kTabEntries; k += blockDim.x) {   // entry k -> 16 copies, 64 bytes
+    const uint32_t t = (k < kTabLive) ? (uint32_t)kT2Live[k] : 0u;
+    const uint32_t a = smem_u32(s_t2 + k * kTabCopies);
+#pragma unroll
+    for (int c = 0; c < kTabCopies; c += 4) st_shared_v4(a + c * 4, t, t, t, t);
+  }
+  if (SINK && threadIdx.x < DH) v0row[threadIdx.x] = p.v8[(long long)krow0 * DH + threadIdx.x];
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(tmem_slot)) : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
@@ -160,12 +168,14 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  if (warp >= 10) {                                  // fold warps: bias both A accumulators
-    const uint32_t ab = tmem + ((uint32_t)((warp & 3) * 32) << 16) + 256 + ((warp - 10) >> 2) * HD;   // (fold warps)
+  bool role_fail = false;                            // fold gave up (the chain learns it via abort)
+  if (warp >= 10) {                                  // fold warps: bias A, zero O
+    const uint32_t rowb = tmem + ((uint32_t)((warp & 3) * 32) << 16);
 #pragma unroll
-    for (int s = 0; s < 2; ++s)
-#pragma unroll
-      for (int cc = 0; cc < HD / 16; ++cc) tmem_fill16(ab + s * 128 + cc * 16, kMagicBits);
+    for (int cc = 0; cc < DH / 16; ++cc) {
+      tmem_fill16(rowb + 256 + cc * 16, kMagicBits);
+      tmem_fill16(rowb + 384 + cc * 16, 0u);
+    }
     tc_wait_st();
   }
   tc_fence_before();
@@ -175,15 +185,13 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
   if (warp == 0) {
     // ================================================================ TMA producer
     if (lane == 0) {
-      mbar_expect_tx(&bars[kBarQ], L::kTile);
-      tma_load_2d(smem + L::kQ, &tm_q, 0, qrow0, &bars[kBarQ]);
-      for (int j = 0; j < nb; ++j) {
+      for (int j = npre; j < nb; ++j) {
         const int s = j & 1;
         const uint32_t ph = (j >> 1) & 1;
-        if (!mbar_wait(&bars[kBarKEmpty + s], ph ^ 1, abort_flag, p.err)) break;
+        if (!mbar_wait(&bars[kBarKEmpty + s], ph ^ 1, abort_flag, p.err, 128)) break;
         mbar_expect_tx(&bars[kBarKFull + s], L::kTile);
         tma_load_2d(smem + L::kK + s * L::kTile, &tm_k, 0, krow0 + j * 128, &bars[kBarKFull + s]);
-        if (!mbar_wait(&bars[kBarVEmpty + s], ph ^ 1, abort_flag, p.err)) break;
+        if (!mbar_wait(&bars[kBarVEmpty + s], ph ^ 1, abort_flag, p.err, 128)) break;
         mbar_expect_tx(&bars[kBarVFull + s], L::kTile);
         tma_load_2d(smem + L::kV + s * L::kTile, &tm_v, 0, krow0 + j * 128, &bars[kBarVFull + s]);
       }
@@ -220,7 +228,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
         const uint32_t ph = (j >> 1) & 1;
         if (!mbar_wait(&bars[kBarPFull + s], ph, abort_flag, p.err)) break;
         if (!mbar_wait(&bars[kBarVFull + s], ph, abort_flag, p.err)) break;
-        if (!mbar_wait(&bars[kBarAEmpty + s], ph ^ 1, abort_flag, p.err)) break;
+        if (!mbar_wait(&bars[kBarAEmpty], (j & 1) ^ 1, abort_flag, p.err)) break;   // single A buffer
         tc_fence_after();
         const uint32_t sp = smem_u32(smem + L::kP + s * 16384);
         const uint32_t sv = smem_u32(smem + L::kV + s * L::kTile);
@@ -229,10 +237,10 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
           // A = P (K-major SW128, 32 keys = 32 bytes per step); B = V (MN-major: 32 keys =
           // 4 groups of 8 rows per step; LBO = MN-atom stride (one atom), SBO = 8-row stride).
           // Every step accumulates: the accumulator starts at the 1.5 * 2^23 bias.
-          umma_i8(tmem + 256 + s * 128, umma_desc(sp + kk * 32, 16, 1024, 2),
+          umma_i8(tmem + 256, umma_desc(sp + kk * 32, 16, 1024, 2),
                   umma_desc(sv + kk * 32 * DH, L::kTile, kRowGroup, kSwz), idesc_pv, 1u);
         }
-        umma_commit(&bars[kBarAFull + s]);
+        umma_commit(&bars[kBarAFull]);
         umma_commit(&bars[kBarVEmpty + s]);
         umma_commit(&bars[kBarPEmpty + s]);
       }
@@ -244,34 +252,37 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
     const int r = q4 * 32 + lane;
     const uint32_t lanebase = (uint32_t)(q4 * 32) << 16;
     const uint32_t lane4 = (uint32_t)(lane & 15) << 2;
+    const uint8_t* tab = reinterpret_cast<const uint8_t*>(s_t2);
     const int eqr = p.eq[(long long)qrow0 + r];
     const int32_t* ekg = p.ek + (long long)(b * p.KVH + g) * p.nblk;
     const uint32_t prow = (uint32_t)((r >> 3) * 1024 + (r & 7) * 128);
     for (int j = 0; j < nb; ++j) {
       const int s = j & 1;
       const uint32_t ph = (j >> 1) & 1;
-      if (!mbar_wait_warp(&bars[kBarSFull + s], ph, abort_flag, p.err)) break;
+      if (!group_wait(&bars[kBarSFull + s], ph, warp == 2 && lane == 0, 1, 256, abort_flag, p.err)) break;
       tc_fence_after();
       const bool diag = (j == tile);                     // key c of the diagonal block visible iff c <= r
       const uint32_t sbase = tmem + lanebase + s * 128 + kh * 64;
-      // pass 1: exact max over this thread's visible keys, then over the row
-      int m = INT32_MIN;
-#pragma unroll 1
-      for (int cc = 0; cc < 4; ++cc) {
-        uint32_t v[16];
-        tmem_ld16(sbase + cc * 16, v);
-        tc_wait_ld();
-        if (diag) {
+      // pass 1: this thread's 64 scores into registers (one TMEM round trip; S is free for the
+      // next QK as soon as they have landed), the exact max over its visible keys, then the row's
+      uint32_t v[64];
+      tmem_ld16(sbase, v);
+      tmem_ld16(sbase + 16, v + 16);
+      tmem_ld16(sbase + 32, v + 32);
+      tmem_ld16(sbase + 48, v + 48);
+      tc_wait_ld();
+      tc_fence_before();
+      mbar_arrive(&bars[kBarSEmpty + s]);
+      if (diag) {
 #pragma unroll
-          for (int c = 0; c < 16; ++c) if (kh * 64 + cc * 16 + c > r) v[c] = 0x80000000u;
-        }
-        int m2 = __vimax3_s32((int)v[0], (int)v[1], (int)v[2]);
-#pragma unroll
-        for (int c = 3; c < 15; c += 2) m2 = __vimax3_s32(m2, (int)v[c], (int)v[c + 1]);
-        m = __vimax3_s32(m, m2, (int)v[15]);
+        for (int c = 0; c < 64; ++c) if (kh * 64 + c > r) v[c] = 0x80000000u;
       }
+      int m = __vimax3_s32((int)v[0], (int)v[1], (int)v[2]);
+#pragma unroll
+      for (int c = 3; c < 63; c += 2) m = __vimax3_s32(m, (int)v[c], (int)v[c + 1]);
+      m = max(m, (int)v[63]);
       pmax[(s * 2 + kh) * 128 + r] = m;
-      named_bar_sync(1, 256);
+      if (bar_any(1, 256, *abort_flag != 0)) break;     // the two halves of each row meet here
       m = max(pmax[(s * 2) * 128 + r], pmax[(s * 2 + 1) * 128 + r]);
       const uint32_t G = g_fold(p.gbase, eqr + ekg[j]);
       const int nbv = nb_of(m, G);
@@ -280,26 +291,19 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
       const int dm = 1 << max(0, 30 - lg);              // dm * G in [2^30, 2^31): >= 9 doublings
       const int lo = m - dm;
       const uint32_t negG = 0u - G;
-      if (!mbar_wait_warp(&bars[kBarPEmpty + s], ph ^ 1, abort_flag, p.err)) break;
+      if (!group_wait(&bars[kBarPEmpty + s], ph ^ 1, warp == 2 && lane == 0, 1, 256, abort_flag, p.err)) break;
       const uint32_t pbase = smem_u32(smem + L::kP + s * 16384) + prow;
       uint32_t lb = 0, eh0 = 0;
-      // pass 2: the chain and the u8 P half-row (one 16-key chunk per 16 columns)
-#pragma unroll 1
-      for (int cc = 0; cc < 4; ++cc) {
-        uint32_t v[16];
-        tmem_ld16(sbase + cc * 16, v);
-        tc_wait_ld();
-        if (diag) {
+      // pass 2: the chain and the u8 P half-row, 16 keys (one 16-byte P chunk) at a time
 #pragma unroll
-          for (int c = 0; c < 16; ++c) if (kh * 64 + cc * 16 + c > r) v[c] = 0x80000000u;
-        }
+      for (int cc = 0; cc < 4; ++cc) {
         uint32_t w[4];
 #pragma unroll
         for (int qq = 0; qq < 4; ++qq) {
           uint32_t e[4];
 #pragma unroll
           for (int x = 0; x < 4; ++x) {
-            const int sc = max((int)v[qq * 4 + x], lo);
+            const int sc = max((int)v[cc * 16 + qq * 4 + x], lo);
             uint32_t d = NBlo + (uint32_t)sc * negG;       // exact: d < 2^32
             d = min(d, kDClamp);                           // index <= 1152 (T2 = 0 from 1152 on)
             e[x] = tab[((d >> (kIdxShift - 6)) & ~63u) | lane4];
@@ -311,11 +315,9 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
         if (SINK && chunk == 0 && j == 0 && p.T > 1) { eh0 = w[0] & 0xFFu; w[0] &= ~0xFFu; }
         st_shared_v4(pbase + (uint32_t)((chunk ^ (r & 7)) << 4), w[0], w[1], w[2], w[3]);
       }
-      tc_fence_before();
-      mbar_arrive(&bars[kBarSEmpty + s]);
       fence_async_smem();
       mbar_arrive(&bars[kBarPFull + s]);
-      if (!mbar_wait_warp(&bars[kBarIEmpty + s], ph ^ 1, abort_flag, p.err)) break;
+      if (!group_wait(&bars[kBarIEmpty + s], ph ^ 1, warp == 2 && lane == 0, 1, 256, abort_flag, p.err)) break;
       int* slot = info + (s * 128 + r) * 4;
       if (kh == 0) { slot[0] = nbv; slot[1] = (int)lb; slot[2] = (int)eh0; }
       else { slot[3] = (int)lb; }
@@ -325,136 +327,175 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
     // ================================================================ fold warps
     const int q4 = warp & 3;
     const int r = q4 * 32 + lane;
-    const int c0 = ((warp - 10) >> 2) * HD;            // this thread's 32 channels
-    const uint32_t lanebase = (uint32_t)(q4 * 32) << 16;
+    const uint32_t rowb = tmem + ((uint32_t)(q4 * 32) << 16);
+    const uint32_t abase = rowb + 256, obase = rowb + 384;
     const int32_t* evg = p.ev + (long long)(b * p.KVH + g) * p.nblk;
     const int ev0 = SINK ? p.ev0[b * p.KVH + g] : 0;
-    uint64_t O2[HD / 2];                               // O as binary32 pairs
-#pragma unroll
-    for (int c = 0; c < HD / 2; ++c) O2[c] = 0ull;
     const uint64_t negM2 = f2_pack(-12582912.0f, -12582912.0f);
     float lseg = 0.0f, lrow = 0.0f;
     int nbrun = 0, nbrow = 0;
     bool have_seg = false, have_row = false;
     bool ok = true;
-    float* orow = MULTI ? p.orow + ((long long)qrow0 + r) * DH + c0 : nullptr;
+    float* orow = MULTI ? p.orow + ((long long)qrow0 + r) * DH : nullptr;
     for (int j = 0; j < nb; ++j) {
       const int s = j & 1;
       const uint32_t ph = (j >> 1) & 1;
-      if (!mbar_wait_warp(&bars[kBarIFull + s], ph, abort_flag, p.err)) { ok = false; break; }
+      if (!group_wait(&bars[kBarIFull + s], ph, warp == 10 && lane == 0, 2, kFoldThreads, abort_flag, p.err)) {
+        ok = false;
+        break;
+      }
       const int4 inf = *reinterpret_cast<const int4*>(info + (s * 128 + r) * 4);
       mbar_arrive(&bars[kBarIEmpty + s]);
       const int nbb = inf.x;
       if (!have_seg) { nbrun = nbb; have_seg = true; }
       const int D = nbb - nbrun;
-      int sg = 0;
-      if (D > 0) {
-#pragma unroll
-        for (int c = 0; c < HD / 2; ++c) {
-          float lo_, hi_;
-          f2_unpack(O2[c], lo_, hi_);
-          O2[c] = f2_pack(rescale(lo_, D), rescale(hi_, D));
-        }
+      // Per-row decisions (rescale by D, add or skip the block) stay in arithmetic: every
+      // tcgen05.ld/st below is warp-collective (.sync.aligned) and runs on all 32 lanes.
+      int sg = 0, Dr = 0;
+      if (D > 0) {                                     // a new running max: rescale O and l
+        Dr = D;
         lseg = rescale(lseg, D);
         nbrun = nbb;
       } else {
         sg = -D;
       }
-      if (!mbar_wait_warp(&bars[kBarAFull + s], ph, abort_flag, p.err)) { ok = false; break; }
+      if (!group_wait(&bars[kBarAFull], j & 1, warp == 10 && lane == 0, 2, kFoldThreads, abort_flag, p.err)) {
+        ok = false;
+        break;
+      }
       tc_fence_after();
-      const uint32_t abase = tmem + lanebase + 256 + s * 128 + c0;
-      if (sg <= kSWIN) {
-        if (SINK && j == 0 && p.T > 1) {
-          const float sc0 = pow2f(-(sg + ev0));
-#pragma unroll
-          for (int c = 0; c < HD / 2; ++c) {
-            float lo_, hi_;
-            f2_unpack(O2[c], lo_, hi_);
-            lo_ = fold_term(lo_, inf.z * (int)v0row[c0 + 2 * c], sc0);
-            hi_ = fold_term(hi_, inf.z * (int)v0row[c0 + 2 * c + 1], sc0);
-            O2[c] = f2_pack(lo_, hi_);
-          }
-        }
-        const float scO = pow2f(-(sg + evg[j]));
+      {
+        const bool add = (sg <= kSWIN);
+        const float scO = pow2f(-(min(sg, kSWIN) + evg[j]));
         const uint64_t scO2 = f2_pack(scO, scO);
-#pragma unroll
-        for (int cc = 0; cc < HD / 8; ++cc) {
-          uint32_t a[8];
-          tmem_ld8(abase + cc * 8, a);
+        const bool sink_term = SINK && j == 0 && p.T > 1;
+        const float sc0 = pow2f(-(min(sg, kSWIN) + ev0));
+        const uint64_t sc02 = f2_pack(sc0, sc0);
+        // 16-column chunks, software-pipelined: chunk cc + 1's TMEM loads are in flight while
+        // chunk cc is folded (tcgen05.wait::ld waits for every earlier load, so the loads of the
+        // next chunk are issued only after the current chunk's wait)
+        uint32_t an[16], on[16];
+        tmem_ld16(abase, an);
+        tmem_ld16(obase, on);
+#pragma unroll 1
+        for (int cc = 0; cc < DH / 16; ++cc) {
+          uint32_t a[16], o[16];
           tc_wait_ld();
 #pragma unroll
-          for (int t = 0; t < 4; ++t) {
-            const uint64_t x = f2_add(f2_pack(__uint_as_float(a[2 * t]), __uint_as_float(a[2 * t + 1])), negM2);
-            O2[cc * 4 + t] = f2_fma(x, scO2, O2[cc * 4 + t]);
+          for (int c = 0; c < 16; ++c) { a[c] = an[c]; o[c] = on[c]; }
+          tmem_fill16(abase + cc * 16, kMagicBits);          // re-bias for the next PV
+          if (cc + 1 < DH / 16) {
+            tmem_ld16(abase + (cc + 1) * 16, an);
+            tmem_ld16(obase + (cc + 1) * 16, on);
           }
+          if (Dr > 0) {
+#pragma unroll
+            for (int c = 0; c < 16; ++c) o[c] = __float_as_uint(rescale(__uint_as_float(o[c]), Dr));
+          }
+          if (add) {
+#pragma unroll
+            for (int t = 0; t < 8; ++t) {
+              uint64_t o2 = f2_pack(__uint_as_float(o[2 * t]), __uint_as_float(o[2 * t + 1]));
+              if (sink_term) {                                // key 0's term first (B9.1)
+                const int c = cc * 16 + 2 * t;
+                const uint64_t z = f2_pack(i2f_small(inf.z * (int)v0row[c]), i2f_small(inf.z * (int)v0row[c + 1]));
+                o2 = f2_fma(z, sc02, o2);
+              }
+              const uint64_t x = f2_add(f2_pack(__uint_as_float(a[2 * t]), __uint_as_float(a[2 * t + 1])), negM2);
+              o2 = f2_fma(x, scO2, o2);
+              float lo_, hi_;
+              f2_unpack(o2, lo_, hi_);
+              o[2 * t] = __float_as_uint(lo_);
+              o[2 * t + 1] = __float_as_uint(hi_);
+            }
+          }
+          tmem_st16(obase + cc * 16, o);
         }
-#pragma unroll
-        for (int cc = 0; cc < HD / 16; ++cc) tmem_fill16(abase + cc * 16, kMagicBits);   // re-bias for the next PV
-        lseg = fold_term(lseg, inf.y + inf.w, pow2f(-sg));
-      } else {
-#pragma unroll
-        for (int cc = 0; cc < HD / 16; ++cc) tmem_fill16(abase + cc * 16, kMagicBits);
+        if (add) lseg = fold_term(lseg, inf.y + inf.w, pow2f(-sg));
       }
       tc_wait_st();
       tc_fence_before();
-      mbar_arrive(&bars[kBarAEmpty + s]);
+      mbar_arrive(&bars[kBarAEmpty]);
       if (MULTI && (((j + 1) % kSEG == 0) || (j == nb - 1))) {
         // segment -> row: the same three rules (reference/lssab8_golden.py:317-331)
-        int s2 = 0;
-        if (!have_row) {
-          nbrow = nbrun; have_row = true;
+        int D2 = 0, s2 = 0;
+        const bool first = !have_row;
+        if (first) { nbrow = nbrun; have_row = true; }
+        else { D2 = nbrun - nbrow; if (D2 > 0) { lrow = rescale(lrow, D2); nbrow = nbrun; } else { s2 = -D2; } }
+#pragma unroll 1
+        for (int cc = 0; cc < DH / 16; ++cc) {
+          uint32_t o[16];
+          tmem_ld16(obase + cc * 16, o);
+          tc_wait_ld();
 #pragma unroll
-          for (int c = 0; c < HD / 2; ++c) {
-            float lo_, hi_;
-            f2_unpack(O2[c], lo_, hi_);
-            *reinterpret_cast<float2*>(orow + 2 * c) = make_float2(rescale(lo_, 0), rescale(hi_, 0));
-          }
-          lrow = rescale(lseg, 0);
-        } else {
-          const int D2 = nbrun - nbrow;
-          if (D2 > 0) { lrow = rescale(lrow, D2); nbrow = nbrun; } else { s2 = -D2; }
-#pragma unroll 4
-          for (int c = 0; c < HD / 2; ++c) {
-            float2 o = *reinterpret_cast<const float2*>(orow + 2 * c);
-            if (D2 > 0) { o.x = rescale(o.x, D2); o.y = rescale(o.y, D2); }
-            if (s2 <= kSWIN) {
-              float lo_, hi_;
-              f2_unpack(O2[c], lo_, hi_);
-              o.x = __fadd_rn(o.x, rescale(lo_, s2));
-              o.y = __fadd_rn(o.y, rescale(hi_, s2));
+          for (int c = 0; c < 16; ++c) {
+            float* pr = orow + cc * 16 + c;
+            const float seg = __uint_as_float(o[c]);
+            if (first) *pr = rescale(seg, 0);
+            else {
+              float x = *pr;
+              if (D2 > 0) x = rescale(x, D2);
+              if (s2 <= kSWIN) x = __fadd_rn(x, rescale(seg, s2));
+              *pr = x;
             }
-            *reinterpret_cast<float2*>(orow + 2 * c) = o;
           }
-          if (s2 <= kSWIN) lrow = __fadd_rn(lrow, rescale(lseg, s2));
+          tmem_fill16(obase + cc * 16, 0u);
         }
-#pragma unroll
-        for (int c = 0; c < HD / 2; ++c) O2[c] = 0ull;
+        tc_wait_st();
+        if (first) lrow = rescale(lseg, 0);
+        else if (s2 <= kSWIN) lrow = __fadd_rn(lrow, rescale(lseg, s2));
         lseg = 0.0f;
         have_seg = false;
       }
     }
-    // ---- epilogue: out = O_row / l_row (one RN division), l_row == 0 -> 0
-    const int i = tile * 128 + r;
-    if (ok && i < p.T) {
-      float y[HD];
-      if constexpr (!MULTI) {
-        lrow = rescale(lseg, 0);                         // a single segment: O_row = 0 + rescale(O_seg, 0)
+    if constexpr (!MULTI) lrow = rescale(lseg, 0);   // a single segment: O_row = 0 + rescale(O_seg, 0)
+    lrow_s[r] = lrow;
+    role_fail = !ok;
+  }
+
+  if (warp >= 2) {
+    // ================================================================ epilogue
+    // out = O_row / l_row (one RN division per element; l_row == 0 -> 0), shared by the chain
+    // and fold warps: TMEM lanes of warp w are rows 32 (w % 4) .. + 31, and the DH / 16 column
+    // chunks are split between the three warps of each row quarter.  The OR-barrier makes the
+    // skip decision (any role gave up) identical on all 384 threads, so the warp-collective
+    // TMEM loads below run on every lane or on none.
+    tc_fence_before();
+    const bool skip = bar_any(3, 384, role_fail || *abort_flag != 0);
+    tc_fence_after();
+    if (!skip) {
+      constexpr int kCh = DH / 16, kC1 = (kCh + 2) / 3;
+      const int q4 = warp & 3;
+      const int role = (warp < 10) ? ((warp - 2) >> 2) : 2;
+      const int c_lo = role * kC1, c_hi = min(kCh, c_lo + kC1);
+      const int r = q4 * 32 + lane;
+      const int i = tile * 128 + r;
+      const bool live = (i < p.T);
+      const float lr = lrow_s[r];
+      const bool nz = (lr != 0.0f);
+      const float rl = nz ? __frcp_rn(lr) : 0.0f;
+      const uint32_t obase = tmem + ((uint32_t)(q4 * 32) << 16) + 384;
+      OutT* dst = reinterpret_cast<OutT*>(p.out) + b * p.os0 + (long long)i * p.os1 + h * p.os2;
+      const float* orow = MULTI ? p.orow + ((long long)qrow0 + r) * DH : nullptr;
+#pragma unroll 1
+      for (int cc = c_lo; cc < c_hi; ++cc) {
+        float q[16];
+        if constexpr (!MULTI) {
+          uint32_t y[16];
+          tmem_ld16(obase + cc * 16, y);
+          tc_wait_ld();
 #pragma unroll
-        for (int c = 0; c < HD / 2; ++c) {
-          float lo_, hi_;
-          f2_unpack(O2[c], lo_, hi_);
-          y[2 * c] = rescale(lo_, 0);
-          y[2 * c + 1] = rescale(hi_, 0);
+          for (int c = 0; c < 16; ++c) q[c] = rescale(__uint_as_float(y[c]), 0);
+        } else {
+#pragma unroll
+          for (int c = 0; c < 16; ++c) q[c] = live ? orow[cc * 16 + c] : 0.0f;
         }
-      } else {
+        if (live) {
 #pragma unroll
-        for (int c = 0; c < HD; ++c) y[c] = orow[c];
+          for (int c = 0; c < 16; ++c) q[c] = nz ? div_rn_shared(q[c], lr, rl) : 0.0f;
+          store_chunk<OutT, 16>(dst + cc * 16 * p.os3, p.os3, q);
+        }
       }
-      const bool nz = (lrow != 0.0f);
-#pragma unroll
-      for (int c = 0; c < HD; ++c) y[c] = nz ? __fdiv_rn(y[c], lrow) : 0.0f;
-      OutT* dst = reinterpret_cast<OutT*>(p.out) + b * p.os0 + (long long)i * p.os1 + h * p.os2 + c0 * p.os3;
-      store_row<OutT, HD>(dst, p.os3, y);
     }
   }
 

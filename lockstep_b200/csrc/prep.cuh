@@ -111,4 +111,152 @@ quant_blocks_kernel(const InT* __restrict__ x, Strides4 xs, int B, int KVH, int 
   }
 }
 
+// ------------------------------------------------------------ vectorised fast paths
+// Used when the channel dimension is contiguous and every row starts on a 16-byte boundary:
+// each lane moves 16 bytes per load, rows stay in registers between the amax and the
+// quantisation, and nothing divides.  Bit-identical to the general kernels above (same
+// exponent rule, same rounding).
+
+template <typename InT> struct Vec16 {
+  static constexpr int kN = 16 / sizeof(InT);          // elements per 16-byte vector
+};
+
+template <typename InT>
+__device__ __forceinline__ void unpack16(const uint4& u, float* f) {
+  const InT* e = reinterpret_cast<const InT*>(&u);
+#pragma unroll
+  for (int i = 0; i < Vec16<InT>::kN; ++i) f[i] = to_f32(e[i]);
+}
+
+// pack kN quantised values (bytes) into kN bytes: 8 -> uint2, 4 -> uint32
+template <int N> struct PackOut;
+template <> struct PackOut<8> {
+  using T = uint2;
+  static __device__ __forceinline__ T pack(const int* q) {
+    T r;
+    r.x = (uint32_t)(q[0] & 0xFF) | ((uint32_t)(q[1] & 0xFF) << 8) | ((uint32_t)(q[2] & 0xFF) << 16) | ((uint32_t)q[3] << 24);
+    r.y = (uint32_t)(q[4] & 0xFF) | ((uint32_t)(q[5] & 0xFF) << 8) | ((uint32_t)(q[6] & 0xFF) << 16) | ((uint32_t)q[7] << 24);
+    return r;
+  }
+};
+template <> struct PackOut<4> {
+  using T = uint32_t;
+  static __device__ __forceinline__ T pack(const int* q) {
+    return (uint32_t)(q[0] & 0xFF) | ((uint32_t)(q[1] & 0xFF) << 8) | ((uint32_t)(q[2] & 0xFF) << 16) | ((uint32_t)q[3] << 24);
+  }
+};
+
+// P1 fast path: G = DH*sizeof/16 lanes per row, 32/G rows per warp.
+template <typename InT, int DH>
+__global__ void __launch_bounds__(256)
+quant_rows_vec_kernel(const InT* __restrict__ x, Strides4 xs, int B, int H, int T, int Tpad,
+                      int8_t* __restrict__ q8, int32_t* __restrict__ eq) {
+  constexpr int N = Vec16<InT>::kN;
+  constexpr int G = DH / N;                            // lanes per row
+  constexpr int RPW = 32 / G;                          // rows per warp
+  const int lane = threadIdx.x & 31;
+  const long long row = ((long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * RPW + lane / G;
+  const int sub = lane % G;
+  const long long nrows = (long long)B * H * Tpad;
+  const bool live = row < nrows;
+  const long long rr = live ? row : 0;
+  const int t = (int)(rr % Tpad);
+  const long long bh = rr / Tpad;
+  const int h = (int)(bh % H), b = (int)(bh / H);
+  const bool data = live && t < T;
+  float f[N];
+  float m = 0.0f;
+  if (data) {
+    const uint4 u = *reinterpret_cast<const uint4*>(x + b * xs.s0 + h * xs.s1 + (long long)t * xs.s2 + sub * N);
+    unpack16<InT>(u, f);
+#pragma unroll
+    for (int i = 0; i < N; ++i) m = fmaxf(m, fabsf(f[i]));
+  } else {
+#pragma unroll
+    for (int i = 0; i < N; ++i) f[i] = 0.0f;
+  }
+#pragma unroll
+  for (int o = G / 2; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if (!live) return;
+  const int e = data ? pow2_exponent(m, 40) : 0;
+  const float sc = pow2f(e);
+  int q[N];
+#pragma unroll
+  for (int i = 0; i < N; ++i) q[i] = quant8(f[i], sc);
+  *reinterpret_cast<typename PackOut<N>::T*>(q8 + rr * DH + sub * N) = PackOut<N>::pack(q);
+  if (sub == 0) eq[rr] = e;
+}
+
+// P2/P3 fast path: one CTA of 256 threads per (block, kv head, batch); the block's 128 x DH
+// values stay in registers (<= 8 vectors per thread) between the amax and the quantisation.
+template <typename InT, int DH>
+__global__ void __launch_bounds__(256)
+quant_blocks_vec_kernel(const InT* __restrict__ x, Strides4 xs, int B, int KVH, int T, int Tpad, int mode,
+                        int8_t* __restrict__ x8, int32_t* __restrict__ eblk, int32_t* __restrict__ e0,
+                        int* __restrict__ err) {
+  constexpr int N = Vec16<InT>::kN;
+  constexpr int VPR = DH / N;                          // vectors per row
+  constexpr int VPT = 128 * VPR / 256;                 // vectors per thread
+  const int blk = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+  const int nblk = (T + kKB - 1) / kKB;
+  const int lo = blk * kKB;
+  const int hi = min(T, lo + kKB);
+  const bool split0 = (mode == 2) && (blk == 0) && (T > 1);
+  const InT* src = x + b * xs.s0 + g * xs.s1;
+  int8_t* dst = x8 + ((long long)(b * KVH + g) * Tpad) * DH;
+  __shared__ float red[2][8];
+  float f[VPT][N];
+  float m = 0.0f, m0 = 0.0f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int v = threadIdx.x + i * 256;
+    const int r = lo + v / VPR, c = (v % VPR) * N;
+    if (r < hi) {
+      unpack16<InT>(*reinterpret_cast<const uint4*>(src + (long long)r * xs.s2 + c), f[i]);
+      float a = 0.0f;
+#pragma unroll
+      for (int k = 0; k < N; ++k) a = fmaxf(a, fabsf(f[i][k]));
+      if (split0 && r == 0) m0 = fmaxf(m0, a); else m = fmaxf(m, a);
+    } else {
+#pragma unroll
+      for (int k = 0; k < N; ++k) f[i][k] = 0.0f;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, o));
+  }
+  if ((threadIdx.x & 31) == 0) { red[0][threadIdx.x >> 5] = m; red[1][threadIdx.x >> 5] = m0; }
+  __syncthreads();
+  m = 0.0f; m0 = 0.0f;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) { m = fmaxf(m, red[0][w]); m0 = fmaxf(m0, red[1][w]); }
+  const int hic = (mode == 0) ? 40 : 48;
+  const int e = pow2_exponent(m, hic);
+  const int ez = split0 ? pow2_exponent(m0, 48) : e;
+  const float sc = pow2f(e), sc0 = pow2f(ez);
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int v = threadIdx.x + i * 256;
+    const int r = lo + v / VPR, c = (v % VPR) * N;
+    if (r < lo + kKB && r < Tpad) {                    // rows past T (padding) become zeros
+      int q[N];
+#pragma unroll
+      for (int k = 0; k < N; ++k) q[k] = (r < hi) ? quant8(f[i][k], (split0 && r == 0) ? sc0 : sc) : 0;
+      *reinterpret_cast<typename PackOut<N>::T*>(dst + (long long)r * DH + c) = PackOut<N>::pack(q);
+    }
+  }
+  // zero padding rows past this (last) block, up to Tpad
+  if (blk == nblk - 1) {
+    const int npad = (Tpad - (lo + kKB)) * DH;
+    for (int i = threadIdx.x; i < npad; i += blockDim.x) dst[(long long)(lo + kKB) * DH + i] = 0;
+  }
+  if (threadIdx.x == 0) {
+    eblk[(long long)(b * KVH + g) * nblk + blk] = e;
+    if (mode == 2 && blk == 0) e0[b * KVH + g] = ez;
+    if (mode != 0 && (e < -32 || e > 40)) atomicOr(err, kDevEvRange);
+  }
+}
+
 }  // namespace lssab8
