@@ -404,6 +404,10 @@ int lssab8_prefill_lattice(const int8_t* q8, const int32_t* eq, const int8_t* k8
   a.out = out; a.os0 = os[0]; a.os1 = os[1]; a.os2 = os[2]; a.os3 = os[3]; a.out_dtype = out_dtype;
   a.orow = orow_scratch;
   a.gbase = gbase_of(dh);
+  a.mul_entry = kTabCopies * 4;
+  a.mul_b1 = 1u << 8;
+  a.mul_b2 = 1u << 16;
+  a.mul_b3 = 1u << 24;
   a.err = ds->err;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool sink = ev0 != nullptr;

@@ -100,6 +100,30 @@ __device__ __forceinline__ float rescale(float x, int D) {
   return (e >= 1 && ne >= 1) ? __uint_as_float((u & 0x807FFFFFu) | ((uint32_t)ne << 23)) : 0.0f;
 }
 
+// The same rescale in floating-point form, for applying one row's D to many values: flush to +0
+// iff |x| < 2^(D - 126) (equivalently biased exponent - D < 1, or x zero / subnormal), else
+// x * 2^-d1 * 2^-d2 with d1 + d2 = D, both products exact because the result is normal.  D == 0
+// gives the identity (thr = 0, factors 1), so lanes without a rescale can share the code.
+// Checked against rescale() for every finite binary32 x at D = 1, 5, 126..128, 150, 200,
+// 252..254 and 1000.
+struct RowRescale { float s1, s2, thr; };
+__device__ __forceinline__ float pow2f_sub(int e) {            // 2^e for e in [-149, 127]
+  return e >= -126 ? __uint_as_float((uint32_t)(e + 127) << 23) : __uint_as_float(1u << (e + 149));
+}
+__device__ __forceinline__ RowRescale row_rescale(int D) {
+  RowRescale r;
+  if (D <= 0) { r.s1 = 1.0f; r.s2 = 1.0f; r.thr = 0.0f; return r; }
+  r.thr = D <= 253 ? __uint_as_float((uint32_t)(D + 1) << 23) : __uint_as_float(0x7F800000u);
+  const int d1 = D < 126 ? D : 126;
+  const int d2 = D - d1 < 127 ? D - d1 : 127;
+  r.s1 = pow2f_sub(-d1);
+  r.s2 = pow2f_sub(-d2);
+  return r;
+}
+__device__ __forceinline__ float apply_rescale(float x, const RowRescale& r) {
+  return fabsf(x) < r.thr ? 0.0f : __fmul_rn(__fmul_rn(x, r.s1), r.s2);
+}
+
 // Exact int -> binary32 for |a| < 2^22 without the conversion pipe: the bit pattern a + 0x4B400000
 // is the float 1.5*2^23 + a (its exponent cannot change for |a| < 2^22), and subtracting
 // 1.5*2^23 is exact.  Every integer the fold converts is below 2^22: |A_b| <= 4,145,280,
@@ -124,16 +148,18 @@ __device__ __forceinline__ float fold_term(float O, int A, float sc) {
 // needs no underflow or overflow in any step, so it is used only for |y|, |l| in
 // [2^-31, 2^32) (quotient and remainder far inside the normal range); any other operand
 // (zero, subnormal, tiny or huge) takes the IEEE division __fdiv_rn.
-__device__ __forceinline__ bool div_window(float x) {
-  return ((__float_as_uint(x) >> 23) & 0xFFu) - 96u <= 62u;   // biased exponent in [96, 158]
+__device__ __forceinline__ bool div_window(float x) {       // 2^-31 <= |x| < 2^32 (biased exponent 96..158)
+  const float ax = fabsf(x);
+  return ax >= 0x1p-31f && ax < 0x1p32f;
+}
+__device__ __forceinline__ float div_markstein(float y, float l, float rl) {
+  const float q0 = __fmul_rn(y, rl);
+  const float q1 = __fmaf_rn(__fmaf_rn(-q0, l, y), rl, q0);
+  return __fmaf_rn(__fmaf_rn(-q1, l, y), rl, q1);
 }
 __device__ __noinline__ float div_rn_ieee(float y, float l) { return __fdiv_rn(y, l); }
 __device__ __forceinline__ float div_rn_shared(float y, float l, float rl) {
-  if (div_window(y) && div_window(l)) {
-    const float q0 = __fmul_rn(y, rl);
-    const float q1 = __fmaf_rn(__fmaf_rn(-q0, l, y), rl, q0);
-    return __fmaf_rn(__fmaf_rn(-q1, l, y), rl, q1);
-  }
+  if (div_window(y) && div_window(l)) return div_markstein(y, l, rl);
   return div_rn_ieee(y, l);                 // rare: kept out of line
 }
 
@@ -257,6 +283,18 @@ __device__ __forceinline__ bool group_wait(uint64_t* bar, uint32_t parity, bool 
   if (bar_any(bar_id, nthreads, fail || *abort != 0)) return false;
   (void)mbar_test(bar, parity);
   return true;
+}
+
+// Warp-uniform poll for phases completed by tcgen05.commit: lane 0 polls (bounded, abort-aware),
+// the verdict is broadcast, and on success every lane observes the completed phase itself (it
+// cannot advance again before this warp arrives on the matching release barrier), which gives
+// each lane the acquire ordering.  Every lane returns the same value.
+__device__ __forceinline__ bool warp_poll(uint64_t* bar, uint32_t parity, volatile int* abort, int* err) {
+  int ok = 0;
+  if ((threadIdx.x & 31) == 0) ok = mbar_poll(bar, parity, abort, err) ? 1 : 0;
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  if (ok) (void)mbar_test(bar, parity);
+  return ok != 0;
 }
 
 // Warp-uniform form of mbar_wait for warps that next issue .sync.aligned instructions

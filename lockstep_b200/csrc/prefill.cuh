@@ -9,23 +9,27 @@
 //   warp 1      TMEM owner and MMA issuer (one thread):
 //                 S_b  = Q8 . K8_b^T   tcgen05.mma kind::i8, s8 x s8 -> s32, M=128 N=128 K=dh
 //                 A_b  = P_b . V8_b    tcgen05.mma kind::i8, u8 x s8 -> s32, M=128 N=dh K=128
-//               TMEM columns: S double-buffered [0, 256), A [256, 384), O [384, 512).
-//   warps 2-9   "chain" warps, two threads per query row (TMEM lane = row, 64 keys each):
-//               exact block max (the two halves meet through shared memory and a named
-//               barrier), G, NB, the 32-bit chain d = NB - max(S, m - dm) * G (mod 2^32), the T2
-//               gather from a lane-replicated shared table (at most 2-way bank conflicts),
-//               l_b = sum eh, and the u8 P half-row written in the SW128 K-major layout the
-//               PV MMA reads.
-//   warps 10-13 "fold" warps, one thread per row: the committed-order binary32 fold of
+//               TMEM columns: S [0, 128) (single: the chain copies a tile into registers
+//               and releases it at once, so QK(j+1) overwrites it while block j's chain
+//               runs), A double-buffered [128, 384) (PV(j+1) overlaps the fold of block j),
+//               O [384, 512).
+//   warps 2-9   row workers, two threads per query row (TMEM lane = row).  Iteration j:
+//               the chain of block j over this thread's 64 keys -- exact block max (the two
+//               halves meet through shared memory at one named barrier per block), G, NB, the
+//               32-bit chain d = NB - max(S, m - dm) * G (mod 2^32), the T2 gather from a
+//               lane-replicated shared table (at most 2-way bank conflicts), l_b, and the u8 P
+//               half-row in the SW128 K-major layout the PV MMA reads -- then the fold of block
+//               j - 1 over this thread's DH/2 channels: the committed-order binary32 fold of
 //               (NB_b, l_b, A_b) into the row's O, which lives in TMEM (paired f32x2
 //               arithmetic), the segment -> row fold at 32-block boundaries (O_row in a
-//               workspace buffer when a row spans > 1 segment), and the epilogue
-//               fl(O / l) -> output dtype.
+//               workspace buffer when a row spans > 1 segment), and finally fl(O / l).
+//               One role per SMSP-resident warp keeps the fold from being starved of issue
+//               slots by separate chain warps, and 10 warps leave 168 registers per thread.
 //
 // The A accumulator is pre-loaded with the bit pattern 0x4B400000 (the float 1.5 * 2^23) and
 // the PV MMA accumulates onto it, so the fold reads 1.5 * 2^23 + A_b as a float: one subtraction
 // recovers A_b exactly (|A_b| < 2^22) and one fused multiply-add folds it (exact product, one
-// rounding).  The fold thread writes the bias back after reading.
+// rounding).  The fold writes the bias back after reading.
 //
 // Exactness: S and A_b are exact integer sums (any MMA order); everything after them is the
 // contract's integer chain and a fixed sequence of RN binary32 operations per row
@@ -48,6 +52,10 @@ struct PrefillArgs {
   int out_dtype;
   float* orow;          // [B, H, Tpad, dh] f32: O_row of rows spanning > 1 segment (else unused)
   uint32_t gbase;
+  // Integer multipliers passed at run time (64, 2^8, 2^16, 2^24): the table address and the P
+  // byte packing then compile to integer multiply-adds on the FMA pipe instead of shifts and
+  // byte permutes on the ALU pipe, which the chain saturates.
+  uint32_t mul_entry, mul_b1, mul_b2, mul_b3;
   int* err;
 };
 
@@ -56,8 +64,7 @@ constexpr int kTabCopies = 16;                                // T2 copies, one 
 constexpr int kTabEntries = kTabLive + 1;                     // index 1152 (T2 = 0) absorbs clamped d
 constexpr uint32_t kDClamp = (uint32_t)kTabLive << kIdxShift; // min(d, 1152 << 19) -> index <= 1152
 constexpr uint32_t kMagicBits = 0x4B400000u;                  // 1.5 * 2^23
-constexpr int kPrefillThreads = 448;                          // 14 warps: TMA, MMA, 8 chain, 4 fold
-constexpr int kFoldThreads = 128;
+constexpr int kPrefillThreads = 320;                          // 10 warps: TMA, MMA, 8 row workers
 constexpr int kTabBytes = kTabEntries * kTabCopies * 4;       // 73,792 B at the start of dynamic smem
 
 template <int DH>
@@ -67,19 +74,17 @@ struct PrefillSmem {
   static constexpr int kK = kTile;                       // 2 stages
   static constexpr int kV = 3 * kTile;                   // 2 stages
   static constexpr int kP = 5 * kTile;                   // 2 x 16 KB, SW128 K-major u8
-  static constexpr int kInfo = kP + 2 * 16384;           // 2 x 128 x {nb, lb0, eh0, lb1}
-  static constexpr int kPmax = kInfo + 2 * 128 * 16;     // 2 parities x 2 halves x 128 rows
-  static constexpr int kV0 = kPmax + 2 * 2 * 128 * 4;    // key 0's int8 value row (sink)
-  static constexpr int kLrow = kV0 + 256;                // 128 x l_row (binary32) for the epilogue
-  static constexpr int kBar = kLrow + 512;               // mbarriers
+  static constexpr int kV0 = kP + 2 * 16384;             // key 0's int8 value row (sink)
+  static constexpr int kBar = kV0 + 256;                 // mbarriers
   static constexpr int kMisc = kBar + 256;               // tmem base, abort flag
   static constexpr int kBytes = kMisc + 64;              // (+ the static T2 table)
 };
 
 enum BarId : int {
-  kBarQ = 0, kBarKFull = 1, kBarKEmpty = 3, kBarVFull = 5, kBarVEmpty = 7, kBarSFull = 9, kBarSEmpty = 11,
-  kBarPFull = 13, kBarPEmpty = 15, kBarAFull = 17, kBarAEmpty = 18, kBarIFull = 19, kBarIEmpty = 21
+  kBarQ = 0, kBarKFull = 1, kBarKEmpty = 3, kBarVFull = 5, kBarVEmpty = 7, kBarSFull = 9, kBarSEmpty = 10,
+  kBarPFull = 13, kBarPEmpty = 15, kBarAFull = 17, kBarAEmpty = 19
 };
+constexpr uint32_t kColS = 0, kColA = 128, kColO = 384;   // TMEM column map (A: two buffers of 128)
 
 // store n consecutive channels, vectorised when contiguous and aligned
 template <typename OutT, int N>
@@ -114,10 +119,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kMisc + 8);
-  int* info = reinterpret_cast<int*>(smem + L::kInfo);
-  int* pmax = reinterpret_cast<int*>(smem + L::kPmax);
   int8_t* v0row = reinterpret_cast<int8_t*>(smem + L::kV0);
-  float* lrow_s = reinterpret_cast<float*>(smem + L::kLrow);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ntile = gridDim.x;
@@ -136,12 +138,11 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
     for (int s = 0; s < 2; ++s) {
       mbar_init(&bars[kBarKFull + s], 1);   mbar_init(&bars[kBarKEmpty + s], 1);
       mbar_init(&bars[kBarVFull + s], 1);   mbar_init(&bars[kBarVEmpty + s], 1);
-      mbar_init(&bars[kBarSFull + s], 1);   mbar_init(&bars[kBarSEmpty + s], 256);
+      mbar_init(&bars[kBarAFull + s], 1);   mbar_init(&bars[kBarAEmpty + s], 256);
       mbar_init(&bars[kBarPFull + s], 256); mbar_init(&bars[kBarPEmpty + s], 1);
-      mbar_init(&bars[kBarIFull + s], 256); mbar_init(&bars[kBarIEmpty + s], kFoldThreads);
     }
-    mbar_init(&bars[kBarAFull], 1);
-    mbar_init(&bars[kBarAEmpty], kFoldThreads);
+    mbar_init(&bars[kBarSFull], 1);
+    mbar_init(&bars[kBarSEmpty], 256);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     mbar_expect_tx(&bars[kBarQ], L::kTile);
@@ -153,11 +154,18 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
       tma_load_2d(smem + L::kV + j * L::kTile, &tm_v, 0, krow0 + j * 128, &bars[kBarVFull + j]);
     }
   }
-  for (int k = threadIdx.x; k < kTabEntries; k += blockDim.x) {   // entry k -> 16 copies, 64 bytes
-    const uint32_t t = (k < kTabLive) ? (uint32_t)kT2Live[k] : 0u;
-    const uint32_t a = smem_u32(s_t2 + k * kTabCopies);
+  for (int k4 = threadIdx.x; k4 * 4 < kTabEntries; k4 += blockDim.x) {   // 4 entries per thread,
+    const uint32_t word = (k4 * 4 < kTabLive) ? reinterpret_cast<const uint32_t*>(kT2Live)[k4] : 0u;
 #pragma unroll
-    for (int c = 0; c < kTabCopies; c += 4) st_shared_v4(a + c * 4, t, t, t, t);
+    for (int e = 0; e < 4; ++e) {                    // entry k -> 16 copies, 64 bytes
+      const int k = k4 * 4 + e;
+      if (k < kTabEntries) {
+        const uint32_t t = (word >> (8 * e)) & 0xFFu;
+        const uint32_t a = smem_u32(s_t2 + k * kTabCopies);
+#pragma unroll
+        for (int c = 0; c < kTabCopies; c += 4) st_shared_v4(a + c * 4, t, t, t, t);
+      }
+    }
   }
   if (SINK && threadIdx.x < DH) v0row[threadIdx.x] = p.v8[(long long)krow0 * DH + threadIdx.x];
   if (warp == 1) {
@@ -168,13 +176,13 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  bool role_fail = false;                            // fold gave up (the chain learns it via abort)
-  if (warp >= 10) {                                  // fold warps: bias A, zero O
-    const uint32_t rowb = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+  if (warp >= 2) {                                   // row workers: bias both A buffers, zero O
+    const uint32_t rowb = tmem + ((uint32_t)((warp & 3) * 32 + ((warp - 2) >> 2) * 16) << 16);
 #pragma unroll
-    for (int cc = 0; cc < DH / 16; ++cc) {
-      tmem_fill16(rowb + 256 + cc * 16, kMagicBits);
-      tmem_fill16(rowb + 384 + cc * 16, 0u);
+    for (int cc = 0; cc < DH / 32; ++cc) {
+      tmem_fill16x2<DH / 2>(rowb + kColA + cc * 16, kMagicBits);
+      tmem_fill16x2<DH / 2>(rowb + kColA + 128 + cc * 16, kMagicBits);
+      tmem_fill16x2<DH / 2>(rowb + kColO + cc * 16, 0u);
     }
     tc_wait_st();
   }
@@ -209,15 +217,17 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
         const int s = j & 1;
         const uint32_t ph = (j >> 1) & 1;
         if (!mbar_wait(&bars[kBarKFull + s], ph, abort_flag, p.err)) return false;
-        if (!mbar_wait(&bars[kBarSEmpty + s], ph ^ 1, abort_flag, p.err)) return false;
+        // S is single-buffered: QK(j) waits until the chain has copied S(j - 1) into registers
+        // (the j-th phase of S_empty, j >= 1)
+        if (j > 0 && !mbar_wait(&bars[kBarSEmpty], (j - 1) & 1, abort_flag, p.err)) return false;
         tc_fence_after();
         const uint32_t sk = smem_u32(smem + L::kK + s * L::kTile);
 #pragma unroll
         for (int kk = 0; kk < DH / 32; ++kk) {
-          umma_i8(tmem + s * 128, umma_desc(sq + kk * 32, 16, kRowGroup, kSwz),
+          umma_i8(tmem + kColS, umma_desc(sq + kk * 32, 16, kRowGroup, kSwz),
                   umma_desc(sk + kk * 32, 16, kRowGroup, kSwz), idesc_qk, kk > 0);
         }
-        umma_commit(&bars[kBarSFull + s]);
+        umma_commit(&bars[kBarSFull]);
         umma_commit(&bars[kBarKEmpty + s]);
         return true;
       };
@@ -228,7 +238,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
         const uint32_t ph = (j >> 1) & 1;
         if (!mbar_wait(&bars[kBarPFull + s], ph, abort_flag, p.err)) break;
         if (!mbar_wait(&bars[kBarVFull + s], ph, abort_flag, p.err)) break;
-        if (!mbar_wait(&bars[kBarAEmpty], (j & 1) ^ 1, abort_flag, p.err)) break;   // single A buffer
+        if (!mbar_wait(&bars[kBarAEmpty + s], ph ^ 1, abort_flag, p.err)) break;   // fold of block j - 2 done
         tc_fence_after();
         const uint32_t sp = smem_u32(smem + L::kP + s * 16384);
         const uint32_t sv = smem_u32(smem + L::kV + s * L::kTile);
@@ -237,42 +247,167 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
           // A = P (K-major SW128, 32 keys = 32 bytes per step); B = V (MN-major: 32 keys =
           // 4 groups of 8 rows per step; LBO = MN-atom stride (one atom), SBO = 8-row stride).
           // Every step accumulates: the accumulator starts at the 1.5 * 2^23 bias.
-          umma_i8(tmem + 256, umma_desc(sp + kk * 32, 16, 1024, 2),
+          umma_i8(tmem + kColA + s * 128, umma_desc(sp + kk * 32, 16, 1024, 2),
                   umma_desc(sv + kk * 32 * DH, L::kTile, kRowGroup, kSwz), idesc_pv, 1u);
         }
-        umma_commit(&bars[kBarAFull]);
+        umma_commit(&bars[kBarAFull + s]);
         umma_commit(&bars[kBarVEmpty + s]);
         umma_commit(&bars[kBarPEmpty + s]);
       }
     }
-  } else if (warp < 10) {
-    // ================================================================ chain warps
+  } else {
+    // ================================================================ row workers
+    // Warp w owns 16 query rows (TMEM lanes 32 (w % 4) + 16 ((w - 2) / 4) + [0, 16)); lanes t and
+    // t + 16 of the warp share row t: lane t takes keys [0, 64) of every block's chain and
+    // channels [0, DH/2) of the fold and output, lane t + 16 keys [64, 128) and channels
+    // [DH/2, DH) (tcgen05.ld/st 16x32bx2 shapes).  The halves of a row meet by warp shuffles, so
+    // the workers never wait on each other; every wait is on an mbarrier, per warp.
+    // Iteration j runs the chain of block j, then folds block j - 1 (its A_{j-1} finished on the
+    // tensor core while the chain ran).
+    constexpr int HALF = DH / 2;
     const int q4 = warp & 3;
-    const int kh = (warp - 2) >> 2;                    // key half: keys [64 kh, 64 kh + 64)
-    const int r = q4 * 32 + lane;
-    const uint32_t lanebase = (uint32_t)(q4 * 32) << 16;
+    const int row0 = q4 * 32 + ((warp - 2) >> 2) * 16;   // first TMEM lane of this warp
+    const int kh = lane >> 4;                          // key half / channel half
+    const int r = row0 + (lane & 15);
+    const uint32_t rowt = tmem + ((uint32_t)row0 << 16);
     const uint32_t lane4 = (uint32_t)(lane & 15) << 2;
     const uint8_t* tab = reinterpret_cast<const uint8_t*>(s_t2);
     const int eqr = p.eq[(long long)qrow0 + r];
     const int32_t* ekg = p.ek + (long long)(b * p.KVH + g) * p.nblk;
+    const int32_t* evg = p.ev + (long long)(b * p.KVH + g) * p.nblk;
+    const int ev0 = SINK ? p.ev0[b * p.KVH + g] : 0;
     const uint32_t prow = (uint32_t)((r >> 3) * 1024 + (r & 7) * 128);
+    const uint32_t obase = rowt + kColO;
+    const uint64_t negM2 = f2_pack(-12582912.0f, -12582912.0f);
+    // fold state: both lanes of a row compute it identically
+    float lseg = 0.0f, lrow = 0.0f;
+    int nbrun = 0, nbrow = 0;
+    bool have_seg = false, have_row = false;
+    float* orow = MULTI ? p.orow + ((long long)qrow0 + r) * DH + kh * HALF : nullptr;
+
+    // fold of block jf: O = fl(O + f32(A) 2^-(s + e_v)), l = fl(l + l_b 2^-s), with the running
+    // maximum rescale first (reference/lssab8_golden.py:293-315); then, at a segment end, the
+    // segment -> row fold (reference/lssab8_golden.py:317-331).
+    auto fold_block = [&](int jf, int nbb, int lbt, int evj, int eh0v) -> bool {
+      const int sa = jf & 1;
+      if (!have_seg) { nbrun = nbb; have_seg = true; }
+      const int D = nbb - nbrun;
+      int sg = 0, Dr = 0;
+      if (D > 0) { Dr = D; lseg = rescale(lseg, D); nbrun = nbb; }
+      else sg = -D;
+      if (!warp_poll(&bars[kBarAFull + sa], (jf >> 1) & 1, abort_flag, p.err)) return false;
+      tc_fence_after();
+      // A block beyond the exact-skip window (sg > S_WIN) is folded with scale +0 instead of being
+      // skipped: O and l are never -0 (they start at +0, an RN sum that cancels exactly is +0, and
+      // the rescale flushes to +0), and A_b, l_b are finite, so O + (+0) x == O bit for bit.
+      const bool add = (sg <= kSWIN);
+      const float scO = add ? pow2f(-(sg + evj)) : 0.0f;
+      const uint64_t scO2 = f2_pack(scO, scO);
+      const bool resc = __any_sync(0xffffffffu, Dr > 0);  // warp-uniform
+      const RowRescale rr = row_rescale(Dr);             // identity on lanes with Dr == 0
+      // DH/2 channels per lane in passes of 32 (two TMEM round trips for DH = 128)
+      constexpr int kPass = HALF < 32 ? HALF : 32;
+#pragma unroll 1
+      for (int c0 = 0; c0 < HALF; c0 += kPass) {
+        const uint32_t abase = rowt + kColA + sa * 128 + c0;
+        const uint32_t ob = obase + c0;
+        uint32_t a[kPass], o[kPass];
+#pragma unroll
+        for (int cc = 0; cc < kPass / 16; ++cc) {
+          tmem_ld16x2<HALF>(abase + cc * 16, a + cc * 16);
+          tmem_ld16x2<HALF>(ob + cc * 16, o + cc * 16);
+        }
+        tc_wait_ld();
+#pragma unroll
+        for (int cc = 0; cc < kPass / 16; ++cc) tmem_fill16x2<HALF>(abase + cc * 16, kMagicBits);   // re-bias
+        if (resc) {
+#pragma unroll
+          for (int c = 0; c < kPass; ++c) o[c] = __float_as_uint(apply_rescale(__uint_as_float(o[c]), rr));
+        }
+        if (SINK && jf == 0 && p.T > 1) {                  // key 0's term first (B9.1); sg == 0 here
+          const float sc0 = pow2f(-ev0);
+          const uint64_t sc02 = f2_pack(sc0, sc0);
+#pragma unroll
+          for (int t = 0; t < kPass / 2; ++t) {
+            const int c = kh * HALF + c0 + 2 * t;
+            const uint64_t z = f2_pack(i2f_small(eh0v * (int)v0row[c]), i2f_small(eh0v * (int)v0row[c + 1]));
+            float lo_, hi_;
+            f2_unpack(f2_fma(z, sc02, f2_pack(__uint_as_float(o[2 * t]), __uint_as_float(o[2 * t + 1]))), lo_, hi_);
+            o[2 * t] = __float_as_uint(lo_);
+            o[2 * t + 1] = __float_as_uint(hi_);
+          }
+        }
+#pragma unroll
+        for (int t = 0; t < kPass / 2; ++t) {
+          const uint64_t x = f2_add(f2_pack(__uint_as_float(a[2 * t]), __uint_as_float(a[2 * t + 1])), negM2);
+          float lo_, hi_;
+          f2_unpack(f2_fma(x, scO2, f2_pack(__uint_as_float(o[2 * t]), __uint_as_float(o[2 * t + 1]))), lo_, hi_);
+          o[2 * t] = __float_as_uint(lo_);
+          o[2 * t + 1] = __float_as_uint(hi_);
+        }
+#pragma unroll
+        for (int cc = 0; cc < kPass / 16; ++cc) tmem_st16x2<HALF>(ob + cc * 16, o + cc * 16);
+      }
+      tc_wait_st();
+      tc_fence_before();
+      mbar_arrive(&bars[kBarAEmpty + sa]);
+      lseg = fold_term(lseg, lbt, add ? pow2f(-sg) : 0.0f);
+      if (MULTI && (((jf + 1) % kSEG == 0) || (jf == nb - 1))) {
+        // segment -> row: the same three rules (reference/lssab8_golden.py:317-331)
+        int D2 = 0, s2 = 0;
+        const bool first = !have_row;
+        if (first) { nbrow = nbrun; have_row = true; }
+        else { D2 = nbrun - nbrow; if (D2 > 0) { lrow = rescale(lrow, D2); nbrow = nbrun; } else { s2 = -D2; } }
+#pragma unroll 1
+        for (int cc = 0; cc < HALF / 16; ++cc) {
+          uint32_t y[16];
+          tmem_ld16x2<HALF>(obase + cc * 16, y);
+          tc_wait_ld();
+#pragma unroll
+          for (int c = 0; c < 16; ++c) {
+            float* pr = orow + cc * 16 + c;
+            const float seg = __uint_as_float(y[c]);
+            if (first) *pr = rescale(seg, 0);
+            else {
+              float x = *pr;
+              if (D2 > 0) x = rescale(x, D2);
+              if (s2 <= kSWIN) x = __fadd_rn(x, rescale(seg, s2));
+              *pr = x;
+            }
+          }
+          tmem_fill16x2<HALF>(obase + cc * 16, 0u);
+        }
+        tc_wait_st();
+        if (first) lrow = rescale(lseg, 0);
+        else if (s2 <= kSWIN) lrow = __fadd_rn(lrow, rescale(lseg, s2));
+        lseg = 0.0f;
+        have_seg = false;
+      }
+      return true;
+    };
+
+    bool ok = true;
+    int nb_prev = 0, ev_prev = 0, lbt_prev = 0, eh0_row = 0;
+    int ek_next = ekg[0], ev_next = evg[0];            // e_k, e_v one block ahead
     for (int j = 0; j < nb; ++j) {
+      const int ekj = ek_next, evj = ev_next;
+      if (j + 1 < nb) { ek_next = ekg[j + 1]; ev_next = evg[j + 1]; }
       const int s = j & 1;
       const uint32_t ph = (j >> 1) & 1;
-      if (!group_wait(&bars[kBarSFull + s], ph, warp == 2 && lane == 0, 1, 256, abort_flag, p.err)) break;
+      if (!warp_poll(&bars[kBarSFull], j & 1, abort_flag, p.err)) { ok = false; break; }
       tc_fence_after();
       const bool diag = (j == tile);                     // key c of the diagonal block visible iff c <= r
-      const uint32_t sbase = tmem + lanebase + s * 128 + kh * 64;
-      // pass 1: this thread's 64 scores into registers (one TMEM round trip; S is free for the
-      // next QK as soon as they have landed), the exact max over its visible keys, then the row's
+      // pass 1: this lane's 64 scores into registers (one TMEM round trip; S is free for the
+      // next QK as soon as they have landed) and the exact max over its visible keys
       uint32_t v[64];
-      tmem_ld16(sbase, v);
-      tmem_ld16(sbase + 16, v + 16);
-      tmem_ld16(sbase + 32, v + 32);
-      tmem_ld16(sbase + 48, v + 48);
+      const uint32_t sbase = rowt + kColS;
+      tmem_ld16x2<64>(sbase, v);
+      tmem_ld16x2<64>(sbase + 16, v + 16);
+      tmem_ld16x2<64>(sbase + 32, v + 32);
+      tmem_ld16x2<64>(sbase + 48, v + 48);
       tc_wait_ld();
       tc_fence_before();
-      mbar_arrive(&bars[kBarSEmpty + s]);
+      mbar_arrive(&bars[kBarSEmpty]);
       if (diag) {
 #pragma unroll
         for (int c = 0; c < 64; ++c) if (kh * 64 + c > r) v[c] = 0x80000000u;
@@ -281,17 +416,15 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
 #pragma unroll
       for (int c = 3; c < 63; c += 2) m = __vimax3_s32(m, (int)v[c], (int)v[c + 1]);
       m = max(m, (int)v[63]);
-      pmax[(s * 2 + kh) * 128 + r] = m;
-      if (bar_any(1, 256, *abort_flag != 0)) break;     // the two halves of each row meet here
-      m = max(pmax[(s * 2) * 128 + r], pmax[(s * 2 + 1) * 128 + r]);
-      const uint32_t G = g_fold(p.gbase, eqr + ekg[j]);
+      m = max(m, __shfl_xor_sync(0xffffffffu, m, 16));  // the row's max over both key halves
+      const uint32_t G = g_fold(p.gbase, eqr + ekj);
       const int nbv = nb_of(m, G);
       const uint32_t NBlo = (uint32_t)nbv << kBHI;
       const int lg = 31 - __clz((int)G);
       const int dm = 1 << max(0, 30 - lg);              // dm * G in [2^30, 2^31): >= 9 doublings
       const int lo = m - dm;
       const uint32_t negG = 0u - G;
-      if (!group_wait(&bars[kBarPEmpty + s], ph ^ 1, warp == 2 && lane == 0, 1, 256, abort_flag, p.err)) break;
+      if (!warp_poll(&bars[kBarPEmpty + s], ph ^ 1, abort_flag, p.err)) { ok = false; break; }
       const uint32_t pbase = smem_u32(smem + L::kP + s * 16384) + prow;
       uint32_t lb = 0, eh0 = 0;
       // pass 2: the chain and the u8 P half-row, 16 keys (one 16-byte P chunk) at a time
@@ -305,10 +438,10 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
           for (int x = 0; x < 4; ++x) {
             const int sc = max((int)v[cc * 16 + qq * 4 + x], lo);
             uint32_t d = NBlo + (uint32_t)sc * negG;       // exact: d < 2^32
-            d = min(d, kDClamp);                           // index <= 1152 (T2 = 0 from 1152 on)
-            e[x] = tab[((d >> (kIdxShift - 6)) & ~63u) | lane4];
+            const uint32_t ix = min(d, kDClamp) >> kIdxShift;  // index <= 1152 (T2 = 0 from 1152 on)
+            e[x] = tab[ix * p.mul_entry + lane4];            // entry ix, this lane's copy
           }
-          w[qq] = __byte_perm(__byte_perm(e[0], e[1], 0x0040), __byte_perm(e[2], e[3], 0x0040), 0x5410);
+          w[qq] = e[0] + e[1] * p.mul_b1 + e[2] * p.mul_b2 + e[3] * p.mul_b3;
           lb = __dp4a(w[qq], 0x01010101u, lb);
         }
         const int chunk = kh * 4 + cc;
@@ -317,182 +450,47 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
       }
       fence_async_smem();
       mbar_arrive(&bars[kBarPFull + s]);
-      if (!group_wait(&bars[kBarIEmpty + s], ph ^ 1, warp == 2 && lane == 0, 1, 256, abort_flag, p.err)) break;
-      int* slot = info + (s * 128 + r) * 4;
-      if (kh == 0) { slot[0] = nbv; slot[1] = (int)lb; slot[2] = (int)eh0; }
-      else { slot[3] = (int)lb; }
-      mbar_arrive(&bars[kBarIFull + s]);
+      const int lbt = (int)lb + __shfl_xor_sync(0xffffffffu, (int)lb, 16);   // the row's l_b
+      if (SINK && j == 0) eh0_row = __shfl_sync(0xffffffffu, (int)eh0, lane & 15);
+      if (j > 0 && !fold_block(j - 1, nb_prev, lbt_prev, ev_prev, eh0_row)) { ok = false; break; }
+      nb_prev = nbv;
+      lbt_prev = lbt;
+      ev_prev = evj;
     }
-  } else {
-    // ================================================================ fold warps
-    const int q4 = warp & 3;
-    const int r = q4 * 32 + lane;
-    const uint32_t rowb = tmem + ((uint32_t)(q4 * 32) << 16);
-    const uint32_t abase = rowb + 256, obase = rowb + 384;
-    const int32_t* evg = p.ev + (long long)(b * p.KVH + g) * p.nblk;
-    const int ev0 = SINK ? p.ev0[b * p.KVH + g] : 0;
-    const uint64_t negM2 = f2_pack(-12582912.0f, -12582912.0f);
-    float lseg = 0.0f, lrow = 0.0f;
-    int nbrun = 0, nbrow = 0;
-    bool have_seg = false, have_row = false;
-    bool ok = true;
-    float* orow = MULTI ? p.orow + ((long long)qrow0 + r) * DH : nullptr;
-    for (int j = 0; j < nb; ++j) {
-      const int s = j & 1;
-      const uint32_t ph = (j >> 1) & 1;
-      if (!group_wait(&bars[kBarIFull + s], ph, warp == 10 && lane == 0, 2, kFoldThreads, abort_flag, p.err)) {
-        ok = false;
-        break;
-      }
-      const int4 inf = *reinterpret_cast<const int4*>(info + (s * 128 + r) * 4);
-      mbar_arrive(&bars[kBarIEmpty + s]);
-      const int nbb = inf.x;
-      if (!have_seg) { nbrun = nbb; have_seg = true; }
-      const int D = nbb - nbrun;
-      // Per-row decisions (rescale by D, add or skip the block) stay in arithmetic: every
-      // tcgen05.ld/st below is warp-collective (.sync.aligned) and runs on all 32 lanes.
-      int sg = 0, Dr = 0;
-      if (D > 0) {                                     // a new running max: rescale O and l
-        Dr = D;
-        lseg = rescale(lseg, D);
-        nbrun = nbb;
-      } else {
-        sg = -D;
-      }
-      if (!group_wait(&bars[kBarAFull], j & 1, warp == 10 && lane == 0, 2, kFoldThreads, abort_flag, p.err)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      {
-        const bool add = (sg <= kSWIN);
-        const float scO = pow2f(-(min(sg, kSWIN) + evg[j]));
-        const uint64_t scO2 = f2_pack(scO, scO);
-        const bool sink_term = SINK && j == 0 && p.T > 1;
-        const float sc0 = pow2f(-(min(sg, kSWIN) + ev0));
-        const uint64_t sc02 = f2_pack(sc0, sc0);
-        // 16-column chunks, software-pipelined: chunk cc + 1's TMEM loads are in flight while
-        // chunk cc is folded (tcgen05.wait::ld waits for every earlier load, so the loads of the
-        // next chunk are issued only after the current chunk's wait)
-        uint32_t an[16], on[16];
-        tmem_ld16(abase, an);
-        tmem_ld16(obase, on);
-#pragma unroll 1
-        for (int cc = 0; cc < DH / 16; ++cc) {
-          uint32_t a[16], o[16];
-          tc_wait_ld();
-#pragma unroll
-          for (int c = 0; c < 16; ++c) { a[c] = an[c]; o[c] = on[c]; }
-          tmem_fill16(abase + cc * 16, kMagicBits);          // re-bias for the next PV
-          if (cc + 1 < DH / 16) {
-            tmem_ld16(abase + (cc + 1) * 16, an);
-            tmem_ld16(obase + (cc + 1) * 16, on);
-          }
-          if (Dr > 0) {
-#pragma unroll
-            for (int c = 0; c < 16; ++c) o[c] = __float_as_uint(rescale(__uint_as_float(o[c]), Dr));
-          }
-          if (add) {
-#pragma unroll
-            for (int t = 0; t < 8; ++t) {
-              uint64_t o2 = f2_pack(__uint_as_float(o[2 * t]), __uint_as_float(o[2 * t + 1]));
-              if (sink_term) {                                // key 0's term first (B9.1)
-                const int c = cc * 16 + 2 * t;
-                const uint64_t z = f2_pack(i2f_small(inf.z * (int)v0row[c]), i2f_small(inf.z * (int)v0row[c + 1]));
-                o2 = f2_fma(z, sc02, o2);
-              }
-              const uint64_t x = f2_add(f2_pack(__uint_as_float(a[2 * t]), __uint_as_float(a[2 * t + 1])), negM2);
-              o2 = f2_fma(x, scO2, o2);
-              float lo_, hi_;
-              f2_unpack(o2, lo_, hi_);
-              o[2 * t] = __float_as_uint(lo_);
-              o[2 * t + 1] = __float_as_uint(hi_);
-            }
-          }
-          tmem_st16(obase + cc * 16, o);
-        }
-        if (add) lseg = fold_term(lseg, inf.y + inf.w, pow2f(-sg));
-      }
-      tc_wait_st();
-      tc_fence_before();
-      mbar_arrive(&bars[kBarAEmpty]);
-      if (MULTI && (((j + 1) % kSEG == 0) || (j == nb - 1))) {
-        // segment -> row: the same three rules (reference/lssab8_golden.py:317-331)
-        int D2 = 0, s2 = 0;
-        const bool first = !have_row;
-        if (first) { nbrow = nbrun; have_row = true; }
-        else { D2 = nbrun - nbrow; if (D2 > 0) { lrow = rescale(lrow, D2); nbrow = nbrun; } else { s2 = -D2; } }
-#pragma unroll 1
-        for (int cc = 0; cc < DH / 16; ++cc) {
-          uint32_t o[16];
-          tmem_ld16(obase + cc * 16, o);
-          tc_wait_ld();
-#pragma unroll
-          for (int c = 0; c < 16; ++c) {
-            float* pr = orow + cc * 16 + c;
-            const float seg = __uint_as_float(o[c]);
-            if (first) *pr = rescale(seg, 0);
-            else {
-              float x = *pr;
-              if (D2 > 0) x = rescale(x, D2);
-              if (s2 <= kSWIN) x = __fadd_rn(x, rescale(seg, s2));
-              *pr = x;
-            }
-          }
-          tmem_fill16(obase + cc * 16, 0u);
-        }
-        tc_wait_st();
-        if (first) lrow = rescale(lseg, 0);
-        else if (s2 <= kSWIN) lrow = __fadd_rn(lrow, rescale(lseg, s2));
-        lseg = 0.0f;
-        have_seg = false;
-      }
-    }
-    if constexpr (!MULTI) lrow = rescale(lseg, 0);   // a single segment: O_row = 0 + rescale(O_seg, 0)
-    lrow_s[r] = lrow;
-    role_fail = !ok;
-  }
+    if (ok) ok = fold_block(nb - 1, nb_prev, lbt_prev, ev_prev, eh0_row);
 
-  if (warp >= 2) {
-    // ================================================================ epilogue
-    // out = O_row / l_row (one RN division per element; l_row == 0 -> 0), shared by the chain
-    // and fold warps: TMEM lanes of warp w are rows 32 (w % 4) .. + 31, and the DH / 16 column
-    // chunks are split between the three warps of each row quarter.  The OR-barrier makes the
-    // skip decision (any role gave up) identical on all 384 threads, so the warp-collective
-    // TMEM loads below run on every lane or on none.
-    tc_fence_before();
-    const bool skip = bar_any(3, 384, role_fail || *abort_flag != 0);
-    tc_fence_after();
-    if (!skip) {
-      constexpr int kCh = DH / 16, kC1 = (kCh + 2) / 3;
-      const int q4 = warp & 3;
-      const int role = (warp < 10) ? ((warp - 2) >> 2) : 2;
-      const int c_lo = role * kC1, c_hi = min(kCh, c_lo + kC1);
-      const int r = q4 * 32 + lane;
+    // ---- epilogue: out = O_row / l_row (one RN division per element; l_row == 0 -> 0).
+    // `ok` is warp-uniform (every wait is decided for the whole warp), so the warp-collective
+    // TMEM loads run on every lane or on none; rows past T skip only the store.
+    if (ok) {
+      if constexpr (!MULTI) lrow = rescale(lseg, 0);   // a single segment: O_row = 0 + rescale(O_seg, 0)
       const int i = tile * 128 + r;
       const bool live = (i < p.T);
-      const float lr = lrow_s[r];
-      const bool nz = (lr != 0.0f);
-      const float rl = nz ? __frcp_rn(lr) : 0.0f;
-      const uint32_t obase = tmem + ((uint32_t)(q4 * 32) << 16) + 384;
-      OutT* dst = reinterpret_cast<OutT*>(p.out) + b * p.os0 + (long long)i * p.os1 + h * p.os2;
-      const float* orow = MULTI ? p.orow + ((long long)qrow0 + r) * DH : nullptr;
+      const bool nz = (lrow != 0.0f);
+      const float rl = nz ? __frcp_rn(lrow) : 0.0f;
+      const bool row_fast = nz && div_window(lrow);
+      OutT* dst = reinterpret_cast<OutT*>(p.out) + b * p.os0 + (long long)i * p.os1 + h * p.os2 + kh * HALF * p.os3;
 #pragma unroll 1
-      for (int cc = c_lo; cc < c_hi; ++cc) {
+      for (int cc = 0; cc < HALF / 16; ++cc) {
         float q[16];
         if constexpr (!MULTI) {
           uint32_t y[16];
-          tmem_ld16(obase + cc * 16, y);
+          tmem_ld16x2<HALF>(obase + cc * 16, y);
           tc_wait_ld();
 #pragma unroll
-          for (int c = 0; c < 16; ++c) q[c] = rescale(__uint_as_float(y[c]), 0);
+          for (int c = 0; c < 16; ++c) q[c] = __uint_as_float(y[c]);
         } else {
 #pragma unroll
           for (int c = 0; c < 16; ++c) q[c] = live ? orow[cc * 16 + c] : 0.0f;
         }
         if (live) {
 #pragma unroll
-          for (int c = 0; c < 16; ++c) q[c] = nz ? div_rn_shared(q[c], lr, rl) : 0.0f;
+          for (int c = 0; c < 16; ++c) {
+            // fast path: both operands inside the Markstein window (then O_seg is normal and
+            // rescale(O_seg, 0) is O_seg itself); anything else takes the IEEE division
+            if (row_fast && div_window(q[c])) q[c] = div_markstein(q[c], lrow, rl);
+            else q[c] = nz ? div_rn_ieee(MULTI ? q[c] : rescale(q[c], 0), lrow) : 0.0f;
+          }
           store_chunk<OutT, 16>(dst + cc * 16 * p.os3, p.os3, q);
         }
       }

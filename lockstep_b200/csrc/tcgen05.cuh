@@ -8,7 +8,7 @@ namespace lssab8 {
 
 // The 1,152 live entries of T2 (k = 0 .. 1151; every later entry is 0), generated from the
 // contract's definition by gen_t2.py and pinned by digest.
-__device__ const uint8_t kT2Live[kTabLive] = {
+__device__ __align__(16) const uint8_t kT2Live[kTabLive] = {
 #include "t2_table.inc"
 };
 
@@ -89,6 +89,31 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* v) {
       "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};"
       ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
         "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]) : "memory");
+}
+
+// 16 lanes x 2 halves: thread t < 16 accesses lane (base + t) at columns [col, col + 16), thread
+// t + 16 the same lane at columns [col + SPLIT, col + SPLIT + 16) -- the two halves of one row
+// in one warp.
+template <int SPLIT>
+__device__ __forceinline__ void tmem_ld16x2(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.16x32bx2.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16], %17;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr), "n"(SPLIT));
+}
+template <int SPLIT>
+__device__ __forceinline__ void tmem_st16x2(uint32_t taddr, const uint32_t* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.16x32bx2.x16.b32 [%0], %17, {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};"
+      ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+        "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "n"(SPLIT) : "memory");
+}
+template <int SPLIT>
+__device__ __forceinline__ void tmem_fill16x2(uint32_t taddr, uint32_t v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.16x32bx2.x16.b32 [%0], %2, {%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1};"
+      ::"r"(taddr), "r"(v), "n"(SPLIT) : "memory");
 }
 
 // store the same 32-bit value into 16 consecutive columns of this warp's 32 lanes
