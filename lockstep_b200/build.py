@@ -11,7 +11,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "liblssab8_b200.so")
-SOURCES = ["capi.cu", "common.cuh", "tcgen05.cuh", "prep.cuh", "prefill.cuh", "decode.cuh", "t2_table.inc"]
+SOURCES = ["capi.cu", "common.cuh", "tcgen05.cuh", "prep.cuh", "prefill.cuh", "decode.cuh", "decode_tc.cuh", "t2_table.inc"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

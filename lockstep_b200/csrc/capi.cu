@@ -17,6 +17,7 @@
 #include "prep.cuh"
 #include "prefill.cuh"
 #include "decode.cuh"
+#include "decode_tc.cuh"
 
 using namespace lssab8;
 
@@ -30,6 +31,7 @@ __device__ int g_dev_err;
 struct DevState {
   int* err = nullptr;
   bool prefill_attr_set = false;
+  int num_sms = 0;
 };
 std::mutex g_mu;
 DevState g_dev[64];
@@ -44,6 +46,8 @@ int dev_state(DevState** out) {
     if (cudaGetSymbolAddress(&p, g_dev_err) != cudaSuccess) return kErrCuda;
     st.err = static_cast<int*>(p);
   }
+  if (st.num_sms <= 0 && cudaDeviceGetAttribute(&st.num_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return kErrCuda;
   *out = &st;
   return kOk;
 }
@@ -68,12 +72,14 @@ int get_encode() {
 }
 
 // rows x dh int8 matrix, box 128 rows x dh, swizzle = dh bytes
-int make_tmap(CUtensorMap* tm, const void* base, long long rows, int dh) {
+// 2-D int8 tensor map over [rows, dh] (row pitch dh bytes), boxes of box_rows x dh, swizzled for
+// the UMMA K-major layouts (128B swizzle at dh 128, 64B at dh 64).
+int make_tmap(CUtensorMap* tm, const void* base, long long rows, int dh, int box_rows = 128) {
   if (get_encode() != kOk) return kErrCuda;
   if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) return kErrArg;
   cuuint64_t dims[2] = {(cuuint64_t)dh, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)dh};
-  cuuint32_t box[2] = {(cuuint32_t)dh, 128};
+  cuuint32_t box[2] = {(cuuint32_t)dh, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = g_encode(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -213,6 +219,33 @@ int launch_decode_out(int out_dtype, const DecodeArgs& a, int max_splits, cudaSt
     case kF32: return launch_decode_t<DH, SINK, float>(a, max_splits, st);
     case kF16: return launch_decode_t<DH, SINK, __half>(a, max_splits, st);
     case kBF16: return launch_decode_t<DH, SINK, __nv_bfloat16>(a, max_splits, st);
+    default: return kErrArg;
+  }
+}
+
+template <bool SINK, typename OutT>
+int launch_decode_tc_t(const DecodeArgs& a, int max_splits, int num_sms, cudaStream_t st) {
+  CUtensorMap tk, tq;
+  int rc;
+  if ((rc = make_tmap(&tk, a.k8p, (long long)a.num_pages * a.KVH * 16, 128, 16))) return rc;
+  if ((rc = make_tmap(&tq, a.q8, (long long)a.B * a.H, 128, 16))) return rc;
+  const int smem = DecTcSmem::kBytes + 1024;
+  auto kfn = decode_tc_kernel<SINK, OutT>;
+  if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return kErrCuda;
+  const long long items = (long long)a.B * a.KVH * max_splits;
+  const int grid = (int)std::min<long long>(items, (long long)std::max(num_sms, 1));
+  kfn<<<grid, kDecThreads, smem, st>>>(tk, tq, a, max_splits);
+  if ((rc = launch_rc())) return rc;
+  decode_merge_kernel<SINK, OutT><<<dim3(a.KVH, a.B), 128, 0, st>>>(a);
+  return launch_rc();
+}
+
+template <bool SINK>
+int launch_decode_tc_out(int out_dtype, const DecodeArgs& a, int max_splits, int num_sms, cudaStream_t st) {
+  switch (out_dtype) {
+    case kF32: return launch_decode_tc_t<SINK, float>(a, max_splits, num_sms, st);
+    case kF16: return launch_decode_tc_t<SINK, __half>(a, max_splits, num_sms, st);
+    case kBF16: return launch_decode_tc_t<SINK, __nv_bfloat16>(a, max_splits, num_sms, st);
     default: return kErrArg;
   }
 }
@@ -509,8 +542,8 @@ int lssab8_decode(const void* q, int dtype, const int64_t* qs, int B, int H, int
   a.gbase = gbase_of(dh);
   a.err = ds->err;
   const int max_splits = (max_blocks + split_blocks - 1) / split_blocks;
-  if (dh == 128) return sink ? launch_decode_out<128, true>(out_dtype, a, max_splits, s)
-                             : launch_decode_out<128, false>(out_dtype, a, max_splits, s);
+  if (dh == 128) return sink ? launch_decode_tc_out<true>(out_dtype, a, max_splits, ds->num_sms, s)
+                             : launch_decode_tc_out<false>(out_dtype, a, max_splits, ds->num_sms, s);
   return sink ? launch_decode_out<64, true>(out_dtype, a, max_splits, s)
               : launch_decode_out<64, false>(out_dtype, a, max_splits, s);
 }
@@ -575,8 +608,8 @@ int lssab8_decode_noalloc(const void* q, int dtype, const int64_t* qs, int B, in
   a.gbase = gbase_of(dh);
   a.err = ds->err;
   const int max_splits = (max_blocks + split_blocks - 1) / split_blocks;
-  if (dh == 128) return sink ? launch_decode_out<128, true>(out_dtype, a, max_splits, s)
-                             : launch_decode_out<128, false>(out_dtype, a, max_splits, s);
+  if (dh == 128) return sink ? launch_decode_tc_out<true>(out_dtype, a, max_splits, ds->num_sms, s)
+                             : launch_decode_tc_out<false>(out_dtype, a, max_splits, ds->num_sms, s);
   return sink ? launch_decode_out<64, true>(out_dtype, a, max_splits, s)
               : launch_decode_out<64, false>(out_dtype, a, max_splits, s);
 }

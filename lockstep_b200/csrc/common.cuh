@@ -200,6 +200,13 @@ __device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile("{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+               : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+  return ok != 0;
+}
+
 // try_wait that may suspend the thread for up to ~20 us while the phase is incomplete, so a
 // waiting warp issues a handful of instructions instead of spinning.
 __device__ __forceinline__ bool mbar_try_suspend(uint64_t* bar, uint32_t parity) {
@@ -220,8 +227,10 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   uint64_t t0 = globaltimer();
   for (uint32_t it = 0;; ++it) {
     if (sleep_ns) {
+      // non-blocking test between naps: a suspended try_wait can sleep past a phase completed
+      // by tcgen05.commit, which is how the pipelines here release their buffers
       __nanosleep(sleep_ns);
-      if (mbar_try(bar, parity)) return true;
+      if (mbar_test(bar, parity)) return true;
     } else if (mbar_try_suspend(bar, parity)) {
       return true;
     }
@@ -236,12 +245,6 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
-__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile("{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
-               : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
-  return ok != 0;
-}
 
 // Non-blocking poll of an mbarrier phase (no hardware suspension: arrivals made by
 // tcgen05.commit are observed as soon as they land).  Same bounds as mbar_wait.

@@ -1,0 +1,356 @@
+// LSSA-B8 split-KV decode on sm_100a, tensor-core form (dh = 128).
+//
+// Same contract and workspace as decode_kernel (decode.cuh): every 128-key block of a sequence
+// yields EXACT integer block partials (A_b = eh . v8 per head and channel, NB_b, l_b, eh0), and
+// the last CTA of a (sequence, kv head) refolds all blocks in ascending order
+// (reference/lssab8_golden.py:350-394).  What changes is how the partials are produced:
+//
+//   * persistent CTAs walk the work items (sequence, kv head, split) and their blocks as one
+//     stream, so the TMA ring never drains between items;
+//   * warp 0 (one thread) streams each block's 8 key pages with cp.async.bulk.tensor (the tensor
+//     map swizzles them into the SW128 K-major layout) and its 8 transposed value pages with
+//     plain cp.async.bulk into a kDecStages-deep ring (no multicast);
+//   * warp 1 (one thread) owns 64 TMEM columns and issues both contractions on the tensor core,
+//     kind::i8 with the GQA group padded to N = 16:
+//       S^T[key, head] = K_b[128 x 128] . Q^T     (s8 x s8, both K-major SW128)
+//       A^T[ch, head]  = V_b^T[128 x 128] . P^T   (s8 x u8; a value page [ch][16 keys] is exactly
+//                                                  8-row x 16-byte core matrices, so V^T is read
+//                                                  in place with no swizzle: LBO = one page)
+//   * warps 2-5 (128 threads, thread = TMEM lane = key for S, channel for A) compute the block
+//     max per head (redux.sync + one named barrier), NB, the 32-bit chain and the T2 gather from a
+//     zero-padded table indexed by d >> 19, write P^T in the core-matrix layout, sum l_b with
+//     redux.sync and shared atomics, and store the partials.
+//   * the refold of each (sequence, kv head) runs afterwards as its own small kernel
+//     (decode_merge_kernel), so no streaming CTA ever stalls on a merge.
+#pragma once
+#include "decode.cuh"
+
+namespace lssab8 {
+
+constexpr int kDecStages = 4;
+constexpr int kDecThreads = 192;   // warp 0 TMA, warp 1 MMA + TMEM, warps 2-5 workers
+constexpr uint32_t kDecTmemCols = 64;
+
+struct DecTcSmem {
+  static constexpr int kPage = 16 * 128;                  // one page of one kv head (dh 128), bytes
+  static constexpr int kStage = 16 * kPage;               // 8 key pages, then 8 value pages
+  static constexpr int kQ = kDecStages * kStage;          // 2 x Q^T [16 rows x 128 B], SW128
+  static constexpr int kP = kQ + 2 * 2048;                // 2 x P^T [16 heads x 128 keys], core matrices
+  static constexpr int kTab = kP + 2 * 2048;              // T2, zero-padded to 8192 entries
+  static constexpr int kRedMax = kTab + kTabPad;          // [2][4 warps][8 heads] block max
+  static constexpr int kLbSum = kRedMax + 2 * 4 * 8 * 4;  // [2][8] l_b
+  static constexpr int kNb = kLbSum + 2 * 8 * 4;          // [2][8] NB_b
+  static constexpr int kEh0 = kNb + 2 * 8 * 4;            // [8] key 0's weight (sink, block 0)
+  static constexpr int kBar = kEh0 + 8 * 4 + 32;          // mbarriers
+  static constexpr int kMisc = kBar + 32 * 8;             // tmem base, abort flag
+  static constexpr int kBytes = kMisc + 64;
+};
+
+enum DecBar : int {
+  kDFull = 0, kDEmpty = kDecStages, kDQFull = 2 * kDecStages, kDQEmpty = kDQFull + 2, kDSFull = kDQEmpty + 2,
+  kDSEmpty = kDSFull + 2, kDPFull = kDSEmpty + 2, kDPEmpty = kDPFull + 2, kDAFull = kDPEmpty + 2,
+  kDAEmpty = kDAFull + 2, kDNumBars = kDAEmpty + 2
+};
+
+struct DecItem {
+  int b, g, blo, bhi, L;
+};
+
+// Work item it = (b * KVH + g) * max_splits + split: 1 = blocks to process, 0 = the split lies
+// past the sequence, 2 = the lattice arrays are too short for the sequence (an error).
+__device__ __forceinline__ int dec_item(const DecodeArgs& p, int max_splits, int it, DecItem& w) {
+  const int split = it % max_splits;
+  const int bg = it / max_splits;
+  w.g = bg % p.KVH;
+  w.b = bg / p.KVH;
+  w.L = p.seq_lens[w.b];
+  const int nblk = (w.L + kKB - 1) / kKB;
+  w.blo = split * p.split_blocks;
+  w.bhi = min(nblk, w.blo + p.split_blocks);
+  if (w.L <= 0 || w.blo >= w.bhi) return 0;
+  return (nblk <= p.max_blocks && (w.L + 15) / 16 <= p.max_pages) ? 1 : 2;
+}
+
+__device__ __forceinline__ uint32_t redux_max_s32(int v) {
+  int r;
+  asm volatile("redux.sync.max.s32 %0, %1, 0xffffffff;" : "=r"(r) : "r"(v));
+  return (uint32_t)r;
+}
+__device__ __forceinline__ uint32_t redux_add_u32(uint32_t v) {
+  uint32_t r;
+  asm volatile("redux.sync.add.u32 %0, %1, 0xffffffff;" : "=r"(r) : "r"(v));
+  return r;
+}
+
+template <bool SINK, typename OutT>
+__global__ void __launch_bounds__(kDecThreads, 1)
+decode_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_q,
+                 const DecodeArgs p, int max_splits) {
+  using L = DecTcSmem;
+  constexpr int DH = 128;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
+  uint8_t* tab = smem + L::kTab;
+  int* redmax = reinterpret_cast<int*>(smem + L::kRedMax);
+  uint32_t* lbsum = reinterpret_cast<uint32_t*>(smem + L::kLbSum);
+  int* nbs = reinterpret_cast<int*>(smem + L::kNb);
+  int* eh0s = reinterpret_cast<int*>(smem + L::kEh0);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMisc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kMisc + 8);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int total = p.B * p.KVH * max_splits;
+  const int gq = p.group;
+
+  for (int i = threadIdx.x; i < kTabPad; i += blockDim.x) tab[i] = (i < kTabLive) ? kT2Live[i] : 0;
+  for (int i = threadIdx.x; i < 2 * 8; i += blockDim.x) lbsum[i] = 0u;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kDecStages; ++s) { mbar_init(&bars[kDFull + s], 1); mbar_init(&bars[kDEmpty + s], 1); }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bars[kDQFull + s], 1);  mbar_init(&bars[kDQEmpty + s], 1);
+      mbar_init(&bars[kDSFull + s], 1);  mbar_init(&bars[kDSEmpty + s], 128);
+      mbar_init(&bars[kDPFull + s], 128); mbar_init(&bars[kDPEmpty + s], 1);
+      mbar_init(&bars[kDAFull + s], 1);  mbar_init(&bars[kDAEmpty + s], 128);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                 ::"r"(smem_u32(tmem_slot)), "r"(kDecTmemCols) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ================================================================ TMA producer
+    if (lane == 0) {
+      int jj = 0, ii = 0;
+      bool ok = true;
+      for (int it = blockIdx.x; ok && it < total; it += gridDim.x) {
+        DecItem w;
+        if (dec_item(p, max_splits, it, w) != 1) continue;
+        const int qb = ii & 1;
+        if (!mbar_wait(&bars[kDQEmpty + qb], ((ii >> 1) & 1) ^ 1, abort_flag, p.err, 128)) { ok = false; break; }
+        mbar_expect_tx(&bars[kDQFull + qb], 2048);
+        tma_load_2d(smem + L::kQ + qb * 2048, &tm_q, 0, w.b * p.H + w.g * gq, &bars[kDQFull + qb]);
+        const int32_t* bt = p.block_table + (long long)w.b * p.max_pages;
+        for (int blk = w.blo; blk < w.bhi; ++blk, ++jj) {
+          const int st = jj % kDecStages;
+          if (!mbar_wait(&bars[kDEmpty + st], ((jj / kDecStages) & 1) ^ 1, abort_flag, p.err, 128)) { ok = false; break; }
+          const int npg = min(8, (w.L - blk * kKB + 15) / 16);
+          int pg[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) pg[i] = (i < npg) ? bt[blk * 8 + i] : 0;
+          mbar_expect_tx(&bars[kDFull + st], (uint32_t)(npg * 2 * L::kPage));
+          uint8_t* kdst = smem + st * L::kStage;
+          uint8_t* vdst = kdst + 8 * L::kPage;
+          for (int i = 0; i < npg; ++i) {
+            int q = pg[i];
+            if (q < 0 || q >= p.num_pages) { atomicOr(p.err, kDevBadPage); q = 0; }
+            const long long prow = (long long)q * p.KVH + w.g;
+            tma_load_2d(kdst + i * L::kPage, &tm_k, 0, (int)(prow * 16), &bars[kDFull + st]);
+            bulk_g2s(vdst + i * L::kPage, p.v8p + prow * L::kPage, L::kPage, &bars[kDFull + st]);
+          }
+        }
+        ++ii;
+      }
+    }
+  } else if (warp == 1) {
+    // ================================================================ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc_qk = idesc_i8(1, 1, 0, 128, 16);
+      constexpr uint32_t idesc_pv = idesc_i8(1, 0, 0, 128, 16);
+      int jj = 0, ii = 0;
+      int pend = -1;                                   // block whose PV is still to issue
+      bool ok = true;
+      auto issue_pv = [&](int jb) -> bool {
+        const int ab = jb & 1, st = jb % kDecStages;
+        if (!mbar_poll(&bars[kDPFull + ab], (jb >> 1) & 1, abort_flag, p.err)) return false;
+        if (!mbar_poll(&bars[kDAEmpty + ab], ((jb >> 1) & 1) ^ 1, abort_flag, p.err)) return false;
+        tc_fence_after();
+        const uint32_t sv = smem_u32(smem + st * L::kStage + 8 * L::kPage);
+        const uint32_t sp = smem_u32(smem + L::kP + ab * 2048);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)   // 32 keys = 2 pages (A) / 2 core matrices (B) per step
+          umma_i8(tmem + 32 + ab * 16, umma_desc(sv + kk * 2 * L::kPage, L::kPage, 128, 0),
+                  umma_desc(sp + kk * 2 * 256, 256, 128, 0), idesc_pv, kk > 0);
+        umma_commit(&bars[kDAFull + ab]);
+        umma_commit(&bars[kDEmpty + st]);
+        umma_commit(&bars[kDPEmpty + ab]);
+        return true;
+      };
+      for (int it = blockIdx.x; ok && it < total; it += gridDim.x) {
+        DecItem w;
+        if (dec_item(p, max_splits, it, w) != 1) continue;
+        const int qb = ii & 1;
+        if (!mbar_poll(&bars[kDQFull + qb], (ii >> 1) & 1, abort_flag, p.err)) { ok = false; break; }
+        const uint32_t sq = smem_u32(smem + L::kQ + qb * 2048);
+        for (int blk = w.blo; blk < w.bhi; ++blk, ++jj) {
+          const int st = jj % kDecStages, sb = jj & 1;
+          if (!mbar_poll(&bars[kDFull + st], (jj / kDecStages) & 1, abort_flag, p.err)) { ok = false; break; }
+          if (!mbar_poll(&bars[kDSEmpty + sb], ((jj >> 1) & 1) ^ 1, abort_flag, p.err)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t sk = smem_u32(smem + st * L::kStage);
+#pragma unroll
+          for (int kk = 0; kk < DH / 32; ++kk)
+            umma_i8(tmem + sb * 16, umma_desc(sk + kk * 32, 16, 1024, 2), umma_desc(sq + kk * 32, 16, 1024, 2),
+                    idesc_qk, kk > 0);
+          umma_commit(&bars[kDSFull + sb]);
+          if (pend >= 0 && !issue_pv(pend)) { ok = false; break; }
+          pend = jj;
+          if (blk + 1 == w.bhi) {                        // item end: Q is free, flush the last PV
+            umma_commit(&bars[kDQEmpty + qb]);
+            if (!issue_pv(pend)) { ok = false; break; }
+            pend = -1;
+          }
+        }
+        ++ii;
+      }
+    }
+  } else {
+    // ================================================================ workers
+    const int wq = warp & 3;
+    const int t = wq * 32 + lane;                        // TMEM lane: key (S) / channel (A)
+    const uint32_t lanebase = tmem + ((uint32_t)(wq * 32) << 16);
+    int jj = 0;
+    bool ok = true;                                    // identical on all 128 workers (barrier-decided)
+    for (int it = blockIdx.x; ok && it < total; it += gridDim.x) {
+      DecItem w;
+      const int kind = dec_item(p, max_splits, it, w);
+      if (kind == 2 && t == 0) atomicOr(p.err, kDevBadPage);
+      if (kind != 1) continue;
+      const long long bg = (long long)w.b * p.KVH + w.g;
+      int eqh[8];
+#pragma unroll
+      for (int h = 0; h < 8; ++h) eqh[h] = (h < gq) ? p.eq[(long long)w.b * p.H + w.g * gq + h] : 0;
+      // partials of block jb: A from TMEM (thread = channel), then NB / l_b / eh0 by threads < gq
+      auto readout_A = [&](int jb, int blk) -> bool {
+        const int ab = jb & 1;
+        const bool okw = warp_poll(&bars[kDAFull + ab], (jb >> 1) & 1, abort_flag, p.err);
+        if (okw) {
+          tc_fence_after();
+          uint32_t a[8];
+          tmem_ld8(lanebase + 32 + ab * 16, a);
+          tc_wait_ld();
+          tc_fence_before();
+          mbar_arrive(&bars[kDAEmpty + ab]);
+          int32_t* dstA = p.partA + ((bg * p.max_blocks + blk) * gq) * DH;
+#pragma unroll
+          for (int h = 0; h < 8; ++h) if (h < gq) __stcg(dstA + h * DH + t, (int32_t)a[h]);
+        }
+        return okw;
+      };
+      auto write_M = [&](int jb, int blk) {             // after a barrier that follows block jb's l_b atomics
+        const int par = jb & 1;
+        if (t < gq) {
+          const int e0 = (SINK && blk == 0 && w.L > 1) ? eh0s[t] : 0;
+          __stcg(&p.partM[(bg * p.max_blocks + blk) * gq + t], make_int4(nbs[par * 8 + t], (int)lbsum[par * 8 + t], e0, 0));
+          lbsum[par * 8 + t] = 0u;
+        }
+      };
+      bool bad = false;                                  // this warp gave up a wait (decided at the next barrier)
+      for (int blk = w.blo; blk < w.bhi; ++blk, ++jj) {
+        const int sb = jj & 1, par = jj & 1;
+        const int ekb = p.ek[bg * p.max_blocks + blk];
+        bool okw = warp_poll(&bars[kDSFull + sb], (jj >> 1) & 1, abort_flag, p.err);
+        int S[8];
+        if (okw) {
+          tc_fence_after();
+          tmem_ld8(lanebase + sb * 16, reinterpret_cast<uint32_t*>(S));
+          tc_wait_ld();
+          tc_fence_before();
+          mbar_arrive(&bars[kDSEmpty + sb]);
+        }
+        const int nkeys = min(kKB, w.L - blk * kKB);
+        if (t >= nkeys) {
+#pragma unroll
+          for (int h = 0; h < 8; ++h) S[h] = INT32_MIN;  // keys past the sequence end
+        }
+#pragma unroll
+        for (int h = 0; h < 8; ++h) {
+          const int wm = (int)redux_max_s32(S[h]);
+          if (lane == 0) redmax[(par * 4 + wq) * 8 + h] = wm;
+        }
+        uint32_t Gh[8];
+        int dmh[8];
+#pragma unroll
+        for (int h = 0; h < 8; ++h) {                    // independent of the block max: before the barrier
+          Gh[h] = g_fold(p.gbase, eqh[h] + ekb);
+          dmh[h] = 1 << max(0, 30 - (31 - __clz((int)Gh[h])));
+        }
+        // every worker meets here once per block; the OR makes giving up a group decision
+        if (bar_any(1, 128, bad || !okw || *abort_flag != 0)) { ok = false; break; }
+        if (blk > w.blo) write_M(jj - 1, blk - 1);       // block jb - 1's l_b atomics are complete
+        uint32_t e[8];
+#pragma unroll
+        for (int h = 0; h < 8; ++h) {
+          const int m = max(max(redmax[(par * 4 + 0) * 8 + h], redmax[(par * 4 + 1) * 8 + h]),
+                            max(redmax[(par * 4 + 2) * 8 + h], redmax[(par * 4 + 3) * 8 + h]));
+          const uint32_t G = Gh[h];
+          const int nbv = nb_of(m, G);
+          const int sc = max(S[h], m - dmh[h]);
+          const uint32_t d = ((uint32_t)nbv << kBHI) + (uint32_t)sc * (0u - G);
+          e[h] = (h < gq && t < nkeys) ? (uint32_t)tab[d >> kIdxShift] : 0u;
+          if (t == 0) nbs[par * 8 + h] = nbv;
+        }
+        if (SINK && blk == 0 && t == 0 && w.L > 1) {    // key 0's weight stays out of the P operand
+#pragma unroll
+          for (int h = 0; h < 8; ++h) eh0s[h] = (int)e[h];
+        }
+        // P^T[head][key] in 8-head x 16-key core matrices: (key / 16) * 256 + (h / 8) * 128 + (h % 8) * 16 + key % 16
+        if (!warp_poll(&bars[kDPEmpty + par], ((jj >> 1) & 1) ^ 1, abort_flag, p.err)) bad = true;
+        uint8_t* pd = smem + L::kP + par * 2048 + (t >> 4) * 256 + (t & 15);
+#pragma unroll
+        for (int h = 0; h < 8; ++h) {                    // rows >= gq of P^T only feed ignored columns of A
+          if (h < gq) {
+            const uint32_t pe = (SINK && blk == 0 && t == 0 && w.L > 1) ? 0u : e[h];
+            pd[(h >> 3) * 128 + (h & 7) * 16] = (uint8_t)pe;
+          }
+        }
+#pragma unroll
+        for (int h = 0; h < 8; ++h) {
+          if (h < gq) {
+            const uint32_t s = redux_add_u32(e[h]);
+            if (lane == 0) atomicAdd(&lbsum[par * 8 + h], s);
+          }
+        }
+        fence_async_smem();
+        mbar_arrive(&bars[kDPFull + par]);
+        if (blk > w.blo && !readout_A(jj - 1, blk - 1)) bad = true;
+      }
+      if (!ok) break;                                    // (decided at a barrier: uniform)
+      // the item's last block: its l_b atomics meet at one more barrier, then its A, then the ticket
+      if (bar_any(1, 128, bad || *abort_flag != 0)) { ok = false; break; }
+      write_M(jj - 1, w.bhi - 1);
+      if (!readout_A(jj - 1, w.bhi - 1)) bad = true;
+      if (bar_any(1, 128, bad || *abort_flag != 0)) { ok = false; break; }
+    }
+  }
+
+  // ---- teardown
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kDecTmemCols) : "memory");
+  }
+}
+
+// The committed-order refold of every (sequence, kv head) from its exact block partials: one CTA
+// per (kv head, sequence), one thread per channel (decode_merge).
+template <bool SINK, typename OutT>
+__global__ void __launch_bounds__(128) decode_merge_kernel(const DecodeArgs p) {
+  const int g = blockIdx.x, b = blockIdx.y;
+  const int L = p.seq_lens[b];
+  const int nblk = (L + kKB - 1) / kKB;
+  if (L <= 0 || nblk > p.max_blocks || (L + 15) / 16 > p.max_pages) return;   // flagged by the stream kernel
+  decode_merge<128, SINK, OutT, 4>(p, b, g, threadIdx.x);
+}
+
+}  // namespace lssab8
