@@ -223,29 +223,32 @@ int launch_decode_out(int out_dtype, const DecodeArgs& a, int max_splits, cudaSt
   }
 }
 
-template <bool SINK, typename OutT>
+template <bool SINK, typename OutT, int GQ>
 int launch_decode_tc_t(const DecodeArgs& a, int max_splits, int num_sms, cudaStream_t st) {
   CUtensorMap tk, tq;
   int rc;
   if ((rc = make_tmap(&tk, a.k8p, (long long)a.num_pages * a.KVH * 16, 128, 16))) return rc;
   if ((rc = make_tmap(&tq, a.q8, (long long)a.B * a.H, 128, 16))) return rc;
   const int smem = DecTcSmem::kBytes + 1024;
-  auto kfn = decode_tc_kernel<SINK, OutT>;
+  auto kfn = decode_tc_kernel<SINK, OutT, GQ>;
   if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return kErrCuda;
   const long long items = (long long)a.B * a.KVH * max_splits;
-  const int grid = (int)std::min<long long>(items, (long long)std::max(num_sms, 1));
+  const int grid = (int)std::min<long long>(items, 2LL * std::max(num_sms, 1));   // two CTAs per SM
   kfn<<<grid, kDecThreads, smem, st>>>(tk, tq, a, max_splits);
   if ((rc = launch_rc())) return rc;
-  decode_merge_kernel<SINK, OutT><<<dim3(a.KVH, a.B), 128, 0, st>>>(a);
+  decode_merge_kernel<SINK, OutT><<<dim3(a.KVH, a.B, a.group), 128, 0, st>>>(a);
   return launch_rc();
 }
 
 template <bool SINK>
 int launch_decode_tc_out(int out_dtype, const DecodeArgs& a, int max_splits, int num_sms, cudaStream_t st) {
   switch (out_dtype) {
-    case kF32: return launch_decode_tc_t<SINK, float>(a, max_splits, num_sms, st);
-    case kF16: return launch_decode_tc_t<SINK, __half>(a, max_splits, num_sms, st);
-    case kBF16: return launch_decode_tc_t<SINK, __nv_bfloat16>(a, max_splits, num_sms, st);
+    case kF32: return a.group == 4 ? launch_decode_tc_t<SINK, float, 4>(a, max_splits, num_sms, st)
+                                   : launch_decode_tc_t<SINK, float, 8>(a, max_splits, num_sms, st);
+    case kF16: return a.group == 4 ? launch_decode_tc_t<SINK, __half, 4>(a, max_splits, num_sms, st)
+                                   : launch_decode_tc_t<SINK, __half, 8>(a, max_splits, num_sms, st);
+    case kBF16: return a.group == 4 ? launch_decode_tc_t<SINK, __nv_bfloat16, 4>(a, max_splits, num_sms, st)
+                                    : launch_decode_tc_t<SINK, __nv_bfloat16, 8>(a, max_splits, num_sms, st);
     default: return kErrArg;
   }
 }

@@ -63,94 +63,70 @@ struct DecodeSmem {
   static constexpr int kBytes = kBar + 64;
 };
 
-// The committed-order refold of one (sequence, kv head) from its exact block partials, for
-// channel c (one thread per channel): per head, blocks in ascending order into 32-block
-// segments, segments into the row (reference/lssab8_golden.py:350-394, 257-335), then one RN
-// division.  The heads' chains are independent, so they advance together, four blocks at a
-// time, with all of those blocks' partial loads issued before any is used.  Partials are read
-// with .cg loads (other CTAs wrote them).
+// The committed-order refold of head h of one (sequence, kv head) from its exact block partials,
+// for channel c: blocks in ascending order into 32-block segments, segments into the row
+// (reference/lssab8_golden.py:350-394, 257-335), then one RN division.  kBatch blocks' partial
+// loads are issued before any is used, so their latencies overlap; partials are read with .cg
+// loads (other CTAs wrote them).
 template <int DH, bool SINK, typename OutT, int kBatch>
-__device__ __forceinline__ void decode_merge(const DecodeArgs& p, int b, int g, int c) {
+__device__ __forceinline__ void decode_merge_head(const DecodeArgs& p, int b, int g, int h, int c) {
   const int gq = p.group;
   const int L_len = p.seq_lens[b];
   const int nblk = (L_len + kKB - 1) / kKB;
   const long long bg = (long long)b * p.KVH + g;
-  const int evs0 = SINK ? p.ev0[bg] : 0;
-  int v0c = 0;
+  int v0c = 0, evs0 = 0, eh0 = 0;
   if (SINK && L_len > 1) {
     const int pg = p.block_table[(long long)b * p.max_pages];
     v0c = (int)p.v8p[((long long)pg * p.KVH + g) * (16 * DH) + c * 16 + 0];
+    evs0 = p.ev0[bg];
+    eh0 = __ldcg(&p.partM[(bg * p.max_blocks) * gq + h]).z;
   }
-  float Orow[8], lrow[8], O[8], lseg[8];
-  int nbrow[8], nbrun[8];
-#pragma unroll
-  for (int h = 0; h < 8; ++h) { Orow[h] = 0.0f; lrow[h] = 0.0f; nbrow[h] = 0; }
+  float Orow = 0.0f, lrow = 0.0f;
+  int nbrow = 0;
   for (int s0 = 0; s0 < nblk; s0 += kSEG) {
     const int s1 = min(nblk, s0 + kSEG);
-#pragma unroll
-    for (int h = 0; h < 8; ++h) { O[h] = 0.0f; lseg[h] = 0.0f; nbrun[h] = 0; }
+    float O = 0.0f, lseg = 0.0f;
+    int nbrun = 0;
     for (int k0 = s0; k0 < s1; k0 += kBatch) {
-      int2 m4[kBatch][8];                                  // (NB_b, l_b); eh0 is read for block 0 only
-      int Av[kBatch][8], evv[kBatch];
+      int2 m2[kBatch];                                   // (NB_b, l_b)
+      int Av[kBatch], evv[kBatch];
 #pragma unroll
       for (int u = 0; u < kBatch; ++u) {
         const int blk = min(k0 + u, s1 - 1);
         evv[u] = p.ev[bg * p.max_blocks + blk];
-#pragma unroll
-        for (int h = 0; h < 8; ++h) {
-          if (h < gq) {
-            m4[u][h] = __ldcg(reinterpret_cast<const int2*>(&p.partM[(bg * p.max_blocks + blk) * gq + h]));
-            Av[u][h] = __ldcg(&p.partA[((bg * p.max_blocks + blk) * gq + h) * DH + c]);
-          }
-        }
+        m2[u] = __ldcg(reinterpret_cast<const int2*>(&p.partM[(bg * p.max_blocks + blk) * gq + h]));
+        Av[u] = __ldcg(&p.partA[((bg * p.max_blocks + blk) * gq + h) * DH + c]);
       }
 #pragma unroll
       for (int u = 0; u < kBatch; ++u) {
         const int blk = k0 + u;
         if (blk >= s1) break;
-#pragma unroll
-        for (int h = 0; h < 8; ++h) {
-          if (h < gq) {
-            if (blk == s0) nbrun[h] = m4[u][h].x;
-            const int D = m4[u][h].x - nbrun[h];
-            int sg = 0;
-            if (D > 0) { O[h] = rescale(O[h], D); lseg[h] = rescale(lseg[h], D); nbrun[h] = m4[u][h].x; }
-            else sg = -D;
-            if (sg <= kSWIN) {
-              if (SINK && blk == 0 && L_len > 1) {
-                const int eh0 = __ldcg(&p.partM[(bg * p.max_blocks) * gq + h]).z;
-                O[h] = fold_term(O[h], eh0 * v0c, pow2f(-(sg + evs0)));
-              }
-              O[h] = fold_term(O[h], Av[u][h], pow2f(-(sg + evv[u])));
-              lseg[h] = fold_term(lseg[h], m4[u][h].y, pow2f(-sg));
-            }
-          }
+        if (blk == s0) nbrun = m2[u].x;
+        const int D = m2[u].x - nbrun;
+        int sg = 0;
+        if (D > 0) { O = rescale(O, D); lseg = rescale(lseg, D); nbrun = m2[u].x; }
+        else sg = -D;
+        if (sg <= kSWIN) {
+          if (SINK && blk == 0 && L_len > 1) O = fold_term(O, eh0 * v0c, pow2f(-(sg + evs0)));
+          O = fold_term(O, Av[u], pow2f(-(sg + evv[u])));
+          lseg = fold_term(lseg, m2[u].y, pow2f(-sg));
         }
       }
     }
-#pragma unroll
-    for (int h = 0; h < 8; ++h) {                        // segment -> row (reference/lssab8_golden.py:317-331)
-      if (h < gq) {
-        if (s0 == 0) { nbrow[h] = nbrun[h]; }
-        const int D2 = nbrun[h] - nbrow[h];
-        int s2 = 0;
-        if (D2 > 0) { Orow[h] = rescale(Orow[h], D2); lrow[h] = rescale(lrow[h], D2); nbrow[h] = nbrun[h]; }
-        else s2 = -D2;
-        if (s2 <= kSWIN) {
-          Orow[h] = __fadd_rn(Orow[h], rescale(O[h], s2));
-          lrow[h] = __fadd_rn(lrow[h], rescale(lseg[h], s2));
-        }
-      }
+    // segment -> row (reference/lssab8_golden.py:317-331)
+    if (s0 == 0) nbrow = nbrun;
+    const int D2 = nbrun - nbrow;
+    int s2 = 0;
+    if (D2 > 0) { Orow = rescale(Orow, D2); lrow = rescale(lrow, D2); nbrow = nbrun; }
+    else s2 = -D2;
+    if (s2 <= kSWIN) {
+      Orow = __fadd_rn(Orow, rescale(O, s2));
+      lrow = __fadd_rn(lrow, rescale(lseg, s2));
     }
   }
-#pragma unroll
-  for (int h = 0; h < 8; ++h) {
-    if (h < gq) {
-      const float y = (lrow[h] != 0.0f) ? __fdiv_rn(Orow[h], lrow[h]) : 0.0f;
-      OutT* dst = reinterpret_cast<OutT*>(p.out) + b * p.os0 + (long long)(g * gq + h) * p.os1 + c * p.os2;
-      *dst = from_f32<OutT>(y);
-    }
-  }
+  const float y = (lrow != 0.0f) ? __fdiv_rn(Orow, lrow) : 0.0f;
+  OutT* dst = reinterpret_cast<OutT*>(p.out) + b * p.os0 + (long long)(g * gq + h) * p.os1 + c * p.os2;
+  *dst = from_f32<OutT>(y);
 }
 
 template <int DH, bool SINK, typename OutT>
@@ -333,7 +309,7 @@ decode_kernel(const DecodeArgs p) {
   __threadfence();
   if (tid == 0) p.tickets[bg] = 0u;                          // ready for the next launch
   if (tid >= DH) return;
-  decode_merge<DH, SINK, OutT, 2>(p, b, g, tid);
+  for (int hh = 0; hh < gq; ++hh) decode_merge_head<DH, SINK, OutT, 8>(p, b, g, hh, tid);
 }
 
 // Decode lattice writer: quantise a sequence's K and V (bf16/f16/f32, any strides) into the

@@ -27,7 +27,8 @@
 
 namespace lssab8 {
 
-constexpr int kDecStages = 4;
+constexpr int kDecStages = 3;                      // two CTAs per SM, three stages each
+constexpr int kDecTab = 1168;                      // T2 entries 0..1152 (1152 = 0), 16-byte padded
 constexpr int kDecThreads = 192;   // warp 0 TMA, warp 1 MMA + TMEM, warps 2-5 workers
 constexpr uint32_t kDecTmemCols = 64;
 
@@ -36,8 +37,8 @@ struct DecTcSmem {
   static constexpr int kStage = 16 * kPage;               // 8 key pages, then 8 value pages
   static constexpr int kQ = kDecStages * kStage;          // 2 x Q^T [16 rows x 128 B], SW128
   static constexpr int kP = kQ + 2 * 2048;                // 2 x P^T [16 heads x 128 keys], core matrices
-  static constexpr int kTab = kP + 2 * 2048;              // T2, zero-padded to 8192 entries
-  static constexpr int kRedMax = kTab + kTabPad;          // [2][4 warps][8 heads] block max
+  static constexpr int kTab = kP + 2 * 2048;              // T2 entries 0..1152 (index clamped to 1152)
+  static constexpr int kRedMax = kTab + kDecTab;          // [2][4 warps][8 heads] block max
   static constexpr int kLbSum = kRedMax + 2 * 4 * 8 * 4;  // [2][8] l_b
   static constexpr int kNb = kLbSum + 2 * 8 * 4;          // [2][8] NB_b
   static constexpr int kEh0 = kNb + 2 * 8 * 4;            // [8] key 0's weight (sink, block 0)
@@ -82,8 +83,9 @@ __device__ __forceinline__ uint32_t redux_add_u32(uint32_t v) {
   return r;
 }
 
-template <bool SINK, typename OutT>
-__global__ void __launch_bounds__(kDecThreads, 1)
+// GQ = compile-time bound on the GQA group (4: exactly 4 heads; 8: any group <= 8, masked).
+template <bool SINK, typename OutT, int GQ>
+__global__ void __launch_bounds__(kDecThreads, 2)
 decode_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_q,
                  const DecodeArgs p, int max_splits) {
   using L = DecTcSmem;
@@ -103,7 +105,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
   const int total = p.B * p.KVH * max_splits;
   const int gq = p.group;
 
-  for (int i = threadIdx.x; i < kTabPad; i += blockDim.x) tab[i] = (i < kTabLive) ? kT2Live[i] : 0;
+  for (int i = threadIdx.x; i < kDecTab; i += blockDim.x) tab[i] = (i < kTabLive) ? kT2Live[i] : 0;
   for (int i = threadIdx.x; i < 2 * 8; i += blockDim.x) lbsum[i] = 0u;
   if (threadIdx.x == 0) {
     for (int s = 0; s < kDecStages; ++s) { mbar_init(&bars[kDFull + s], 1); mbar_init(&bars[kDEmpty + s], 1); }
@@ -139,13 +141,22 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
         mbar_expect_tx(&bars[kDQFull + qb], 2048);
         tma_load_2d(smem + L::kQ + qb * 2048, &tm_q, 0, w.b * p.H + w.g * gq, &bars[kDQFull + qb]);
         const int32_t* bt = p.block_table + (long long)w.b * p.max_pages;
+        // a block's page ids are loaded one block ahead, so their latency is off the critical path
+        int pgn[8];
+        auto load_pages = [&](int blk) {
+          const int npg = min(8, (w.L - blk * kKB + 15) / 16);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) pgn[i] = (i < npg) ? bt[blk * 8 + i] : 0;
+        };
+        load_pages(w.blo);
         for (int blk = w.blo; blk < w.bhi; ++blk, ++jj) {
           const int st = jj % kDecStages;
-          if (!mbar_wait(&bars[kDEmpty + st], ((jj / kDecStages) & 1) ^ 1, abort_flag, p.err, 128)) { ok = false; break; }
-          const int npg = min(8, (w.L - blk * kKB + 15) / 16);
           int pg[8];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) pg[i] = (i < npg) ? bt[blk * 8 + i] : 0;
+          for (int i = 0; i < 8; ++i) pg[i] = pgn[i];
+          if (blk + 1 < w.bhi) load_pages(blk + 1);
+          if (!mbar_wait(&bars[kDEmpty + st], ((jj / kDecStages) & 1) ^ 1, abort_flag, p.err, 128)) { ok = false; break; }
+          const int npg = min(8, (w.L - blk * kKB + 15) / 16);
           mbar_expect_tx(&bars[kDFull + st], (uint32_t)(npg * 2 * L::kPage));
           uint8_t* kdst = smem + st * L::kStage;
           uint8_t* vdst = kdst + 8 * L::kPage;
@@ -225,9 +236,9 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
       if (kind == 2 && t == 0) atomicOr(p.err, kDevBadPage);
       if (kind != 1) continue;
       const long long bg = (long long)w.b * p.KVH + w.g;
-      int eqh[8];
+      int eqh[GQ];
 #pragma unroll
-      for (int h = 0; h < 8; ++h) eqh[h] = (h < gq) ? p.eq[(long long)w.b * p.H + w.g * gq + h] : 0;
+      for (int h = 0; h < GQ; ++h) eqh[h] = (h < gq) ? p.eq[(long long)w.b * p.H + w.g * gq + h] : 0;
       // partials of block jb: A from TMEM (thread = channel), then NB / l_b / eh0 by threads < gq
       auto readout_A = [&](int jb, int blk) -> bool {
         const int ab = jb & 1;
@@ -241,7 +252,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
           mbar_arrive(&bars[kDAEmpty + ab]);
           int32_t* dstA = p.partA + ((bg * p.max_blocks + blk) * gq) * DH;
 #pragma unroll
-          for (int h = 0; h < 8; ++h) if (h < gq) __stcg(dstA + h * DH + t, (int32_t)a[h]);
+          for (int h = 0; h < GQ; ++h) if (h < gq) __stcg(dstA + h * DH + t, (int32_t)a[h]);
         }
         return okw;
       };
@@ -269,51 +280,51 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
         const int nkeys = min(kKB, w.L - blk * kKB);
         if (t >= nkeys) {
 #pragma unroll
-          for (int h = 0; h < 8; ++h) S[h] = INT32_MIN;  // keys past the sequence end
+          for (int h = 0; h < GQ; ++h) S[h] = INT32_MIN;  // keys past the sequence end
         }
 #pragma unroll
-        for (int h = 0; h < 8; ++h) {
+        for (int h = 0; h < GQ; ++h) {
           const int wm = (int)redux_max_s32(S[h]);
           if (lane == 0) redmax[(par * 4 + wq) * 8 + h] = wm;
         }
-        uint32_t Gh[8];
-        int dmh[8];
+        uint32_t Gh[GQ];
+        int dmh[GQ];
 #pragma unroll
-        for (int h = 0; h < 8; ++h) {                    // independent of the block max: before the barrier
+        for (int h = 0; h < GQ; ++h) {                    // independent of the block max: before the barrier
           Gh[h] = g_fold(p.gbase, eqh[h] + ekb);
           dmh[h] = 1 << max(0, 30 - (31 - __clz((int)Gh[h])));
         }
         // every worker meets here once per block; the OR makes giving up a group decision
         if (bar_any(1, 128, bad || !okw || *abort_flag != 0)) { ok = false; break; }
         if (blk > w.blo) write_M(jj - 1, blk - 1);       // block jb - 1's l_b atomics are complete
-        uint32_t e[8];
+        uint32_t e[GQ];
 #pragma unroll
-        for (int h = 0; h < 8; ++h) {
+        for (int h = 0; h < GQ; ++h) {
           const int m = max(max(redmax[(par * 4 + 0) * 8 + h], redmax[(par * 4 + 1) * 8 + h]),
                             max(redmax[(par * 4 + 2) * 8 + h], redmax[(par * 4 + 3) * 8 + h]));
           const uint32_t G = Gh[h];
           const int nbv = nb_of(m, G);
           const int sc = max(S[h], m - dmh[h]);
           const uint32_t d = ((uint32_t)nbv << kBHI) + (uint32_t)sc * (0u - G);
-          e[h] = (h < gq && t < nkeys) ? (uint32_t)tab[d >> kIdxShift] : 0u;
+          e[h] = (h < gq && t < nkeys) ? (uint32_t)tab[min(d >> kIdxShift, (uint32_t)kTabLive)] : 0u;
           if (t == 0) nbs[par * 8 + h] = nbv;
         }
         if (SINK && blk == 0 && t == 0 && w.L > 1) {    // key 0's weight stays out of the P operand
 #pragma unroll
-          for (int h = 0; h < 8; ++h) eh0s[h] = (int)e[h];
+          for (int h = 0; h < GQ; ++h) eh0s[h] = (int)e[h];
         }
         // P^T[head][key] in 8-head x 16-key core matrices: (key / 16) * 256 + (h / 8) * 128 + (h % 8) * 16 + key % 16
         if (!warp_poll(&bars[kDPEmpty + par], ((jj >> 1) & 1) ^ 1, abort_flag, p.err)) bad = true;
         uint8_t* pd = smem + L::kP + par * 2048 + (t >> 4) * 256 + (t & 15);
 #pragma unroll
-        for (int h = 0; h < 8; ++h) {                    // rows >= gq of P^T only feed ignored columns of A
+        for (int h = 0; h < GQ; ++h) {                    // rows >= gq of P^T only feed ignored columns of A
           if (h < gq) {
             const uint32_t pe = (SINK && blk == 0 && t == 0 && w.L > 1) ? 0u : e[h];
             pd[(h >> 3) * 128 + (h & 7) * 16] = (uint8_t)pe;
           }
         }
 #pragma unroll
-        for (int h = 0; h < 8; ++h) {
+        for (int h = 0; h < GQ; ++h) {
           if (h < gq) {
             const uint32_t s = redux_add_u32(e[h]);
             if (lane == 0) atomicAdd(&lbsum[par * 8 + h], s);
@@ -346,11 +357,11 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
 // per (kv head, sequence), one thread per channel (decode_merge).
 template <bool SINK, typename OutT>
 __global__ void __launch_bounds__(128) decode_merge_kernel(const DecodeArgs p) {
-  const int g = blockIdx.x, b = blockIdx.y;
+  const int g = blockIdx.x, b = blockIdx.y, h = blockIdx.z;
   const int L = p.seq_lens[b];
   const int nblk = (L + kKB - 1) / kKB;
   if (L <= 0 || nblk > p.max_blocks || (L + 15) / 16 > p.max_pages) return;   // flagged by the stream kernel
-  decode_merge<128, SINK, OutT, 4>(p, b, g, threadIdx.x);
+  decode_merge_head<128, SINK, OutT, 16>(p, b, g, h, threadIdx.x);
 }
 
 }  // namespace lssab8
