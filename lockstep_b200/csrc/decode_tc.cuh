@@ -353,15 +353,75 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
   }
 }
 
-// The committed-order refold of every (sequence, kv head) from its exact block partials: one CTA
-// per (kv head, sequence), one thread per channel (decode_merge).
+// The committed-order refold of every (sequence, kv head, head) from its exact block partials:
+// one CTA per (kv head, sequence, head of the group), one thread per channel.  Each 32-block
+// segment of the head's partial rows (32 x 512 contiguous bytes) is staged into shared memory
+// with cp.async in one round trip, then every thread folds its channel in the committed order:
+// blocks ascending into the segment, segments into the row (reference/lssab8_golden.py:257-335,
+// 350-394), then one RN division.
 template <bool SINK, typename OutT>
 __global__ void __launch_bounds__(128) decode_merge_kernel(const DecodeArgs p) {
-  const int g = blockIdx.x, b = blockIdx.y, h = blockIdx.z;
+  constexpr int DH = 128;
+  __shared__ __align__(16) int sA[kSEG][DH];
+  __shared__ int2 sM[kSEG];
+  __shared__ int sEv[kSEG];
+  const int g = blockIdx.x, b = blockIdx.y, h = blockIdx.z, c = threadIdx.x;
+  const int gq = p.group;
   const int L = p.seq_lens[b];
   const int nblk = (L + kKB - 1) / kKB;
   if (L <= 0 || nblk > p.max_blocks || (L + 15) / 16 > p.max_pages) return;   // flagged by the stream kernel
-  decode_merge_head<128, SINK, OutT, 16>(p, b, g, h, threadIdx.x);
+  const long long bg = (long long)b * p.KVH + g;
+  int v0c = 0, evs0 = 0, eh0 = 0;
+  if (SINK && L > 1) {
+    const int pg = p.block_table[(long long)b * p.max_pages];
+    v0c = (int)p.v8p[((long long)pg * p.KVH + g) * (16 * DH) + c * 16 + 0];
+    evs0 = p.ev0[bg];
+    eh0 = __ldcg(&p.partM[(bg * p.max_blocks) * gq + h]).z;
+  }
+  float Orow = 0.0f, lrow = 0.0f;
+  int nbrow = 0;
+  for (int s0 = 0; s0 < nblk; s0 += kSEG) {
+    const int n = min(kSEG, nblk - s0);
+    for (int i = c; i < n * (DH / 4); i += blockDim.x) {     // 16-byte pieces of the n partial rows
+      const int u = i / (DH / 4), q = i % (DH / 4);
+      const int32_t* src = p.partA + ((bg * p.max_blocks + s0 + u) * gq + h) * DH + q * 4;
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(&sA[u][q * 4])), "l"(src) : "memory");
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    if (c < n) {
+      sM[c] = __ldcg(reinterpret_cast<const int2*>(&p.partM[(bg * p.max_blocks + s0 + c) * gq + h]));
+      sEv[c] = p.ev[bg * p.max_blocks + s0 + c];
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncthreads();
+    float O = 0.0f, lseg = 0.0f;
+    int nbrun = sM[0].x;
+    for (int u = 0; u < n; ++u) {
+      const int2 m = sM[u];
+      const int D = m.x - nbrun;
+      int sg = 0;
+      if (D > 0) { O = rescale(O, D); lseg = rescale(lseg, D); nbrun = m.x; }
+      else sg = -D;
+      if (sg <= kSWIN) {
+        if (SINK && s0 + u == 0 && L > 1) O = fold_term(O, eh0 * v0c, pow2f(-(sg + evs0)));
+        O = fold_term(O, sA[u][c], pow2f(-(sg + sEv[u])));
+        lseg = fold_term(lseg, m.y, pow2f(-sg));
+      }
+    }
+    __syncthreads();                                       // the stage is refilled next
+    if (s0 == 0) nbrow = nbrun;                            // segment -> row (reference/lssab8_golden.py:317-331)
+    const int D2 = nbrun - nbrow;
+    int s2 = 0;
+    if (D2 > 0) { Orow = rescale(Orow, D2); lrow = rescale(lrow, D2); nbrow = nbrun; }
+    else s2 = -D2;
+    if (s2 <= kSWIN) {
+      Orow = __fadd_rn(Orow, rescale(O, s2));
+      lrow = __fadd_rn(lrow, rescale(lseg, s2));
+    }
+  }
+  const float y = (lrow != 0.0f) ? __fdiv_rn(Orow, lrow) : 0.0f;
+  OutT* dst = reinterpret_cast<OutT*>(p.out) + b * p.os0 + (long long)(g * gq + h) * p.os1 + c * p.os2;
+  *dst = from_f32<OutT>(y);
 }
 
 }  // namespace lssab8
