@@ -30,6 +30,10 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "LSSA-B8 attn: prefill % int8 MMA peak; decode KV GB/s; 0 bit diffs vs ref"
+# DRAM bytes (read + write) of one launch, from one `ncu --set full` capture of the same workload
+# (profiles/prefill_kernel_cfg2.md, profiles/decode_kernel_cfg3.md)
+PREFILL_TRAFFIC_BYTES = 68_740_000
+DECODE_TRAFFIC_BYTES = 569_280_000
 CFG = dict(B=4, H=32, KVH=8, dh=128, T=2048, outliers=0.01)
 DEC = dict(B=32, H=32, KVH=8, dh=128, L=8192, nsplit=16)
 
@@ -203,7 +207,9 @@ def run_gpu(args):
                 "peak": round(int8_peak, 1), "unit": "TOPS", "frac": round(achieved / int8_peak, 4),
                 "peak_source": "2 x %s bf16 dense (cuBLAS burst %.1f TF/s), int8 dense rate = 2x bf16 on B200"
                                % (peaks["src"], peaks["bf16"]),
-                "traffic": None, "kernel_ms": round(kms, 4), "algorithmic_ops_per_launch": ops}
+                "traffic": PREFILL_TRAFFIC_BYTES, "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, "
+                "one launch (profiles/prefill_kernel_cfg2.md)", "kernel_ms": round(kms, 4),
+                "algorithmic_ops_per_launch": ops}
 
     # ---------------------------------------------------------------- end to end (public API)
     qo = torch.empty_like(out, device="cpu").pin_memory()
@@ -256,7 +262,9 @@ def run_gpu(args):
     A.check_device_errors(dev)
     decode = {"config": "cfg3 B32 H32/KVH8 dh128 L8192, 16 splits, sink off", "ms_per_step": round(dms, 4),
               "kv_gbps": round(dec_gbs, 1), "frac_hbm": round(dec_gbs / peaks["hbm"], 4),
-              "hbm_peak_gbps": peaks["hbm"], "algorithmic_bytes": lattice_bytes}
+              "hbm_peak_gbps": peaks["hbm"], "algorithmic_bytes": lattice_bytes,
+              "traffic": DECODE_TRAFFIC_BYTES, "traffic_source": "ncu, streaming + refold kernels of one call "
+              "(profiles/decode_kernel_cfg3.md)"}
 
     gather = None
     if world > 1:
