@@ -232,9 +232,10 @@ int launch_decode_tc_t(const DecodeArgs& a, int max_splits, int num_sms, cudaStr
   const int smem = DecTcSmem::kBytes + 1024;
   auto kfn = decode_tc_kernel<SINK, OutT, GQ>;
   if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return kErrCuda;
-  const long long items = (long long)a.B * a.KVH * max_splits;
-  const int grid = (int)std::min<long long>(items, 2LL * std::max(num_sms, 1));   // two CTAs per SM
-  kfn<<<grid, kDecThreads, smem, st>>>(tk, tq, a, max_splits);
+  (void)max_splits;     // exact block partials: the streaming kernel schedules blocks, not splits
+  const long long chunks = ((long long)a.B * a.KVH * a.max_blocks + kDecChunk - 1) / kDecChunk;
+  const int grid = (int)std::min<long long>(chunks, 2LL * std::max(num_sms, 1));   // two CTAs per SM
+  kfn<<<grid, kDecThreads, smem, st>>>(tk, tq, a);
   if ((rc = launch_rc())) return rc;
   decode_merge_kernel<SINK, OutT><<<dim3(a.KVH, a.B, a.group), 128, 0, st>>>(a);
   return launch_rc();

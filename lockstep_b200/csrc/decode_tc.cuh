@@ -5,8 +5,10 @@
 // the last CTA of a (sequence, kv head) refolds all blocks in ascending order
 // (reference/lssab8_golden.py:350-394).  What changes is how the partials are produced:
 //
-//   * persistent CTAs walk the work items (sequence, kv head, split) and their blocks as one
-//     stream, so the TMA ring never drains between items;
+//   * persistent CTAs walk the (sequence, kv head, block) list in interleaved chunks of
+//     kDecChunk blocks as ONE stream (block partials are exact, so where a split or chunk ends
+//     changes no bit): the TMA ring never drains, the one-block lag of the partial readout runs
+//     across chunk boundaries, and Q is reloaded only when (sequence, kv head) changes;
 //   * warp 0 (one thread) streams each block's 8 key pages with cp.async.bulk.tensor (the tensor
 //     map swizzles them into the SW128 K-major layout) and its 8 transposed value pages with
 //     plain cp.async.bulk into a kDecStages-deep ring (no multicast);
@@ -41,8 +43,8 @@ struct DecTcSmem {
   static constexpr int kRedMax = kTab + kDecTab;          // [2][4 warps][8 heads] block max
   static constexpr int kLbSum = kRedMax + 2 * 4 * 8 * 4;  // [2][8] l_b
   static constexpr int kNb = kLbSum + 2 * 8 * 4;          // [2][8] NB_b
-  static constexpr int kEh0 = kNb + 2 * 8 * 4;            // [8] key 0's weight (sink, block 0)
-  static constexpr int kBar = kEh0 + 8 * 4 + 32;          // mbarriers
+  static constexpr int kEh0 = kNb + 2 * 8 * 4;            // [2][8] key 0's weight (sink, block 0)
+  static constexpr int kBar = kEh0 + 2 * 8 * 4 + 32;      // mbarriers
   static constexpr int kMisc = kBar + 32 * 8;             // tmem base, abort flag
   static constexpr int kBytes = kMisc + 64;
 };
@@ -53,24 +55,48 @@ enum DecBar : int {
   kDAEmpty = kDAFull + 2, kDNumBars = kDAEmpty + 2
 };
 
-struct DecItem {
-  int b, g, blo, bhi, L;
-};
+constexpr int kDecChunk = 8;                       // blocks per scheduling chunk
 
-// Work item it = (b * KVH + g) * max_splits + split: 1 = blocks to process, 0 = the split lies
-// past the sequence, 2 = the lattice arrays are too short for the sequence (an error).
-__device__ __forceinline__ int dec_item(const DecodeArgs& p, int max_splits, int it, DecItem& w) {
-  const int split = it % max_splits;
-  const int bg = it / max_splits;
-  w.g = bg % p.KVH;
-  w.b = bg / p.KVH;
-  w.L = p.seq_lens[w.b];
-  const int nblk = (w.L + kKB - 1) / kKB;
-  w.blo = split * p.split_blocks;
-  w.bhi = min(nblk, w.blo + p.split_blocks);
-  if (w.L <= 0 || w.blo >= w.bhi) return 0;
-  return (nblk <= p.max_blocks && (w.L + 15) / 16 <= p.max_pages) ? 1 : 2;
-}
+// The CTA's walk over the virtual block list v = (b * KVH + g) * max_blocks + blk, in chunks of
+// kDecChunk: chunks blockIdx.x, blockIdx.x + gridDim.x, ...  Blocks past a sequence's end are
+// skipped, and so is every block of a sequence the lattice arrays are too short for (flagged by
+// the workers).  Every role runs its own copy and sees the same sequence of blocks.
+struct DecIter {
+  int v, vend, chunk, nchunks, total;
+  int cur_b, L;
+  bool bad;
+  __device__ __forceinline__ void init(const DecodeArgs& p) {
+    total = p.B * p.KVH * p.max_blocks;
+    nchunks = (total + kDecChunk - 1) / kDecChunk;
+    chunk = blockIdx.x;
+    v = chunk * kDecChunk;
+    vend = min(v + kDecChunk, total);
+    cur_b = -1;
+    L = 0;
+    bad = false;
+  }
+  __device__ __forceinline__ bool next(const DecodeArgs& p, int& b, int& g, int& blk) {
+    for (;;) {
+      if (v >= vend) {
+        chunk += gridDim.x;
+        if (chunk >= nchunks) return false;
+        v = chunk * kDecChunk;
+        vend = min(v + kDecChunk, total);
+      }
+      const int vv = v++;
+      blk = vv % p.max_blocks;
+      const int bg = vv / p.max_blocks;
+      g = bg % p.KVH;
+      b = bg / p.KVH;
+      if (b != cur_b) {
+        cur_b = b;
+        L = p.seq_lens[b];
+        bad = ((L + kKB - 1) / kKB > p.max_blocks) || ((L + 15) / 16 > p.max_pages);
+      }
+      if (L > 0 && blk * kKB < L && !bad) return true;
+    }
+  }
+};
 
 __device__ __forceinline__ uint32_t redux_max_s32(int v) {
   int r;
@@ -87,7 +113,7 @@ __device__ __forceinline__ uint32_t redux_add_u32(uint32_t v) {
 template <bool SINK, typename OutT, int GQ>
 __global__ void __launch_bounds__(kDecThreads, 2)
 decode_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_q,
-                 const DecodeArgs p, int max_splits) {
+                 const DecodeArgs p) {
   using L = DecTcSmem;
   constexpr int DH = 128;
   extern __shared__ uint8_t smem_raw[];
@@ -102,7 +128,6 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kMisc + 8);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int total = p.B * p.KVH * max_splits;
   const int gq = p.group;
 
   for (int i = threadIdx.x; i < kDecTab; i += blockDim.x) tab[i] = (i < kTabLive) ? kT2Live[i] : 0;
@@ -131,44 +156,37 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
   if (warp == 0) {
     // ================================================================ TMA producer
     if (lane == 0) {
-      int jj = 0, ii = 0;
-      bool ok = true;
-      for (int it = blockIdx.x; ok && it < total; it += gridDim.x) {
-        DecItem w;
-        if (dec_item(p, max_splits, it, w) != 1) continue;
-        const int qb = ii & 1;
-        if (!mbar_wait(&bars[kDQEmpty + qb], ((ii >> 1) & 1) ^ 1, abort_flag, p.err, 128)) { ok = false; break; }
-        mbar_expect_tx(&bars[kDQFull + qb], 2048);
-        tma_load_2d(smem + L::kQ + qb * 2048, &tm_q, 0, w.b * p.H + w.g * gq, &bars[kDQFull + qb]);
-        const int32_t* bt = p.block_table + (long long)w.b * p.max_pages;
-        // a block's page ids are loaded one block ahead, so their latency is off the critical path
-        int pgn[8];
-        auto load_pages = [&](int blk) {
-          const int npg = min(8, (w.L - blk * kKB + 15) / 16);
-#pragma unroll
-          for (int i = 0; i < 8; ++i) pgn[i] = (i < npg) ? bt[blk * 8 + i] : 0;
-        };
-        load_pages(w.blo);
-        for (int blk = w.blo; blk < w.bhi; ++blk, ++jj) {
-          const int st = jj % kDecStages;
-          int pg[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) pg[i] = pgn[i];
-          if (blk + 1 < w.bhi) load_pages(blk + 1);
-          if (!mbar_wait(&bars[kDEmpty + st], ((jj / kDecStages) & 1) ^ 1, abort_flag, p.err, 128)) { ok = false; break; }
-          const int npg = min(8, (w.L - blk * kKB + 15) / 16);
-          mbar_expect_tx(&bars[kDFull + st], (uint32_t)(npg * 2 * L::kPage));
-          uint8_t* kdst = smem + st * L::kStage;
-          uint8_t* vdst = kdst + 8 * L::kPage;
-          for (int i = 0; i < npg; ++i) {
-            int q = pg[i];
-            if (q < 0 || q >= p.num_pages) { atomicOr(p.err, kDevBadPage); q = 0; }
-            const long long prow = (long long)q * p.KVH + w.g;
-            tma_load_2d(kdst + i * L::kPage, &tm_k, 0, (int)(prow * 16), &bars[kDFull + st]);
-            bulk_g2s(vdst + i * L::kPage, p.v8p + prow * L::kPage, L::kPage, &bars[kDFull + st]);
-          }
+      DecIter itr;
+      itr.init(p);
+      int jj = 0, run = -1, cur_bg = -1, b, g, blk;
+      while (itr.next(p, b, g, blk)) {
+        const int bg = b * p.KVH + g;
+        if (bg != cur_bg) {                              // a new (sequence, kv head): its Q^T tile
+          cur_bg = bg;
+          ++run;
+          const int qb = run & 1;
+          if (!mbar_wait(&bars[kDQEmpty + qb], ((run >> 1) & 1) ^ 1, abort_flag, p.err, 128)) break;
+          mbar_expect_tx(&bars[kDQFull + qb], 2048);
+          tma_load_2d(smem + L::kQ + qb * 2048, &tm_q, 0, b * p.H + g * gq, &bars[kDQFull + qb]);
         }
-        ++ii;
+        const int st = jj % kDecStages;
+        const int npg = min(8, (itr.L - blk * kKB + 15) / 16);
+        const int32_t* bt = p.block_table + (long long)b * p.max_pages + blk * 8;
+        int pg[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) pg[i] = (i < npg) ? bt[i] : 0;   // in flight during the wait
+        if (!mbar_wait(&bars[kDEmpty + st], ((jj / kDecStages) & 1) ^ 1, abort_flag, p.err, 128)) break;
+        mbar_expect_tx(&bars[kDFull + st], (uint32_t)(npg * 2 * L::kPage));
+        uint8_t* kdst = smem + st * L::kStage;
+        uint8_t* vdst = kdst + 8 * L::kPage;
+        for (int i = 0; i < npg; ++i) {
+          int q = pg[i];
+          if (q < 0 || q >= p.num_pages) { atomicOr(p.err, kDevBadPage); q = 0; }
+          const long long prow = (long long)q * p.KVH + g;
+          tma_load_2d(kdst + i * L::kPage, &tm_k, 0, (int)(prow * 16), &bars[kDFull + st]);
+          bulk_g2s(vdst + i * L::kPage, p.v8p + prow * L::kPage, L::kPage, &bars[kDFull + st]);
+        }
+        ++jj;
       }
     }
   } else if (warp == 1) {
@@ -176,9 +194,6 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
     if (lane == 0) {
       constexpr uint32_t idesc_qk = idesc_i8(1, 1, 0, 128, 16);
       constexpr uint32_t idesc_pv = idesc_i8(1, 0, 0, 128, 16);
-      int jj = 0, ii = 0;
-      int pend = -1;                                   // block whose PV is still to issue
-      bool ok = true;
       auto issue_pv = [&](int jb) -> bool {
         const int ab = jb & 1, st = jb % kDecStages;
         if (!mbar_poll(&bars[kDPFull + ab], (jb >> 1) & 1, abort_flag, p.err)) return false;
@@ -195,151 +210,162 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
         umma_commit(&bars[kDPEmpty + ab]);
         return true;
       };
-      for (int it = blockIdx.x; ok && it < total; it += gridDim.x) {
-        DecItem w;
-        if (dec_item(p, max_splits, it, w) != 1) continue;
-        const int qb = ii & 1;
-        if (!mbar_poll(&bars[kDQFull + qb], (ii >> 1) & 1, abort_flag, p.err)) { ok = false; break; }
-        const uint32_t sq = smem_u32(smem + L::kQ + qb * 2048);
-        for (int blk = w.blo; blk < w.bhi; ++blk, ++jj) {
-          const int st = jj % kDecStages, sb = jj & 1;
-          if (!mbar_poll(&bars[kDFull + st], (jj / kDecStages) & 1, abort_flag, p.err)) { ok = false; break; }
-          if (!mbar_poll(&bars[kDSEmpty + sb], ((jj >> 1) & 1) ^ 1, abort_flag, p.err)) { ok = false; break; }
-          tc_fence_after();
-          const uint32_t sk = smem_u32(smem + st * L::kStage);
-#pragma unroll
-          for (int kk = 0; kk < DH / 32; ++kk)
-            umma_i8(tmem + sb * 16, umma_desc(sk + kk * 32, 16, 1024, 2), umma_desc(sq + kk * 32, 16, 1024, 2),
-                    idesc_qk, kk > 0);
-          umma_commit(&bars[kDSFull + sb]);
-          if (pend >= 0 && !issue_pv(pend)) { ok = false; break; }
-          pend = jj;
-          if (blk + 1 == w.bhi) {                        // item end: Q is free, flush the last PV
-            umma_commit(&bars[kDQEmpty + qb]);
-            if (!issue_pv(pend)) { ok = false; break; }
-            pend = -1;
-          }
+      DecIter itr;
+      itr.init(p);
+      int jj = 0, run = -1, cur_bg = -1, b, g, blk;
+      bool ok = true;
+      while (ok && itr.next(p, b, g, blk)) {
+        const int bg = b * p.KVH + g;
+        if (bg != cur_bg) {
+          // every QK of the previous (sequence, kv head) is issued: its Q^T buffer frees when they finish
+          if (run >= 0) umma_commit(&bars[kDQEmpty + (run & 1)]);
+          cur_bg = bg;
+          ++run;
+          if (!mbar_poll(&bars[kDQFull + (run & 1)], (run >> 1) & 1, abort_flag, p.err)) { ok = false; break; }
         }
-        ++ii;
+        const uint32_t sq = smem_u32(smem + L::kQ + (run & 1) * 2048);
+        const int st = jj % kDecStages, sb = jj & 1;
+        if (!mbar_poll(&bars[kDFull + st], (jj / kDecStages) & 1, abort_flag, p.err)) { ok = false; break; }
+        if (!mbar_poll(&bars[kDSEmpty + sb], ((jj >> 1) & 1) ^ 1, abort_flag, p.err)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t sk = smem_u32(smem + st * L::kStage);
+#pragma unroll
+        for (int kk = 0; kk < DH / 32; ++kk)
+          umma_i8(tmem + sb * 16, umma_desc(sk + kk * 32, 16, 1024, 2), umma_desc(sq + kk * 32, 16, 1024, 2),
+                  idesc_qk, kk > 0);
+        umma_commit(&bars[kDSFull + sb]);
+        if (jj > 0 && !issue_pv(jj - 1)) { ok = false; break; }   // PV lags QK by one block
+        ++jj;
       }
+      if (ok && jj > 0) issue_pv(jj - 1);
     }
   } else {
     // ================================================================ workers
     const int wq = warp & 3;
     const int t = wq * 32 + lane;                        // TMEM lane: key (S) / channel (A)
     const uint32_t lanebase = tmem + ((uint32_t)(wq * 32) << 16);
-    int jj = 0;
-    bool ok = true;                                    // identical on all 128 workers (barrier-decided)
-    for (int it = blockIdx.x; ok && it < total; it += gridDim.x) {
-      DecItem w;
-      const int kind = dec_item(p, max_splits, it, w);
-      if (kind == 2 && t == 0) atomicOr(p.err, kDevBadPage);
-      if (kind != 1) continue;
-      const long long bg = (long long)w.b * p.KVH + w.g;
-      int eqh[GQ];
+    DecIter itr;
+    itr.init(p);
+    int jj = 0, cur_bg = -1, b, g, blk;
+    bool bad = false;                                    // this warp gave up a wait (decided at a barrier)
+    int eqh[GQ];
+    // the previous block: its A partial is read out one block later, its M after the next barrier
+    bool have_prev = false;
+    long long prev_bg = 0;
+    int prev_blk = 0, prev_L = 0;
+    auto readout_A = [&](int jb, long long bgx, int blkx) -> bool {
+      const int ab = jb & 1;
+      const bool okw = warp_poll(&bars[kDAFull + ab], (jb >> 1) & 1, abort_flag, p.err);
+      if (okw) {
+        tc_fence_after();
+        uint32_t a[8];
+        tmem_ld8(lanebase + 32 + ab * 16, a);
+        tc_wait_ld();
+        tc_fence_before();
+        mbar_arrive(&bars[kDAEmpty + ab]);
+        int32_t* dstA = p.partA + ((bgx * p.max_blocks + blkx) * gq) * DH;
 #pragma unroll
-      for (int h = 0; h < GQ; ++h) eqh[h] = (h < gq) ? p.eq[(long long)w.b * p.H + w.g * gq + h] : 0;
-      // partials of block jb: A from TMEM (thread = channel), then NB / l_b / eh0 by threads < gq
-      auto readout_A = [&](int jb, int blk) -> bool {
-        const int ab = jb & 1;
-        const bool okw = warp_poll(&bars[kDAFull + ab], (jb >> 1) & 1, abort_flag, p.err);
-        if (okw) {
-          tc_fence_after();
-          uint32_t a[8];
-          tmem_ld8(lanebase + 32 + ab * 16, a);
-          tc_wait_ld();
-          tc_fence_before();
-          mbar_arrive(&bars[kDAEmpty + ab]);
-          int32_t* dstA = p.partA + ((bg * p.max_blocks + blk) * gq) * DH;
-#pragma unroll
-          for (int h = 0; h < GQ; ++h) if (h < gq) __stcg(dstA + h * DH + t, (int32_t)a[h]);
-        }
-        return okw;
-      };
-      auto write_M = [&](int jb, int blk) {             // after a barrier that follows block jb's l_b atomics
-        const int par = jb & 1;
-        if (t < gq) {
-          const int e0 = (SINK && blk == 0 && w.L > 1) ? eh0s[t] : 0;
-          __stcg(&p.partM[(bg * p.max_blocks + blk) * gq + t], make_int4(nbs[par * 8 + t], (int)lbsum[par * 8 + t], e0, 0));
-          lbsum[par * 8 + t] = 0u;
-        }
-      };
-      bool bad = false;                                  // this warp gave up a wait (decided at the next barrier)
-      for (int blk = w.blo; blk < w.bhi; ++blk, ++jj) {
-        const int sb = jj & 1, par = jj & 1;
-        const int ekb = p.ek[bg * p.max_blocks + blk];
-        bool okw = warp_poll(&bars[kDSFull + sb], (jj >> 1) & 1, abort_flag, p.err);
-        int S[8];
-        if (okw) {
-          tc_fence_after();
-          tmem_ld8(lanebase + sb * 16, reinterpret_cast<uint32_t*>(S));
-          tc_wait_ld();
-          tc_fence_before();
-          mbar_arrive(&bars[kDSEmpty + sb]);
-        }
-        const int nkeys = min(kKB, w.L - blk * kKB);
-        if (t >= nkeys) {
-#pragma unroll
-          for (int h = 0; h < GQ; ++h) S[h] = INT32_MIN;  // keys past the sequence end
-        }
-#pragma unroll
-        for (int h = 0; h < GQ; ++h) {
-          const int wm = (int)redux_max_s32(S[h]);
-          if (lane == 0) redmax[(par * 4 + wq) * 8 + h] = wm;
-        }
-        uint32_t Gh[GQ];
-        int dmh[GQ];
-#pragma unroll
-        for (int h = 0; h < GQ; ++h) {                    // independent of the block max: before the barrier
-          Gh[h] = g_fold(p.gbase, eqh[h] + ekb);
-          dmh[h] = 1 << max(0, 30 - (31 - __clz((int)Gh[h])));
-        }
-        // every worker meets here once per block; the OR makes giving up a group decision
-        if (bar_any(1, 128, bad || !okw || *abort_flag != 0)) { ok = false; break; }
-        if (blk > w.blo) write_M(jj - 1, blk - 1);       // block jb - 1's l_b atomics are complete
-        uint32_t e[GQ];
-#pragma unroll
-        for (int h = 0; h < GQ; ++h) {
-          const int m = max(max(redmax[(par * 4 + 0) * 8 + h], redmax[(par * 4 + 1) * 8 + h]),
-                            max(redmax[(par * 4 + 2) * 8 + h], redmax[(par * 4 + 3) * 8 + h]));
-          const uint32_t G = Gh[h];
-          const int nbv = nb_of(m, G);
-          const int sc = max(S[h], m - dmh[h]);
-          const uint32_t d = ((uint32_t)nbv << kBHI) + (uint32_t)sc * (0u - G);
-          e[h] = (h < gq && t < nkeys) ? (uint32_t)tab[min(d >> kIdxShift, (uint32_t)kTabLive)] : 0u;
-          if (t == 0) nbs[par * 8 + h] = nbv;
-        }
-        if (SINK && blk == 0 && t == 0 && w.L > 1) {    // key 0's weight stays out of the P operand
-#pragma unroll
-          for (int h = 0; h < GQ; ++h) eh0s[h] = (int)e[h];
-        }
-        // P^T[head][key] in 8-head x 16-key core matrices: (key / 16) * 256 + (h / 8) * 128 + (h % 8) * 16 + key % 16
-        if (!warp_poll(&bars[kDPEmpty + par], ((jj >> 1) & 1) ^ 1, abort_flag, p.err)) bad = true;
-        uint8_t* pd = smem + L::kP + par * 2048 + (t >> 4) * 256 + (t & 15);
-#pragma unroll
-        for (int h = 0; h < GQ; ++h) {                    // rows >= gq of P^T only feed ignored columns of A
-          if (h < gq) {
-            const uint32_t pe = (SINK && blk == 0 && t == 0 && w.L > 1) ? 0u : e[h];
-            pd[(h >> 3) * 128 + (h & 7) * 16] = (uint8_t)pe;
-          }
-        }
-#pragma unroll
-        for (int h = 0; h < GQ; ++h) {
-          if (h < gq) {
-            const uint32_t s = redux_add_u32(e[h]);
-            if (lane == 0) atomicAdd(&lbsum[par * 8 + h], s);
-          }
-        }
-        fence_async_smem();
-        mbar_arrive(&bars[kDPFull + par]);
-        if (blk > w.blo && !readout_A(jj - 1, blk - 1)) bad = true;
+        for (int h = 0; h < GQ; ++h) if (h < gq) __stcg(dstA + h * DH + t, (int32_t)a[h]);
       }
-      if (!ok) break;                                    // (decided at a barrier: uniform)
-      // the item's last block: its l_b atomics meet at one more barrier, then its A, then the ticket
-      if (bar_any(1, 128, bad || *abort_flag != 0)) { ok = false; break; }
-      write_M(jj - 1, w.bhi - 1);
-      if (!readout_A(jj - 1, w.bhi - 1)) bad = true;
-      if (bar_any(1, 128, bad || *abort_flag != 0)) { ok = false; break; }
+      return okw;
+    };
+    auto write_M = [&](int jb, long long bgx, int blkx, int Lx) {   // after a barrier that follows jb's atomics
+      const int par = jb & 1;
+      if (t < gq) {
+        const int e0 = (SINK && blkx == 0 && Lx > 1) ? eh0s[par * 8 + t] : 0;
+        __stcg(&p.partM[(bgx * p.max_blocks + blkx) * gq + t], make_int4(nbs[par * 8 + t], (int)lbsum[par * 8 + t], e0, 0));
+        lbsum[par * 8 + t] = 0u;
+      }
+    };
+    while (itr.next(p, b, g, blk)) {
+      const long long bg = (long long)b * p.KVH + g;
+      if (bg != cur_bg) {
+        cur_bg = bg;
+#pragma unroll
+        for (int h = 0; h < GQ; ++h) eqh[h] = (h < gq) ? p.eq[(long long)b * p.H + g * gq + h] : 0;
+      }
+      const int Lb = itr.L;
+      const int sb = jj & 1, par = jj & 1;
+      const int ekb = p.ek[bg * p.max_blocks + blk];
+      bool okw = warp_poll(&bars[kDSFull + sb], (jj >> 1) & 1, abort_flag, p.err);
+      int S[8];
+      if (okw) {
+        tc_fence_after();
+        tmem_ld8(lanebase + sb * 16, reinterpret_cast<uint32_t*>(S));
+        tc_wait_ld();
+        tc_fence_before();
+        mbar_arrive(&bars[kDSEmpty + sb]);
+      }
+      const int nkeys = min(kKB, Lb - blk * kKB);
+      if (t >= nkeys) {
+#pragma unroll
+        for (int h = 0; h < 8; ++h) S[h] = INT32_MIN;  // keys past the sequence end
+      }
+#pragma unroll
+      for (int h = 0; h < GQ; ++h) {
+        const int wm = (int)redux_max_s32(S[h]);
+        if (lane == 0) redmax[(par * 4 + wq) * 8 + h] = wm;
+      }
+      uint32_t Gh[GQ];
+      int dmh[GQ];
+#pragma unroll
+      for (int h = 0; h < GQ; ++h) {                    // independent of the block max: before the barrier
+        Gh[h] = g_fold(p.gbase, eqh[h] + ekb);
+        dmh[h] = 1 << max(0, 30 - (31 - __clz((int)Gh[h])));
+      }
+      // every worker meets here once per block; the OR makes giving up a group decision
+      if (bar_any(1, 128, bad || !okw || *abort_flag != 0)) { have_prev = false; break; }
+      if (have_prev) write_M(jj - 1, prev_bg, prev_blk, prev_L);   // the previous block's l_b atomics are complete
+      uint32_t e[GQ];
+#pragma unroll
+      for (int h = 0; h < GQ; ++h) {
+        const int m = max(max(redmax[(par * 4 + 0) * 8 + h], redmax[(par * 4 + 1) * 8 + h]),
+                          max(redmax[(par * 4 + 2) * 8 + h], redmax[(par * 4 + 3) * 8 + h]));
+        const uint32_t G = Gh[h];
+        const int nbv = nb_of(m, G);
+        const int sc = max(S[h], m - dmh[h]);
+        const uint32_t d = ((uint32_t)nbv << kBHI) + (uint32_t)sc * (0u - G);
+        e[h] = (h < gq && t < nkeys) ? (uint32_t)tab[min(d >> kIdxShift, (uint32_t)kTabLive)] : 0u;
+        if (t == 0) nbs[par * 8 + h] = nbv;
+      }
+      const bool key0 = SINK && blk == 0 && t == 0 && Lb > 1;
+      if (key0) {                                        // key 0's weight stays out of the P operand
+#pragma unroll
+        for (int h = 0; h < GQ; ++h) eh0s[par * 8 + h] = (int)e[h];
+      }
+      // P^T[head][key] in 8-head x 16-key core matrices: (key / 16) * 256 + (h / 8) * 128 + (h % 8) * 16 + key % 16
+      if (!warp_poll(&bars[kDPEmpty + par], ((jj >> 1) & 1) ^ 1, abort_flag, p.err)) bad = true;
+      uint8_t* pd = smem + L::kP + par * 2048 + (t >> 4) * 256 + (t & 15);
+#pragma unroll
+      for (int h = 0; h < GQ; ++h) {                     // rows >= gq of P^T only feed ignored columns of A
+        if (h < gq) pd[(h >> 3) * 128 + (h & 7) * 16] = (uint8_t)(key0 ? 0u : e[h]);
+      }
+#pragma unroll
+      for (int h = 0; h < GQ; ++h) {
+        if (h < gq) {
+          const uint32_t sum = redux_add_u32(e[h]);
+          if (lane == 0) atomicAdd(&lbsum[par * 8 + h], sum);
+        }
+      }
+      fence_async_smem();
+      mbar_arrive(&bars[kDPFull + par]);
+      if (have_prev && !readout_A(jj - 1, prev_bg, prev_blk)) bad = true;
+      have_prev = true;
+      prev_bg = bg;
+      prev_blk = blk;
+      prev_L = Lb;
+      ++jj;
+    }
+    // the last block: its l_b atomics meet at one more barrier, then its partials
+    if (have_prev && !bar_any(1, 128, bad || *abort_flag != 0)) {
+      write_M(jj - 1, prev_bg, prev_blk, prev_L);
+      readout_A(jj - 1, prev_bg, prev_blk);
+    }
+    if (t == 0) {                                        // sequences the lattice arrays are too short for
+      for (int bb = blockIdx.x; bb < p.B; bb += gridDim.x) {
+        const int Lx = p.seq_lens[bb];
+        if ((Lx + kKB - 1) / kKB > p.max_blocks || (Lx + 15) / 16 > p.max_pages) atomicOr(p.err, kDevBadPage);
+      }
     }
   }
 
