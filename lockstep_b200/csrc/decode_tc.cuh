@@ -380,18 +380,25 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
 }
 
 // The committed-order refold of every (sequence, kv head, head) from its exact block partials:
-// one CTA per (kv head, sequence, head of the group), one thread per channel.  Each 32-block
-// segment of the head's partial rows (32 x 512 contiguous bytes) is staged into shared memory
-// with cp.async in one round trip, then every thread folds its channel in the committed order:
-// blocks ascending into the segment, segments into the row (reference/lssab8_golden.py:257-335,
-// 350-394), then one RN division.
+// one CTA per (kv head, sequence, head of the group), one thread per channel.  Per 32-block
+// segment: the partial rows (32 x 512 contiguous bytes) are staged into shared memory with
+// cp.async; warp 0 derives the segment's fold schedule, which depends on the block and head only
+// (running max by a prefix-max scan, rescale distance D, skip distance s, the scale
+// 2^-(s + e_v), and l folded by one lane); then every thread folds its channel with one exact
+// multiply-add per block (reference/lssab8_golden.py:257-335, 350-394).  A block past the skip
+// window gets scale +0, which leaves O bit-identical (O is never -0).
 template <bool SINK, typename OutT>
 __global__ void __launch_bounds__(128) decode_merge_kernel(const DecodeArgs p) {
   constexpr int DH = 128;
   __shared__ __align__(16) int sA[kSEG][DH];
   __shared__ int2 sM[kSEG];
   __shared__ int sEv[kSEG];
+  __shared__ int sD[kSEG];                 // rescale distance before block u (0: none)
+  __shared__ float sSc[kSEG];              // 2^-(s_u + e_v,u), or +0 past the skip window
+  __shared__ int sSeg[4];                  // segment -> row: D2, s2 (and the segment's NB)
+  __shared__ float sLrow;
   const int g = blockIdx.x, b = blockIdx.y, h = blockIdx.z, c = threadIdx.x;
+  const int lane = c & 31;
   const int gq = p.group;
   const int L = p.seq_lens[b];
   const int nblk = (L + kKB - 1) / kKB;
@@ -404,7 +411,7 @@ __global__ void __launch_bounds__(128) decode_merge_kernel(const DecodeArgs p) {
     evs0 = p.ev0[bg];
     eh0 = __ldcg(&p.partM[(bg * p.max_blocks) * gq + h]).z;
   }
-  float Orow = 0.0f, lrow = 0.0f;
+  float Orow = 0.0f, lrow = 0.0f;          // lrow: warp 0 lane 0 only
   int nbrow = 0;
   for (int s0 = 0; s0 < nblk; s0 += kSEG) {
     const int n = min(kSEG, nblk - s0);
@@ -414,38 +421,72 @@ __global__ void __launch_bounds__(128) decode_merge_kernel(const DecodeArgs p) {
       asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(&sA[u][q * 4])), "l"(src) : "memory");
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
-    if (c < n) {
-      sM[c] = __ldcg(reinterpret_cast<const int2*>(&p.partM[(bg * p.max_blocks + s0 + c) * gq + h]));
-      sEv[c] = p.ev[bg * p.max_blocks + s0 + c];
+    if (c < 32) {
+      // ---- the segment's schedule: lane u owns block u
+      const bool live = lane < n;
+      int2 m = make_int2(INT32_MIN, 0);
+      int ev = 0;
+      if (live) {
+        m = __ldcg(reinterpret_cast<const int2*>(&p.partM[(bg * p.max_blocks + s0 + lane) * gq + h]));
+        ev = p.ev[bg * p.max_blocks + s0 + lane];
+      }
+      int run = m.x;                                         // inclusive prefix max of NB_b
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, run, o);
+        if (lane >= o) run = max(run, y);
+      }
+      int prev = __shfl_up_sync(0xffffffffu, run, 1);        // running max before block u
+      const int nb0 = __shfl_sync(0xffffffffu, m.x, 0);
+      if (lane == 0) prev = nb0;                             // block 0 opens the segment
+      const int D = live ? m.x - prev : 0;
+      const int sg = D > 0 ? 0 : -D;
+      const bool add = sg <= kSWIN;
+      if (live) {
+        sM[lane] = m;
+        sEv[lane] = ev;
+        sD[lane] = D > 0 ? D : 0;
+        sSc[lane] = add ? pow2f(-(sg + ev)) : 0.0f;
+      }
+      __syncwarp();
+      if (lane == 0) {                                       // l: the same rules, in order
+        float lseg = 0.0f;
+        int nbrun = sM[0].x;
+        for (int u = 0; u < n; ++u) {
+          const int Du = sM[u].x - nbrun;
+          int su = 0;
+          if (Du > 0) { lseg = rescale(lseg, Du); nbrun = sM[u].x; }
+          else su = -Du;
+          if (su <= kSWIN) lseg = fold_term(lseg, sM[u].y, pow2f(-su));
+        }
+        // segment -> row (reference/lssab8_golden.py:317-331)
+        if (s0 == 0) nbrow = nbrun;
+        const int D2 = nbrun - nbrow;
+        int s2 = 0;
+        if (D2 > 0) { lrow = rescale(lrow, D2); nbrow = nbrun; }
+        else s2 = -D2;
+        if (s2 <= kSWIN) lrow = __fadd_rn(lrow, rescale(lseg, s2));
+        sSeg[0] = D2 > 0 ? D2 : 0;
+        sSeg[1] = s2;
+        sLrow = lrow;
+      }
     }
     asm volatile("cp.async.wait_group 0;" ::: "memory");
     __syncthreads();
-    float O = 0.0f, lseg = 0.0f;
-    int nbrun = sM[0].x;
+    float O = 0.0f;
     for (int u = 0; u < n; ++u) {
-      const int2 m = sM[u];
-      const int D = m.x - nbrun;
-      int sg = 0;
-      if (D > 0) { O = rescale(O, D); lseg = rescale(lseg, D); nbrun = m.x; }
-      else sg = -D;
-      if (sg <= kSWIN) {
-        if (SINK && s0 + u == 0 && L > 1) O = fold_term(O, eh0 * v0c, pow2f(-(sg + evs0)));
-        O = fold_term(O, sA[u][c], pow2f(-(sg + sEv[u])));
-        lseg = fold_term(lseg, m.y, pow2f(-sg));
-      }
+      const int Du = sD[u];
+      if (Du > 0) O = rescale(O, Du);                        // block-uniform branch
+      if (SINK && s0 + u == 0 && L > 1) O = fold_term(O, eh0 * v0c, pow2f(-evs0));
+      O = fold_term(O, sA[u][c], sSc[u]);
     }
-    __syncthreads();                                       // the stage is refilled next
-    if (s0 == 0) nbrow = nbrun;                            // segment -> row (reference/lssab8_golden.py:317-331)
-    const int D2 = nbrun - nbrow;
-    int s2 = 0;
-    if (D2 > 0) { Orow = rescale(Orow, D2); lrow = rescale(lrow, D2); nbrow = nbrun; }
-    else s2 = -D2;
-    if (s2 <= kSWIN) {
-      Orow = __fadd_rn(Orow, rescale(O, s2));
-      lrow = __fadd_rn(lrow, rescale(lseg, s2));
-    }
+    const int D2 = sSeg[0], s2 = sSeg[1];
+    if (D2 > 0) Orow = rescale(Orow, D2);
+    if (s2 <= kSWIN) Orow = __fadd_rn(Orow, rescale(O, s2));
+    __syncthreads();                                         // the stage and schedule are refilled next
   }
-  const float y = (lrow != 0.0f) ? __fdiv_rn(Orow, lrow) : 0.0f;
+  const float lr = sLrow;
+  const float y = (lr != 0.0f) ? __fdiv_rn(Orow, lr) : 0.0f;
   OutT* dst = reinterpret_cast<OutT*>(p.out) + b * p.os0 + (long long)(g * gq + h) * p.os1 + c * p.os2;
   *dst = from_f32<OutT>(y);
 }
