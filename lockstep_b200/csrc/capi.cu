@@ -9,6 +9,7 @@
 
 #include <cstdio>
 #include <algorithm>
+#include <utility>
 #include <cstring>
 #include <mutex>
 
@@ -223,6 +224,23 @@ int launch_decode_out(int out_dtype, const DecodeArgs& a, int max_splits, cudaSt
   }
 }
 
+// Launch with programmatic dependent launch: the kernel may start while the previous kernel on
+// the stream finishes; it executes griddepcontrol.wait before it reads that kernel's output.
+template <typename... KArgs, typename... Args>
+int launch_pdl(void (*kfn)(KArgs...), dim3 grid, dim3 block, int smem, cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = (size_t)smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cuda_rc(cudaLaunchKernelEx(&cfg, kfn, std::forward<Args>(args)...));
+}
+
 template <bool SINK, typename OutT, int GQ>
 int launch_decode_tc_t(const DecodeArgs& a, int max_splits, int num_sms, cudaStream_t st) {
   CUtensorMap tk, tq;
@@ -235,10 +253,8 @@ int launch_decode_tc_t(const DecodeArgs& a, int max_splits, int num_sms, cudaStr
   (void)max_splits;     // exact block partials: the streaming kernel schedules blocks, not splits
   const long long chunks = ((long long)a.B * a.KVH * a.max_blocks + kDecChunk - 1) / kDecChunk;
   const int grid = (int)std::min<long long>(chunks, 2LL * std::max(num_sms, 1));   // two CTAs per SM
-  kfn<<<grid, kDecThreads, smem, st>>>(tk, tq, a);
-  if ((rc = launch_rc())) return rc;
-  decode_merge_kernel<SINK, OutT><<<dim3(a.KVH, a.B, a.group), 128, 0, st>>>(a);
-  return launch_rc();
+  if ((rc = launch_pdl(kfn, dim3(grid), dim3(kDecThreads), smem, st, tk, tq, a))) return rc;
+  return launch_pdl(decode_merge_kernel<SINK, OutT>, dim3(a.KVH, a.B, a.group), dim3(128), 0, st, a);
 }
 
 template <bool SINK>
@@ -533,8 +549,10 @@ int lssab8_decode(const void* q, int dtype, const int64_t* qs, int B, int H, int
   int32_t* eq = reinterpret_cast<int32_t*>(base + w.eq);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int64_t q4[4] = {qs[0], qs[1], 0, qs[2]};
-  if ((rc = lssab8_quant_rows(q, dtype, B, H, 1, dh, q4, 1, q8, eq, stream))) return rc;
+  // (the ticket reset comes first so the query quantiser directly precedes the decode kernel,
+  // which may then start under programmatic dependent launch)
   if (cudaMemsetAsync(base + w.tickets, 0, (size_t)B * KVH * 4, s) != cudaSuccess) return kErrCuda;
+  if ((rc = lssab8_quant_rows(q, dtype, B, H, 1, dh, q4, 1, q8, eq, stream))) return rc;
   DecodeArgs a{};
   a.B = B; a.H = H; a.KVH = KVH; a.dh = dh; a.group = H / KVH; a.max_blocks = max_blocks; a.max_pages = max_pages;
   a.split_blocks = split_blocks; a.num_pages = num_pages; a.seq_lens = seq_lens; a.block_table = block_table;

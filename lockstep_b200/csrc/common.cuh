@@ -169,6 +169,11 @@ __device__ __forceinline__ int nb_of(int m, uint32_t G) {
   return (int)((sg + ((1ll << kBHI) - 1)) >> kBHI);
 }
 
+// Programmatic dependent launch: allow the next kernel on the stream to start launching, and
+// wait for the previous kernel's completion and memory (a no-op when launched without PDL).
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // ------------------------------------------------------------------ bounded waits + PTX
 __device__ __forceinline__ uint64_t globaltimer() {
   uint64_t t;

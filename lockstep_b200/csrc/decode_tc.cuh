@@ -152,6 +152,8 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_launch_dependents();                             // the refold kernel may queue up behind us
+  pdl_wait();                                          // the query quantiser's q8 / eq are complete
 
   if (warp == 0) {
     // ================================================================ TMA producer
@@ -397,6 +399,7 @@ __global__ void __launch_bounds__(128) decode_merge_kernel(const DecodeArgs p) {
   __shared__ float sSc[kSEG];              // 2^-(s_u + e_v,u), or +0 past the skip window
   __shared__ int sSeg[4];                  // segment -> row: D2, s2 (and the segment's NB)
   __shared__ float sLrow;
+  pdl_wait();                                          // every block partial is written
   const int g = blockIdx.x, b = blockIdx.y, h = blockIdx.z, c = threadIdx.x;
   const int lane = c & 31;
   const int gq = p.group;

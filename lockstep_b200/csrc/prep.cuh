@@ -151,6 +151,7 @@ template <typename InT, int DH>
 __global__ void __launch_bounds__(256)
 quant_rows_vec_kernel(const InT* __restrict__ x, Strides4 xs, int B, int H, int T, int Tpad,
                       int8_t* __restrict__ q8, int32_t* __restrict__ eq) {
+  pdl_launch_dependents();                             // a PDL-launched consumer may start its setup
   constexpr int N = Vec16<InT>::kN;
   constexpr int G = DH / N;                            // lanes per row
   constexpr int RPW = 32 / G;                          // rows per warp
