@@ -175,9 +175,26 @@ int with_in_dtype(int dtype, F&& f) {
   }
 }
 
+// Launch with programmatic dependent launch: the kernel may start while the previous kernel on
+// the stream finishes; it executes griddepcontrol.wait before it reads that kernel's output.
+template <typename... KArgs, typename... Args>
+int launch_pdl(void (*kfn)(KArgs...), dim3 grid, dim3 block, int smem, cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = (size_t)smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cuda_rc(cudaLaunchKernelEx(&cfg, kfn, std::forward<Args>(args)...));
+}
+
 template <int DH, bool SINK, typename OutT>
 int launch_prefill_t(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const PrefillArgs& a,
-                     cudaStream_t st) {
+                     int num_sms, cudaStream_t st) {
   using L = PrefillSmem<DH>;
   const int multi = a.nblk > kSEG;
   if (multi && !a.orow) return kErrWorkspace;
@@ -187,18 +204,18 @@ int launch_prefill_t(const CUtensorMap& tq, const CUtensorMap& tk, const CUtenso
   if (smem < 116 * 1024) smem = 116 * 1024;
   auto kfn = multi ? prefill_kernel<DH, SINK, OutT, true> : prefill_kernel<DH, SINK, OutT, false>;
   if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return kErrCuda;
-  dim3 grid(a.Tpad / 128, a.H, a.B);
-  kfn<<<grid, kPrefillThreads, smem, st>>>(tq, tk, tv, a);
-  return launch_rc();
+  const long long items = (long long)(a.Tpad / 128) * a.H * a.B;      // persistent: one CTA per SM
+  const int grid = (int)std::min<long long>(items, (long long)std::max(num_sms, 1));
+  return launch_pdl(kfn, dim3(grid), dim3(kPrefillThreads), smem, st, tq, tk, tv, a);
 }
 
 template <int DH, bool SINK>
 int launch_prefill_out(int out_dtype, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
-                       const PrefillArgs& a, cudaStream_t st) {
+                       const PrefillArgs& a, int num_sms, cudaStream_t st) {
   switch (out_dtype) {
-    case kF32: return launch_prefill_t<DH, SINK, float>(tq, tk, tv, a, st);
-    case kF16: return launch_prefill_t<DH, SINK, __half>(tq, tk, tv, a, st);
-    case kBF16: return launch_prefill_t<DH, SINK, __nv_bfloat16>(tq, tk, tv, a, st);
+    case kF32: return launch_prefill_t<DH, SINK, float>(tq, tk, tv, a, num_sms, st);
+    case kF16: return launch_prefill_t<DH, SINK, __half>(tq, tk, tv, a, num_sms, st);
+    case kBF16: return launch_prefill_t<DH, SINK, __nv_bfloat16>(tq, tk, tv, a, num_sms, st);
     default: return kErrArg;
   }
 }
@@ -222,23 +239,6 @@ int launch_decode_out(int out_dtype, const DecodeArgs& a, int max_splits, cudaSt
     case kBF16: return launch_decode_t<DH, SINK, __nv_bfloat16>(a, max_splits, st);
     default: return kErrArg;
   }
-}
-
-// Launch with programmatic dependent launch: the kernel may start while the previous kernel on
-// the stream finishes; it executes griddepcontrol.wait before it reads that kernel's output.
-template <typename... KArgs, typename... Args>
-int launch_pdl(void (*kfn)(KArgs...), dim3 grid, dim3 block, int smem, cudaStream_t st, Args&&... args) {
-  cudaLaunchConfig_t cfg{};
-  cfg.gridDim = grid;
-  cfg.blockDim = block;
-  cfg.dynamicSmemBytes = (size_t)smem;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cuda_rc(cudaLaunchKernelEx(&cfg, kfn, std::forward<Args>(args)...));
 }
 
 template <bool SINK, typename OutT, int GQ>
@@ -464,10 +464,10 @@ int lssab8_prefill_lattice(const int8_t* q8, const int32_t* eq, const int8_t* k8
   a.err = ds->err;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool sink = ev0 != nullptr;
-  if (dh == 128) return sink ? launch_prefill_out<128, true>(out_dtype, tq, tk, tv, a, st)
-                             : launch_prefill_out<128, false>(out_dtype, tq, tk, tv, a, st);
-  return sink ? launch_prefill_out<64, true>(out_dtype, tq, tk, tv, a, st)
-              : launch_prefill_out<64, false>(out_dtype, tq, tk, tv, a, st);
+  if (dh == 128) return sink ? launch_prefill_out<128, true>(out_dtype, tq, tk, tv, a, ds->num_sms, st)
+                             : launch_prefill_out<128, false>(out_dtype, tq, tk, tv, a, ds->num_sms, st);
+  return sink ? launch_prefill_out<64, true>(out_dtype, tq, tk, tv, a, ds->num_sms, st)
+              : launch_prefill_out<64, false>(out_dtype, tq, tk, tv, a, ds->num_sms, st);
 }
 
 size_t lssab8_prefill_workspace_size(int B, int H, int KVH, int T, int dh) {

@@ -1,11 +1,16 @@
 // LSSA-B8 causal / GQA prefill on sm_100a: tcgen05 int8 MMA with TMEM accumulators.
 //
-// One CTA = one (batch, query head, 128-row query tile).  It walks the key blocks
-// 0 .. tile ASCENDING (the contract's committed order; a descending walk is a different
-// function, docs/contract/BLOCK_EXPONENT_VARIANT.md B8.6) with warp-specialised roles:
+// Persistent: one CTA per SM walks the (query tile, batch, head) work items, longest tiles first
+// in snake order, and for each item the key blocks 0 .. tile ASCENDING (the contract's
+// committed order; a descending walk is a different function,
+// docs/contract/BLOCK_EXPONENT_VARIANT.md B8.6).  Every pipeline (the TMA ring, S, P, A) runs on
+// counters that continue across items, so the next item's loads and QK overlap this item's
+// last folds and epilogue, and the setup (T2 copies, barriers, TMEM) is paid once per SM.
+// Warp-specialised roles:
 //
-//   warp 0      TMA producer: Q tile once, then K/V 128-key blocks into a 2-stage ring
-//               (plain cp.async.bulk.tensor, no multicast).
+//   warp 0      TMA producer: per item the Q tile (double-buffered across items) and key 0's
+//               value row, then K/V 128-key blocks into a 2-stage ring (plain
+//               cp.async.bulk.tensor, no multicast).
 //   warp 1      TMEM owner and MMA issuer (one thread):
 //                 S_b  = Q8 . K8_b^T   tcgen05.mma kind::i8, s8 x s8 -> s32, M=128 N=128 K=dh
 //                 A_b  = P_b . V8_b    tcgen05.mma kind::i8, u8 x s8 -> s32, M=128 N=dh K=128
@@ -70,20 +75,37 @@ constexpr int kTabBytes = kTabEntries * kTabCopies * 4;       // 73,792 B at the
 template <int DH>
 struct PrefillSmem {
   static constexpr int kTile = 128 * DH;                 // one Q/K/V tile, bytes
-  static constexpr int kQ = 0;
-  static constexpr int kK = kTile;                       // 2 stages
-  static constexpr int kV = 3 * kTile;                   // 2 stages
-  static constexpr int kP = 5 * kTile;                   // 2 x 16 KB, SW128 K-major u8
-  static constexpr int kV0 = kP + 2 * 16384;             // key 0's int8 value row (sink)
-  static constexpr int kBar = kV0 + 256;                 // mbarriers
+  static constexpr int kQ = 0;                           // 2 items
+  static constexpr int kK = 2 * kTile;                   // 2 stages
+  static constexpr int kV = 4 * kTile;                   // 2 stages
+  static constexpr int kP = 6 * kTile;                   // 2 x 16 KB, SW128 K-major u8
+  static constexpr int kV0 = kP + 2 * 16384;             // 2 items x key 0's int8 value row (sink)
+  static constexpr int kBar = kV0 + 2 * 128;             // mbarriers
   static constexpr int kMisc = kBar + 256;               // tmem base, abort flag
   static constexpr int kBytes = kMisc + 64;              // (+ the static T2 table)
 };
 
 enum BarId : int {
-  kBarQ = 0, kBarKFull = 1, kBarKEmpty = 3, kBarVFull = 5, kBarVEmpty = 7, kBarSFull = 9, kBarSEmpty = 10,
-  kBarPFull = 13, kBarPEmpty = 15, kBarAFull = 17, kBarAEmpty = 19
+  kBarQFull = 0, kBarKFull = 2, kBarKEmpty = 4, kBarVFull = 6, kBarVEmpty = 8, kBarSFull = 10, kBarSEmpty = 11,
+  kBarPFull = 12, kBarPEmpty = 14, kBarAFull = 16, kBarAEmpty = 18, kBarQEmpty = 20
 };
+
+// Work item i (i = 0 .. ntile * B * H - 1), longest first: query tile ntile - 1 - i / (B * H),
+// (b, h) = i % (B * H).  CTA k takes items r * G + k in even rounds r and r * G + G - 1 - k in odd
+// rounds (snake order, G = gridDim.x), which balances the decreasing item sizes.
+struct PfItem {
+  int tile, b, h;
+};
+__device__ __forceinline__ bool pf_item(const PrefillArgs& p, int ntile, int round, PfItem& it) {
+  const int G = gridDim.x;
+  const int i = round * G + ((round & 1) ? (G - 1 - (int)blockIdx.x) : (int)blockIdx.x);
+  if (i >= ntile * p.B * p.H) return false;
+  const int bh = i % (p.B * p.H);
+  it.tile = ntile - 1 - i / (p.B * p.H);
+  it.b = bh / p.H;
+  it.h = bh % p.H;
+  return true;
+}
 constexpr uint32_t kColS = 0, kColA = 128, kColO = 384;   // TMEM column map (A: two buffers of 128)
 
 // store n consecutive channels, vectorised when contiguous and aligned
@@ -122,20 +144,13 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
   int8_t* v0row = reinterpret_cast<int8_t*>(smem + L::kV0);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int ntile = gridDim.x;
-  const int tile = ntile - 1 - (int)blockIdx.x;      // longest rows first
-  const int h = blockIdx.y, b = blockIdx.z;
-  const int g = h / p.group;
-  const int nb = tile + 1;                           // causal: blocks 0 .. tile
-  const int qrow0 = (b * p.H + h) * p.Tpad + tile * 128;
-  const int krow0 = (b * p.KVH + g) * p.Tpad;
+  const int ntile = p.Tpad / 128;
+  const int nrounds = (ntile * p.B * p.H + (int)gridDim.x - 1) / (int)gridDim.x;
 
-  // ---- setup: barriers and the first loads (thread 0 is the TMA producer, so its loads need
-  // no CTA barrier; they overlap the table fill), then T2 copies and TMEM
-  const int npre = min(nb, 2);                       // stages that start empty
+  // ---- setup, once per CTA: barriers, T2 copies, TMEM
   if (threadIdx.x == 0) {
-    mbar_init(&bars[kBarQ], 1);
     for (int s = 0; s < 2; ++s) {
+      mbar_init(&bars[kBarQFull + s], 1);   mbar_init(&bars[kBarQEmpty + s], 1 + 256);
       mbar_init(&bars[kBarKFull + s], 1);   mbar_init(&bars[kBarKEmpty + s], 1);
       mbar_init(&bars[kBarVFull + s], 1);   mbar_init(&bars[kBarVEmpty + s], 1);
       mbar_init(&bars[kBarAFull + s], 1);   mbar_init(&bars[kBarAEmpty + s], 256);
@@ -145,14 +160,6 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
     mbar_init(&bars[kBarSEmpty], 256);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    mbar_expect_tx(&bars[kBarQ], L::kTile);
-    tma_load_2d(smem + L::kQ, &tm_q, 0, qrow0, &bars[kBarQ]);
-    for (int j = 0; j < npre; ++j) {
-      mbar_expect_tx(&bars[kBarKFull + j], L::kTile);
-      tma_load_2d(smem + L::kK + j * L::kTile, &tm_k, 0, krow0 + j * 128, &bars[kBarKFull + j]);
-      mbar_expect_tx(&bars[kBarVFull + j], L::kTile);
-      tma_load_2d(smem + L::kV + j * L::kTile, &tm_v, 0, krow0 + j * 128, &bars[kBarVFull + j]);
-    }
   }
   for (int k4 = threadIdx.x; k4 * 4 < kTabEntries; k4 += blockDim.x) {   // 4 entries per thread,
     const uint32_t word = (k4 * 4 < kTabLive) ? reinterpret_cast<const uint32_t*>(kT2Live)[k4] : 0u;
@@ -167,7 +174,6 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
       }
     }
   }
-  if (SINK && threadIdx.x < DH) v0row[threadIdx.x] = p.v8[(long long)krow0 * DH + threadIdx.x];
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(tmem_slot)) : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
@@ -189,19 +195,36 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  pdl_wait();                                        // the quantisers' lattice is complete
 
   if (warp == 0) {
     // ================================================================ TMA producer
     if (lane == 0) {
-      for (int j = npre; j < nb; ++j) {
-        const int s = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        if (!mbar_wait(&bars[kBarKEmpty + s], ph ^ 1, abort_flag, p.err, 128)) break;
-        mbar_expect_tx(&bars[kBarKFull + s], L::kTile);
-        tma_load_2d(smem + L::kK + s * L::kTile, &tm_k, 0, krow0 + j * 128, &bars[kBarKFull + s]);
-        if (!mbar_wait(&bars[kBarVEmpty + s], ph ^ 1, abort_flag, p.err, 128)) break;
-        mbar_expect_tx(&bars[kBarVFull + s], L::kTile);
-        tma_load_2d(smem + L::kV + s * L::kTile, &tm_v, 0, krow0 + j * 128, &bars[kBarVFull + s]);
+      int jj = 0, tt = 0;
+      bool ok = true;
+      PfItem it;
+      for (int rd = 0; ok && rd < nrounds; ++rd) {
+        if (!pf_item(p, ntile, rd, it)) continue;
+        const int g = it.h / p.group;
+        const int qrow0 = (it.b * p.H + it.h) * p.Tpad + it.tile * 128;
+        const int krow0 = (it.b * p.KVH + g) * p.Tpad;
+        const int qb = tt & 1;
+        // buffer qb is free once item tt - 2's last QK has finished and its workers are done
+        if (!mbar_wait(&bars[kBarQEmpty + qb], ((tt >> 1) & 1) ^ 1, abort_flag, p.err, 128)) { ok = false; break; }
+        mbar_expect_tx(&bars[kBarQFull + qb], L::kTile + (SINK ? DH : 0));
+        tma_load_2d(smem + L::kQ + qb * L::kTile, &tm_q, 0, qrow0, &bars[kBarQFull + qb]);
+        if (SINK) bulk_g2s(v0row + qb * 128, p.v8 + (long long)krow0 * DH, DH, &bars[kBarQFull + qb]);
+        for (int j = 0; j <= it.tile; ++j, ++jj) {
+          const int s = jj & 1;
+          const uint32_t ph = (jj >> 1) & 1;
+          if (!mbar_wait(&bars[kBarKEmpty + s], ph ^ 1, abort_flag, p.err, 128)) { ok = false; break; }
+          mbar_expect_tx(&bars[kBarKFull + s], L::kTile);
+          tma_load_2d(smem + L::kK + s * L::kTile, &tm_k, 0, krow0 + j * 128, &bars[kBarKFull + s]);
+          if (!mbar_wait(&bars[kBarVEmpty + s], ph ^ 1, abort_flag, p.err, 128)) { ok = false; break; }
+          mbar_expect_tx(&bars[kBarVFull + s], L::kTile);
+          tma_load_2d(smem + L::kV + s * L::kTile, &tm_v, 0, krow0 + j * 128, &bars[kBarVFull + s]);
+        }
+        ++tt;
       }
     }
   } else if (warp == 1) {
@@ -211,15 +234,15 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
       constexpr uint32_t kRowGroup = 8 * DH;                    // bytes per 8 rows of a tile
       constexpr uint32_t idesc_qk = idesc_i8(1, 1, 0, 128, 128);
       constexpr uint32_t idesc_pv = idesc_i8(0, 1, 1, 128, DH);
-      const uint32_t sq = smem_u32(smem + L::kQ);
-      bool ok = mbar_wait(&bars[kBarQ], 0, abort_flag, p.err);
-      auto issue_qk = [&](int j) -> bool {
-        const int s = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
+      int jj = 0, tt = 0;                                       // global block / item counters
+      bool ok = true;
+      auto issue_qk = [&](int jg, uint32_t sq) -> bool {
+        const int s = jg & 1;
+        const uint32_t ph = (jg >> 1) & 1;
         if (!mbar_wait(&bars[kBarKFull + s], ph, abort_flag, p.err)) return false;
-        // S is single-buffered: QK(j) waits until the chain has copied S(j - 1) into registers
-        // (the j-th phase of S_empty, j >= 1)
-        if (j > 0 && !mbar_wait(&bars[kBarSEmpty], (j - 1) & 1, abort_flag, p.err)) return false;
+        // S is single-buffered: QK(jg) waits until the chain has copied S(jg - 1) into registers
+        // (the jg-th phase of S_empty, jg >= 1)
+        if (jg > 0 && !mbar_wait(&bars[kBarSEmpty], (jg - 1) & 1, abort_flag, p.err)) return false;
         tc_fence_after();
         const uint32_t sk = smem_u32(smem + L::kK + s * L::kTile);
 #pragma unroll
@@ -231,28 +254,43 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
         umma_commit(&bars[kBarKEmpty + s]);
         return true;
       };
-      if (ok) ok = issue_qk(0);
-      for (int j = 0; ok && j < nb; ++j) {
-        if (j + 1 < nb && !issue_qk(j + 1)) break;
-        const int s = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        if (!mbar_wait(&bars[kBarPFull + s], ph, abort_flag, p.err)) break;
-        if (!mbar_wait(&bars[kBarVFull + s], ph, abort_flag, p.err)) break;
-        if (!mbar_wait(&bars[kBarAEmpty + s], ph ^ 1, abort_flag, p.err)) break;   // fold of block j - 2 done
-        tc_fence_after();
-        const uint32_t sp = smem_u32(smem + L::kP + s * 16384);
-        const uint32_t sv = smem_u32(smem + L::kV + s * L::kTile);
+      PfItem it;
+      for (int rd = 0; ok && rd < nrounds; ++rd) {
+        if (!pf_item(p, ntile, rd, it)) continue;
+        const int nb = it.tile + 1;
+        const int qb = tt & 1;
+        if (!mbar_wait(&bars[kBarQFull + qb], (tt >> 1) & 1, abort_flag, p.err)) { ok = false; break; }
+        const uint32_t sq = smem_u32(smem + L::kQ + qb * L::kTile);
+        ok = issue_qk(jj, sq);
+        if (ok && nb == 1) umma_commit(&bars[kBarQEmpty + qb]);   // the item's last QK is issued
+        for (int j = 0; ok && j < nb; ++j) {
+          const int jg = jj + j;
+          if (j + 1 < nb) {
+            if (!issue_qk(jg + 1, sq)) { ok = false; break; }
+            if (j + 2 == nb) umma_commit(&bars[kBarQEmpty + qb]);
+          }
+          const int s = jg & 1;
+          const uint32_t ph = (jg >> 1) & 1;
+          if (!mbar_wait(&bars[kBarPFull + s], ph, abort_flag, p.err)) { ok = false; break; }
+          if (!mbar_wait(&bars[kBarVFull + s], ph, abort_flag, p.err)) { ok = false; break; }
+          if (!mbar_wait(&bars[kBarAEmpty + s], ph ^ 1, abort_flag, p.err)) { ok = false; break; }   // fold of jg - 2 done
+          tc_fence_after();
+          const uint32_t sp = smem_u32(smem + L::kP + s * 16384);
+          const uint32_t sv = smem_u32(smem + L::kV + s * L::kTile);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          // A = P (K-major SW128, 32 keys = 32 bytes per step); B = V (MN-major: 32 keys =
-          // 4 groups of 8 rows per step; LBO = MN-atom stride (one atom), SBO = 8-row stride).
-          // Every step accumulates: the accumulator starts at the 1.5 * 2^23 bias.
-          umma_i8(tmem + kColA + s * 128, umma_desc(sp + kk * 32, 16, 1024, 2),
-                  umma_desc(sv + kk * 32 * DH, L::kTile, kRowGroup, kSwz), idesc_pv, 1u);
+          for (int kk = 0; kk < 4; ++kk) {
+            // A = P (K-major SW128, 32 keys = 32 bytes per step); B = V (MN-major: 32 keys =
+            // 4 groups of 8 rows per step; LBO = MN-atom stride (one atom), SBO = 8-row stride).
+            // Every step accumulates: the accumulator starts at the 1.5 * 2^23 bias.
+            umma_i8(tmem + kColA + s * 128, umma_desc(sp + kk * 32, 16, 1024, 2),
+                    umma_desc(sv + kk * 32 * DH, L::kTile, kRowGroup, kSwz), idesc_pv, 1u);
+          }
+          umma_commit(&bars[kBarAFull + s]);
+          umma_commit(&bars[kBarVEmpty + s]);
+          umma_commit(&bars[kBarPEmpty + s]);
         }
-        umma_commit(&bars[kBarAFull + s]);
-        umma_commit(&bars[kBarVEmpty + s]);
-        umma_commit(&bars[kBarPEmpty + s]);
+        jj += nb;
+        ++tt;
       }
     }
   } else {
@@ -272,229 +310,251 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
     const uint32_t rowt = tmem + ((uint32_t)row0 << 16);
     const uint32_t lane4 = (uint32_t)(lane & 15) << 2;
     const uint8_t* tab = reinterpret_cast<const uint8_t*>(s_t2);
-    const int eqr = p.eq[(long long)qrow0 + r];
-    const int32_t* ekg = p.ek + (long long)(b * p.KVH + g) * p.nblk;
-    const int32_t* evg = p.ev + (long long)(b * p.KVH + g) * p.nblk;
-    const int ev0 = SINK ? p.ev0[b * p.KVH + g] : 0;
-    const uint32_t prow = (uint32_t)((r >> 3) * 1024 + (r & 7) * 128);
     const uint32_t obase = rowt + kColO;
     const uint64_t negM2 = f2_pack(-12582912.0f, -12582912.0f);
-    // fold state: both lanes of a row compute it identically
-    float lseg = 0.0f, lrow = 0.0f;
-    int nbrun = 0, nbrow = 0;
-    bool have_seg = false, have_row = false;
-    float* orow = MULTI ? p.orow + ((long long)qrow0 + r) * DH + kh * HALF : nullptr;
+    const uint32_t prow = (uint32_t)((r >> 3) * 1024 + (r & 7) * 128);
+    int jj0 = 0, tt = 0;                                 // global index of the item's block 0; item count
+    bool ok = true;
+    PfItem it;
+    for (int rd = 0; ok && rd < nrounds; ++rd) {
+      if (!pf_item(p, ntile, rd, it)) continue;
+      const int tile = it.tile, b = it.b, h = it.h;
+      const int g = h / p.group;
+      const int nb = tile + 1;                           // causal: blocks 0 .. tile
+      const int qrow0 = (b * p.H + h) * p.Tpad + tile * 128;
+      const int qb = tt & 1;
+      const int8_t* v0 = v0row + qb * 128;               // key 0's value row of this item (sink)
+      const int eqr = p.eq[(long long)qrow0 + r];
+      const int32_t* ekg = p.ek + (long long)(b * p.KVH + g) * p.nblk;
+      const int32_t* evg = p.ev + (long long)(b * p.KVH + g) * p.nblk;
+      const int ev0 = SINK ? p.ev0[b * p.KVH + g] : 0;
+      // fold state: both lanes of a row compute it identically
+      float lseg = 0.0f, lrow = 0.0f;
+      int nbrun = 0, nbrow = 0;
+      bool have_seg = false, have_row = false;
+      float* orow = MULTI ? p.orow + ((long long)qrow0 + r) * DH + kh * HALF : nullptr;
 
-    // fold of block jf: O = fl(O + f32(A) 2^-(s + e_v)), l = fl(l + l_b 2^-s), with the running
-    // maximum rescale first (reference/lssab8_golden.py:293-315); then, at a segment end, the
-    // segment -> row fold (reference/lssab8_golden.py:317-331).
-    auto fold_block = [&](int jf, int nbb, int lbt, int evj, int eh0v) -> bool {
-      const int sa = jf & 1;
-      if (!have_seg) { nbrun = nbb; have_seg = true; }
-      const int D = nbb - nbrun;
-      int sg = 0, Dr = 0;
-      if (D > 0) { Dr = D; lseg = rescale(lseg, D); nbrun = nbb; }
-      else sg = -D;
-      if (!warp_poll(&bars[kBarAFull + sa], (jf >> 1) & 1, abort_flag, p.err)) return false;
-      tc_fence_after();
-      // A block beyond the exact-skip window (sg > S_WIN) is folded with scale +0 instead of being
-      // skipped: O and l are never -0 (they start at +0, an RN sum that cancels exactly is +0, and
-      // the rescale flushes to +0), and A_b, l_b are finite, so O + (+0) x == O bit for bit.
-      const bool add = (sg <= kSWIN);
-      const float scO = add ? pow2f(-(sg + evj)) : 0.0f;
-      const uint64_t scO2 = f2_pack(scO, scO);
-      const bool resc = __any_sync(0xffffffffu, Dr > 0);  // warp-uniform
-      const RowRescale rr = row_rescale(Dr);             // identity on lanes with Dr == 0
-      // DH/2 channels per lane in passes of 32 (two TMEM round trips for DH = 128)
-      constexpr int kPass = HALF < 32 ? HALF : 32;
-#pragma unroll 1
-      for (int c0 = 0; c0 < HALF; c0 += kPass) {
-        const uint32_t abase = rowt + kColA + sa * 128 + c0;
-        const uint32_t ob = obase + c0;
-        uint32_t a[kPass], o[kPass];
-#pragma unroll
-        for (int cc = 0; cc < kPass / 16; ++cc) {
-          tmem_ld16x2<HALF>(abase + cc * 16, a + cc * 16);
-          tmem_ld16x2<HALF>(ob + cc * 16, o + cc * 16);
-        }
-        tc_wait_ld();
-#pragma unroll
-        for (int cc = 0; cc < kPass / 16; ++cc) tmem_fill16x2<HALF>(abase + cc * 16, kMagicBits);   // re-bias
-        if (resc) {
-#pragma unroll
-          for (int c = 0; c < kPass; ++c) o[c] = __float_as_uint(apply_rescale(__uint_as_float(o[c]), rr));
-        }
-        if (SINK && jf == 0 && p.T > 1) {                  // key 0's term first (B9.1); sg == 0 here
-          const float sc0 = pow2f(-ev0);
-          const uint64_t sc02 = f2_pack(sc0, sc0);
-#pragma unroll
+      // fold of block jf: O = fl(O + f32(A) 2^-(s + e_v)), l = fl(l + l_b 2^-s), with the running
+      // maximum rescale first (reference/lssab8_golden.py:293-315); then, at a segment end, the
+      // segment -> row fold (reference/lssab8_golden.py:317-331).
+      auto fold_block = [&](int jf, int nbb, int lbt, int evj, int eh0v) -> bool {
+        const int jgf = jj0 + jf;                          // global block index (pipeline parities)
+        const int sa = jgf & 1;
+        if (!have_seg) { nbrun = nbb; have_seg = true; }
+        const int D = nbb - nbrun;
+        int sg = 0, Dr = 0;
+        if (D > 0) { Dr = D; lseg = rescale(lseg, D); nbrun = nbb; }
+        else sg = -D;
+        if (!warp_poll(&bars[kBarAFull + sa], (jgf >> 1) & 1, abort_flag, p.err)) return false;
+        // key 0's value row arrives with the item's Q tile
+        if (SINK && jf == 0 && p.T > 1 && !warp_poll(&bars[kBarQFull + qb], (tt >> 1) & 1, abort_flag, p.err)) return false;
+        tc_fence_after();
+        // A block beyond the exact-skip window (sg > S_WIN) is folded with scale +0 instead of being
+        // skipped: O and l are never -0 (they start at +0, an RN sum that cancels exactly is +0, and
+        // the rescale flushes to +0), and A_b, l_b are finite, so O + (+0) x == O bit for bit.
+        const bool add = (sg <= kSWIN);
+        const float scO = add ? pow2f(-(sg + evj)) : 0.0f;
+        const uint64_t scO2 = f2_pack(scO, scO);
+        const bool resc = __any_sync(0xffffffffu, Dr > 0);  // warp-uniform
+        const RowRescale rr = row_rescale(Dr);             // identity on lanes with Dr == 0
+        // DH/2 channels per lane in passes of 32 (two TMEM round trips for DH = 128)
+        constexpr int kPass = HALF < 32 ? HALF : 32;
+  #pragma unroll 1
+        for (int c0 = 0; c0 < HALF; c0 += kPass) {
+          const uint32_t abase = rowt + kColA + sa * 128 + c0;
+          const uint32_t ob = obase + c0;
+          uint32_t a[kPass], o[kPass];
+  #pragma unroll
+          for (int cc = 0; cc < kPass / 16; ++cc) {
+            tmem_ld16x2<HALF>(abase + cc * 16, a + cc * 16);
+            tmem_ld16x2<HALF>(ob + cc * 16, o + cc * 16);
+          }
+          tc_wait_ld();
+  #pragma unroll
+          for (int cc = 0; cc < kPass / 16; ++cc) tmem_fill16x2<HALF>(abase + cc * 16, kMagicBits);   // re-bias
+          if (resc) {
+  #pragma unroll
+            for (int c = 0; c < kPass; ++c) o[c] = __float_as_uint(apply_rescale(__uint_as_float(o[c]), rr));
+          }
+          if (SINK && jf == 0 && p.T > 1) {                  // key 0's term first (B9.1); sg == 0 here
+            const float sc0 = pow2f(-ev0);
+            const uint64_t sc02 = f2_pack(sc0, sc0);
+  #pragma unroll
+            for (int t = 0; t < kPass / 2; ++t) {
+              const int c = kh * HALF + c0 + 2 * t;
+              const uint64_t z = f2_pack(i2f_small(eh0v * (int)v0[c]), i2f_small(eh0v * (int)v0[c + 1]));
+              float lo_, hi_;
+              f2_unpack(f2_fma(z, sc02, f2_pack(__uint_as_float(o[2 * t]), __uint_as_float(o[2 * t + 1]))), lo_, hi_);
+              o[2 * t] = __float_as_uint(lo_);
+              o[2 * t + 1] = __float_as_uint(hi_);
+            }
+          }
+  #pragma unroll
           for (int t = 0; t < kPass / 2; ++t) {
-            const int c = kh * HALF + c0 + 2 * t;
-            const uint64_t z = f2_pack(i2f_small(eh0v * (int)v0row[c]), i2f_small(eh0v * (int)v0row[c + 1]));
+            const uint64_t x = f2_add(f2_pack(__uint_as_float(a[2 * t]), __uint_as_float(a[2 * t + 1])), negM2);
             float lo_, hi_;
-            f2_unpack(f2_fma(z, sc02, f2_pack(__uint_as_float(o[2 * t]), __uint_as_float(o[2 * t + 1]))), lo_, hi_);
+            f2_unpack(f2_fma(x, scO2, f2_pack(__uint_as_float(o[2 * t]), __uint_as_float(o[2 * t + 1]))), lo_, hi_);
             o[2 * t] = __float_as_uint(lo_);
             o[2 * t + 1] = __float_as_uint(hi_);
           }
-        }
-#pragma unroll
-        for (int t = 0; t < kPass / 2; ++t) {
-          const uint64_t x = f2_add(f2_pack(__uint_as_float(a[2 * t]), __uint_as_float(a[2 * t + 1])), negM2);
-          float lo_, hi_;
-          f2_unpack(f2_fma(x, scO2, f2_pack(__uint_as_float(o[2 * t]), __uint_as_float(o[2 * t + 1]))), lo_, hi_);
-          o[2 * t] = __float_as_uint(lo_);
-          o[2 * t + 1] = __float_as_uint(hi_);
-        }
-#pragma unroll
-        for (int cc = 0; cc < kPass / 16; ++cc) tmem_st16x2<HALF>(ob + cc * 16, o + cc * 16);
-      }
-      tc_wait_st();
-      tc_fence_before();
-      mbar_arrive(&bars[kBarAEmpty + sa]);
-      lseg = fold_term(lseg, lbt, add ? pow2f(-sg) : 0.0f);
-      if (MULTI && (((jf + 1) % kSEG == 0) || (jf == nb - 1))) {
-        // segment -> row: the same three rules (reference/lssab8_golden.py:317-331)
-        int D2 = 0, s2 = 0;
-        const bool first = !have_row;
-        if (first) { nbrow = nbrun; have_row = true; }
-        else { D2 = nbrun - nbrow; if (D2 > 0) { lrow = rescale(lrow, D2); nbrow = nbrun; } else { s2 = -D2; } }
-#pragma unroll 1
-        for (int cc = 0; cc < HALF / 16; ++cc) {
-          uint32_t y[16];
-          tmem_ld16x2<HALF>(obase + cc * 16, y);
-          tc_wait_ld();
-#pragma unroll
-          for (int c = 0; c < 16; ++c) {
-            float* pr = orow + cc * 16 + c;
-            const float seg = __uint_as_float(y[c]);
-            if (first) *pr = rescale(seg, 0);
-            else {
-              float x = *pr;
-              if (D2 > 0) x = rescale(x, D2);
-              if (s2 <= kSWIN) x = __fadd_rn(x, rescale(seg, s2));
-              *pr = x;
-            }
-          }
-          tmem_fill16x2<HALF>(obase + cc * 16, 0u);
+  #pragma unroll
+          for (int cc = 0; cc < kPass / 16; ++cc) tmem_st16x2<HALF>(ob + cc * 16, o + cc * 16);
         }
         tc_wait_st();
-        if (first) lrow = rescale(lseg, 0);
-        else if (s2 <= kSWIN) lrow = __fadd_rn(lrow, rescale(lseg, s2));
-        lseg = 0.0f;
-        have_seg = false;
-      }
-      return true;
-    };
+        tc_fence_before();
+        mbar_arrive(&bars[kBarAEmpty + sa]);
+        lseg = fold_term(lseg, lbt, add ? pow2f(-sg) : 0.0f);
+        if (MULTI && (((jf + 1) % kSEG == 0) || (jf == nb - 1))) {
+          // segment -> row: the same three rules (reference/lssab8_golden.py:317-331)
+          int D2 = 0, s2 = 0;
+          const bool first = !have_row;
+          if (first) { nbrow = nbrun; have_row = true; }
+          else { D2 = nbrun - nbrow; if (D2 > 0) { lrow = rescale(lrow, D2); nbrow = nbrun; } else { s2 = -D2; } }
+  #pragma unroll 1
+          for (int cc = 0; cc < HALF / 16; ++cc) {
+            uint32_t y[16];
+            tmem_ld16x2<HALF>(obase + cc * 16, y);
+            tc_wait_ld();
+  #pragma unroll
+            for (int c = 0; c < 16; ++c) {
+              float* pr = orow + cc * 16 + c;
+              const float seg = __uint_as_float(y[c]);
+              if (first) *pr = rescale(seg, 0);
+              else {
+                float x = *pr;
+                if (D2 > 0) x = rescale(x, D2);
+                if (s2 <= kSWIN) x = __fadd_rn(x, rescale(seg, s2));
+                *pr = x;
+              }
+            }
+            tmem_fill16x2<HALF>(obase + cc * 16, 0u);
+          }
+          tc_wait_st();
+          if (first) lrow = rescale(lseg, 0);
+          else if (s2 <= kSWIN) lrow = __fadd_rn(lrow, rescale(lseg, s2));
+          lseg = 0.0f;
+          have_seg = false;
+        }
+        return true;
+      };
 
-    bool ok = true;
-    int nb_prev = 0, ev_prev = 0, lbt_prev = 0, eh0_row = 0;
-    int ek_next = ekg[0], ev_next = evg[0];            // e_k, e_v one block ahead
-    for (int j = 0; j < nb; ++j) {
-      const int ekj = ek_next, evj = ev_next;
-      if (j + 1 < nb) { ek_next = ekg[j + 1]; ev_next = evg[j + 1]; }
-      const int s = j & 1;
-      const uint32_t ph = (j >> 1) & 1;
-      if (!warp_poll(&bars[kBarSFull], j & 1, abort_flag, p.err)) { ok = false; break; }
-      tc_fence_after();
-      const bool diag = (j == tile);                     // key c of the diagonal block visible iff c <= r
-      // pass 1: this lane's 64 scores into registers (one TMEM round trip; S is free for the
-      // next QK as soon as they have landed) and the exact max over its visible keys
-      uint32_t v[64];
-      const uint32_t sbase = rowt + kColS;
-      tmem_ld16x2<64>(sbase, v);
-      tmem_ld16x2<64>(sbase + 16, v + 16);
-      tmem_ld16x2<64>(sbase + 32, v + 32);
-      tmem_ld16x2<64>(sbase + 48, v + 48);
-      tc_wait_ld();
+      int nb_prev = 0, ev_prev = 0, lbt_prev = 0, eh0_row = 0;
+      int ek_next = ekg[0], ev_next = evg[0];            // e_k, e_v one block ahead
+      for (int j = 0; j < nb; ++j) {
+        const int ekj = ek_next, evj = ev_next;
+        if (j + 1 < nb) { ek_next = ekg[j + 1]; ev_next = evg[j + 1]; }
+        const int jg = jj0 + j;
+        const int s = jg & 1;
+        const uint32_t ph = (jg >> 1) & 1;
+        if (!warp_poll(&bars[kBarSFull], jg & 1, abort_flag, p.err)) { ok = false; break; }
+        tc_fence_after();
+        const bool diag = (j == tile);                     // key c of the diagonal block visible iff c <= r
+        // pass 1: this lane's 64 scores into registers (one TMEM round trip; S is free for the
+        // next QK as soon as they have landed) and the exact max over its visible keys
+        uint32_t v[64];
+        const uint32_t sbase = rowt + kColS;
+        tmem_ld16x2<64>(sbase, v);
+        tmem_ld16x2<64>(sbase + 16, v + 16);
+        tmem_ld16x2<64>(sbase + 32, v + 32);
+        tmem_ld16x2<64>(sbase + 48, v + 48);
+        tc_wait_ld();
+        tc_fence_before();
+        mbar_arrive(&bars[kBarSEmpty]);
+        if (diag) {
+  #pragma unroll
+          for (int c = 0; c < 64; ++c) if (kh * 64 + c > r) v[c] = 0x80000000u;
+        }
+        int m = __vimax3_s32((int)v[0], (int)v[1], (int)v[2]);
+  #pragma unroll
+        for (int c = 3; c < 63; c += 2) m = __vimax3_s32(m, (int)v[c], (int)v[c + 1]);
+        m = max(m, (int)v[63]);
+        m = max(m, __shfl_xor_sync(0xffffffffu, m, 16));  // the row's max over both key halves
+        const uint32_t G = g_fold(p.gbase, eqr + ekj);
+        const int nbv = nb_of(m, G);
+        const uint32_t NBlo = (uint32_t)nbv << kBHI;
+        const int lg = 31 - __clz((int)G);
+        const int dm = 1 << max(0, 30 - lg);              // dm * G in [2^30, 2^31): >= 9 doublings
+        const int lo = m - dm;
+        const uint32_t negG = 0u - G;
+        if (!warp_poll(&bars[kBarPEmpty + s], ph ^ 1, abort_flag, p.err)) { ok = false; break; }
+        const uint32_t pbase = smem_u32(smem + L::kP + s * 16384) + prow;
+        uint32_t lb = 0, eh0 = 0;
+        // pass 2: the chain and the u8 P half-row, 16 keys (one 16-byte P chunk) at a time
+  #pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+          uint32_t w[4];
+  #pragma unroll
+          for (int qq = 0; qq < 4; ++qq) {
+            uint32_t e[4];
+  #pragma unroll
+            for (int x = 0; x < 4; ++x) {
+              const int sc = max((int)v[cc * 16 + qq * 4 + x], lo);
+              uint32_t d = NBlo + (uint32_t)sc * negG;       // exact: d < 2^32
+              const uint32_t ix = min(d, kDClamp) >> kIdxShift;  // index <= 1152 (T2 = 0 from 1152 on)
+              e[x] = tab[ix * p.mul_entry + lane4];            // entry ix, this lane's copy
+            }
+            w[qq] = e[0] + e[1] * p.mul_b1 + e[2] * p.mul_b2 + e[3] * p.mul_b3;
+            lb = __dp4a(w[qq], 0x01010101u, lb);
+          }
+          const int chunk = kh * 4 + cc;
+          if (SINK && chunk == 0 && j == 0 && p.T > 1) { eh0 = w[0] & 0xFFu; w[0] &= ~0xFFu; }
+          st_shared_v4(pbase + (uint32_t)((chunk ^ (r & 7)) << 4), w[0], w[1], w[2], w[3]);
+        }
+        fence_async_smem();
+        mbar_arrive(&bars[kBarPFull + s]);
+        const int lbt = (int)lb + __shfl_xor_sync(0xffffffffu, (int)lb, 16);   // the row's l_b
+        if (SINK && j == 0) eh0_row = __shfl_sync(0xffffffffu, (int)eh0, lane & 15);
+        if (j > 0 && !fold_block(j - 1, nb_prev, lbt_prev, ev_prev, eh0_row)) { ok = false; break; }
+        nb_prev = nbv;
+        lbt_prev = lbt;
+        ev_prev = evj;
+      }
+      if (ok) ok = fold_block(nb - 1, nb_prev, lbt_prev, ev_prev, eh0_row);
+
+      // ---- epilogue: out = O_row / l_row (one RN division per element; l_row == 0 -> 0).
+      // `ok` is warp-uniform (every wait is decided for the whole warp), so the warp-collective
+      // TMEM loads run on every lane or on none; rows past T skip only the store.
+      if (ok) {
+        if constexpr (!MULTI) lrow = rescale(lseg, 0);   // a single segment: O_row = 0 + rescale(O_seg, 0)
+        const int i = tile * 128 + r;
+        const bool live = (i < p.T);
+        const bool nz = (lrow != 0.0f);
+        const float rl = nz ? __frcp_rn(lrow) : 0.0f;
+        const bool row_fast = nz && div_window(lrow);
+        OutT* dst = reinterpret_cast<OutT*>(p.out) + b * p.os0 + (long long)i * p.os1 + h * p.os2 + kh * HALF * p.os3;
+  #pragma unroll 1
+        for (int cc = 0; cc < HALF / 16; ++cc) {
+          float q[16];
+          if constexpr (!MULTI) {
+            uint32_t y[16];
+            tmem_ld16x2<HALF>(obase + cc * 16, y);
+            tc_wait_ld();
+            tmem_fill16x2<HALF>(obase + cc * 16, 0u);        // O starts at +0 for the next item
+  #pragma unroll
+            for (int c = 0; c < 16; ++c) q[c] = __uint_as_float(y[c]);
+          } else {
+  #pragma unroll
+            for (int c = 0; c < 16; ++c) q[c] = live ? orow[cc * 16 + c] : 0.0f;
+          }
+          if (live) {
+  #pragma unroll
+            for (int c = 0; c < 16; ++c) {
+              // fast path: both operands inside the Markstein window (then O_seg is normal and
+              // rescale(O_seg, 0) is O_seg itself); anything else takes the IEEE division
+              if (row_fast && div_window(q[c])) q[c] = div_markstein(q[c], lrow, rl);
+              else q[c] = nz ? div_rn_ieee(MULTI ? q[c] : rescale(q[c], 0), lrow) : 0.0f;
+            }
+            store_chunk<OutT, 16>(dst + cc * 16 * p.os3, p.os3, q);
+          }
+        }
+        tc_wait_st();
+      }
+      // this item is done with O, its sink row and (through the MMA's commit) its Q tile
       tc_fence_before();
-      mbar_arrive(&bars[kBarSEmpty]);
-      if (diag) {
-#pragma unroll
-        for (int c = 0; c < 64; ++c) if (kh * 64 + c > r) v[c] = 0x80000000u;
-      }
-      int m = __vimax3_s32((int)v[0], (int)v[1], (int)v[2]);
-#pragma unroll
-      for (int c = 3; c < 63; c += 2) m = __vimax3_s32(m, (int)v[c], (int)v[c + 1]);
-      m = max(m, (int)v[63]);
-      m = max(m, __shfl_xor_sync(0xffffffffu, m, 16));  // the row's max over both key halves
-      const uint32_t G = g_fold(p.gbase, eqr + ekj);
-      const int nbv = nb_of(m, G);
-      const uint32_t NBlo = (uint32_t)nbv << kBHI;
-      const int lg = 31 - __clz((int)G);
-      const int dm = 1 << max(0, 30 - lg);              // dm * G in [2^30, 2^31): >= 9 doublings
-      const int lo = m - dm;
-      const uint32_t negG = 0u - G;
-      if (!warp_poll(&bars[kBarPEmpty + s], ph ^ 1, abort_flag, p.err)) { ok = false; break; }
-      const uint32_t pbase = smem_u32(smem + L::kP + s * 16384) + prow;
-      uint32_t lb = 0, eh0 = 0;
-      // pass 2: the chain and the u8 P half-row, 16 keys (one 16-byte P chunk) at a time
-#pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {
-        uint32_t w[4];
-#pragma unroll
-        for (int qq = 0; qq < 4; ++qq) {
-          uint32_t e[4];
-#pragma unroll
-          for (int x = 0; x < 4; ++x) {
-            const int sc = max((int)v[cc * 16 + qq * 4 + x], lo);
-            uint32_t d = NBlo + (uint32_t)sc * negG;       // exact: d < 2^32
-            const uint32_t ix = min(d, kDClamp) >> kIdxShift;  // index <= 1152 (T2 = 0 from 1152 on)
-            e[x] = tab[ix * p.mul_entry + lane4];            // entry ix, this lane's copy
-          }
-          w[qq] = e[0] + e[1] * p.mul_b1 + e[2] * p.mul_b2 + e[3] * p.mul_b3;
-          lb = __dp4a(w[qq], 0x01010101u, lb);
-        }
-        const int chunk = kh * 4 + cc;
-        if (SINK && chunk == 0 && j == 0 && p.T > 1) { eh0 = w[0] & 0xFFu; w[0] &= ~0xFFu; }
-        st_shared_v4(pbase + (uint32_t)((chunk ^ (r & 7)) << 4), w[0], w[1], w[2], w[3]);
-      }
-      fence_async_smem();
-      mbar_arrive(&bars[kBarPFull + s]);
-      const int lbt = (int)lb + __shfl_xor_sync(0xffffffffu, (int)lb, 16);   // the row's l_b
-      if (SINK && j == 0) eh0_row = __shfl_sync(0xffffffffu, (int)eh0, lane & 15);
-      if (j > 0 && !fold_block(j - 1, nb_prev, lbt_prev, ev_prev, eh0_row)) { ok = false; break; }
-      nb_prev = nbv;
-      lbt_prev = lbt;
-      ev_prev = evj;
-    }
-    if (ok) ok = fold_block(nb - 1, nb_prev, lbt_prev, ev_prev, eh0_row);
-
-    // ---- epilogue: out = O_row / l_row (one RN division per element; l_row == 0 -> 0).
-    // `ok` is warp-uniform (every wait is decided for the whole warp), so the warp-collective
-    // TMEM loads run on every lane or on none; rows past T skip only the store.
-    if (ok) {
-      if constexpr (!MULTI) lrow = rescale(lseg, 0);   // a single segment: O_row = 0 + rescale(O_seg, 0)
-      const int i = tile * 128 + r;
-      const bool live = (i < p.T);
-      const bool nz = (lrow != 0.0f);
-      const float rl = nz ? __frcp_rn(lrow) : 0.0f;
-      const bool row_fast = nz && div_window(lrow);
-      OutT* dst = reinterpret_cast<OutT*>(p.out) + b * p.os0 + (long long)i * p.os1 + h * p.os2 + kh * HALF * p.os3;
-#pragma unroll 1
-      for (int cc = 0; cc < HALF / 16; ++cc) {
-        float q[16];
-        if constexpr (!MULTI) {
-          uint32_t y[16];
-          tmem_ld16x2<HALF>(obase + cc * 16, y);
-          tc_wait_ld();
-#pragma unroll
-          for (int c = 0; c < 16; ++c) q[c] = __uint_as_float(y[c]);
-        } else {
-#pragma unroll
-          for (int c = 0; c < 16; ++c) q[c] = live ? orow[cc * 16 + c] : 0.0f;
-        }
-        if (live) {
-#pragma unroll
-          for (int c = 0; c < 16; ++c) {
-            // fast path: both operands inside the Markstein window (then O_seg is normal and
-            // rescale(O_seg, 0) is O_seg itself); anything else takes the IEEE division
-            if (row_fast && div_window(q[c])) q[c] = div_markstein(q[c], lrow, rl);
-            else q[c] = nz ? div_rn_ieee(MULTI ? q[c] : rescale(q[c], 0), lrow) : 0.0f;
-          }
-          store_chunk<OutT, 16>(dst + cc * 16 * p.os3, p.os3, q);
-        }
-      }
-    }
+      mbar_arrive(&bars[kBarQEmpty + qb]);
+      jj0 += nb;
+      ++tt;
+    }                                                  // items
   }
 
   // ---- teardown
