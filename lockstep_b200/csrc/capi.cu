@@ -397,7 +397,8 @@ int lssab8_quant_rows(const void* x, int dtype, int B, int H, int T, int dh, con
     if (vec_ok<InT>(x, s, dh)) {
       constexpr int N = Vec16<InT>::kN;
       const int rpw = 32 / (dh / N);
-      const int grid = (int)((rows + 8LL * rpw - 1) / (8LL * rpw));
+      const long long per_cta = 8LL * rpw * kRowsPerLane;
+      const int grid = (int)((rows + per_cta - 1) / per_cta);
       if (dh == 128) quant_rows_vec_kernel<InT, 128><<<grid, 256, 0, st>>>(static_cast<const InT*>(x), s, B, H, T, Tpad, q8, eq);
       else quant_rows_vec_kernel<InT, 64><<<grid, 256, 0, st>>>(static_cast<const InT*>(x), s, B, H, T, Tpad, q8, eq);
       return launch_rc();
@@ -492,10 +493,28 @@ int lssab8_prefill(const void* q, const void* k, const void* v, int dtype, int B
   int32_t* ev = reinterpret_cast<int32_t*>(base + w.ev);
   int32_t* ev0 = reinterpret_cast<int32_t*>(base + w.ev0);
   int rc;
-  if ((rc = lssab8_quant_rows(q, dtype, B, H, T, dh, qs, Tpad, q8, eq, stream))) return rc;
-  if ((rc = lssab8_quant_blocks(k, dtype, B, KVH, T, dh, ks, Tpad, 0, k8, ek, nullptr, stream))) return rc;
   const int vmode = sink ? (T > 1 ? 2 : 1) : 0;
-  if ((rc = lssab8_quant_blocks(v, dtype, B, KVH, T, dh, vs, Tpad, vmode, v8, ev, ev0, stream))) return rc;
+  if (!strides_ok(qs, 4) || !strides_ok(ks, 4) || !strides_ok(vs, 4)) return kErrArg;
+  DevState* ds = nullptr;
+  if ((rc = dev_state(&ds))) return rc;
+  const Strides4 sk{ks[0], ks[1], ks[2], ks[3]}, sv{vs[0], vs[1], vs[2], vs[3]};
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if ((rc = lssab8_quant_rows(q, dtype, B, H, T, dh, qs, Tpad, q8, eq, stream))) return rc;
+  // K and V in one launch when both take the vectorised path
+  rc = with_in_dtype(dtype, [&](auto tag) -> int {
+    using InT = std::remove_const_t<std::remove_pointer_t<decltype(tag)>>;
+    if (!vec_ok<InT>(k, sk, dh) || !vec_ok<InT>(v, sv, dh)) return -1;
+    const int grid = 2 * (Tpad / 128) * KVH * B;
+    auto kfn = (dh == 128) ? quant_kv_vec_kernel<InT, 128> : quant_kv_vec_kernel<InT, 64>;
+    kfn<<<grid, 256, 0, st>>>(static_cast<const InT*>(k), sk, static_cast<const InT*>(v), sv, B, KVH, T, Tpad, vmode,
+                              k8, ek, v8, ev, ev0, ds->err);
+    return launch_rc();
+  });
+  if (rc > 0) return rc;
+  if (rc < 0) {                                      // strided or unaligned inputs: the generic quantisers
+    if ((rc = lssab8_quant_blocks(k, dtype, B, KVH, T, dh, ks, Tpad, 0, k8, ek, nullptr, stream))) return rc;
+    if ((rc = lssab8_quant_blocks(v, dtype, B, KVH, T, dh, vs, Tpad, vmode, v8, ev, ev0, stream))) return rc;
+  }
   float* orow = (Tpad / 128 > kSEG) ? reinterpret_cast<float*>(base + w.orow) : nullptr;
   return lssab8_prefill_lattice(q8, eq, k8, ek, v8, ev, (sink && T > 1) ? ev0 : nullptr, B, H, KVH, T, dh, Tpad,
                                 orow, out, out_dtype, os, stream);

@@ -146,59 +146,90 @@ template <> struct PackOut<4> {
   }
 };
 
-// P1 fast path: G = DH*sizeof/16 lanes per row, 32/G rows per warp.
+// P1 fast path: G = DH*sizeof/16 lanes per row, 32/G rows per warp, kRowsPerLane row groups per
+// CTA pass (all their 16-byte loads are issued before any is used); `cta` = the 256-thread CTA's
+// index in the row space.
+constexpr int kRowsPerLane = 4;
+template <typename InT, int DH>
+__device__ __forceinline__ void quant_rows_vec(int cta, const InT* __restrict__ x, Strides4 xs, int B, int H, int T,
+                                               int Tpad, int8_t* __restrict__ q8, int32_t* __restrict__ eq) {
+  constexpr int N = Vec16<InT>::kN;
+  constexpr int G = DH / N;                            // lanes per row
+  constexpr int RPW = 32 / G;                          // rows per warp
+  constexpr int RPC = 8 * RPW;                         // rows per CTA and row group
+  const int lane = threadIdx.x & 31;
+  const int sub = lane % G;
+  const long long nrows = (long long)B * H * Tpad;
+  const long long row0 = (long long)cta * RPC * kRowsPerLane + (threadIdx.x >> 5) * RPW + lane / G;
+  uint4 u[kRowsPerLane];
+  bool data[kRowsPerLane];
+  if (Tpad % (RPC * kRowsPerLane) == 0) {
+    // the CTA's rows lie in one window of one (b, h): one index computation per thread
+    const long long rr0 = row0 < nrows ? row0 : 0;
+    const int t0 = (int)(rr0 % Tpad);
+    const long long bh = rr0 / Tpad;
+    const int h = (int)(bh % H), b = (int)(bh / H);
+    const InT* xrow = x + b * xs.s0 + h * xs.s1 + sub * N;
+#pragma unroll
+    for (int k = 0; k < kRowsPerLane; ++k) {
+      const long long row = row0 + (long long)k * RPC;
+      const int t = t0 + k * RPC;
+      data[k] = row < nrows && t < T;
+      u[k] = data[k] ? *reinterpret_cast<const uint4*>(xrow + (long long)t * xs.s2) : make_uint4(0u, 0u, 0u, 0u);
+    }
+  } else {                                             // e.g. one row per (b, h) (decode queries)
+#pragma unroll
+    for (int k = 0; k < kRowsPerLane; ++k) {
+      const long long row = row0 + (long long)k * RPC;
+      const long long rr = row < nrows ? row : 0;
+      const int t = (int)(rr % Tpad);
+      const long long bh = rr / Tpad;
+      const int h = (int)(bh % H), b = (int)(bh / H);
+      data[k] = row < nrows && t < T;
+      u[k] = data[k] ? *reinterpret_cast<const uint4*>(x + b * xs.s0 + h * xs.s1 + (long long)t * xs.s2 + sub * N)
+                     : make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < kRowsPerLane; ++k) {
+    const long long row = row0 + (long long)k * RPC;
+    float f[N];
+    unpack16<InT>(u[k], f);
+    float m = 0.0f;
+#pragma unroll
+    for (int i = 0; i < N; ++i) m = fmaxf(m, fabsf(f[i]));
+#pragma unroll
+    for (int o = G / 2; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (row < nrows) {
+      const int e = data[k] ? pow2_exponent(m, 40) : 0;
+      const float sc = pow2f(e);
+      int q[N];
+#pragma unroll
+      for (int i = 0; i < N; ++i) q[i] = quant8(f[i], sc);     // rows past T: zeros
+      *reinterpret_cast<typename PackOut<N>::T*>(q8 + row * DH + sub * N) = PackOut<N>::pack(q);
+      if (sub == 0) eq[row] = e;
+    }
+  }
+}
+
 template <typename InT, int DH>
 __global__ void __launch_bounds__(256)
 quant_rows_vec_kernel(const InT* __restrict__ x, Strides4 xs, int B, int H, int T, int Tpad,
                       int8_t* __restrict__ q8, int32_t* __restrict__ eq) {
   pdl_launch_dependents();                             // a PDL-launched consumer may start its setup
-  constexpr int N = Vec16<InT>::kN;
-  constexpr int G = DH / N;                            // lanes per row
-  constexpr int RPW = 32 / G;                          // rows per warp
-  const int lane = threadIdx.x & 31;
-  const long long row = ((long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * RPW + lane / G;
-  const int sub = lane % G;
-  const long long nrows = (long long)B * H * Tpad;
-  const bool live = row < nrows;
-  const long long rr = live ? row : 0;
-  const int t = (int)(rr % Tpad);
-  const long long bh = rr / Tpad;
-  const int h = (int)(bh % H), b = (int)(bh / H);
-  const bool data = live && t < T;
-  float f[N];
-  float m = 0.0f;
-  if (data) {
-    const uint4 u = *reinterpret_cast<const uint4*>(x + b * xs.s0 + h * xs.s1 + (long long)t * xs.s2 + sub * N);
-    unpack16<InT>(u, f);
-#pragma unroll
-    for (int i = 0; i < N; ++i) m = fmaxf(m, fabsf(f[i]));
-  } else {
-#pragma unroll
-    for (int i = 0; i < N; ++i) f[i] = 0.0f;
-  }
-#pragma unroll
-  for (int o = G / 2; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-  if (!live) return;
-  const int e = data ? pow2_exponent(m, 40) : 0;
-  const float sc = pow2f(e);
-  int q[N];
-#pragma unroll
-  for (int i = 0; i < N; ++i) q[i] = quant8(f[i], sc);
-  *reinterpret_cast<typename PackOut<N>::T*>(q8 + rr * DH + sub * N) = PackOut<N>::pack(q);
-  if (sub == 0) eq[rr] = e;
+  quant_rows_vec<InT, DH>((int)blockIdx.x, x, xs, B, H, T, Tpad, q8, eq);
 }
 
 // P2/P3 fast path: one CTA of 256 threads per (block, kv head, batch); the block's 128 x DH
 // values stay in registers (<= 8 vectors per thread) between the amax and the quantisation.
 template <typename InT, int DH>
-__global__ void __launch_bounds__(256)
-quant_blocks_vec_kernel(const InT* __restrict__ x, Strides4 xs, int B, int KVH, int T, int Tpad, int mode,
-                        int8_t* __restrict__ x8, int32_t* __restrict__ eblk, int32_t* __restrict__ e0,
-                        int* __restrict__ err) {
+__device__ __forceinline__ void quant_blocks_vec(int blk, int g, int b, const InT* __restrict__ x, Strides4 xs,
+                                                 int B, int KVH, int T, int Tpad, int mode, int8_t* __restrict__ x8,
+                                                 int32_t* __restrict__ eblk, int32_t* __restrict__ e0,
+                                                 int* __restrict__ err) {
   constexpr int N = Vec16<InT>::kN;
   constexpr int VPR = DH / N;                          // vectors per row
   constexpr int VPT = 128 * VPR / 256;                 // vectors per thread
-  const int blk = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
   const int nblk = (T + kKB - 1) / kKB;
   const int lo = blk * kKB;
   const int hi = min(T, lo + kKB);
@@ -206,22 +237,24 @@ quant_blocks_vec_kernel(const InT* __restrict__ x, Strides4 xs, int B, int KVH, 
   const InT* src = x + b * xs.s0 + g * xs.s1;
   int8_t* dst = x8 + ((long long)(b * KVH + g) * Tpad) * DH;
   __shared__ float red[2][8];
-  float f[VPT][N];
+  uint4 raw[VPT];                                      // raw 16-byte vectors: half the registers of floats
   float m = 0.0f, m0 = 0.0f;
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
     const int v = threadIdx.x + i * 256;
     const int r = lo + v / VPR, c = (v % VPR) * N;
-    if (r < hi) {
-      unpack16<InT>(*reinterpret_cast<const uint4*>(src + (long long)r * xs.s2 + c), f[i]);
-      float a = 0.0f;
+    raw[i] = (r < hi) ? *reinterpret_cast<const uint4*>(src + (long long)r * xs.s2 + c) : make_uint4(0u, 0u, 0u, 0u);
+  }
 #pragma unroll
-      for (int k = 0; k < N; ++k) a = fmaxf(a, fabsf(f[i][k]));
-      if (split0 && r == 0) m0 = fmaxf(m0, a); else m = fmaxf(m, a);
-    } else {
+  for (int i = 0; i < VPT; ++i) {
+    const int v = threadIdx.x + i * 256;
+    const int r = lo + v / VPR;
+    float f[N];
+    unpack16<InT>(raw[i], f);
+    float a = 0.0f;
 #pragma unroll
-      for (int k = 0; k < N; ++k) f[i][k] = 0.0f;
-    }
+    for (int k = 0; k < N; ++k) a = fmaxf(a, fabsf(f[k]));
+    if (split0 && r == 0) m0 = fmaxf(m0, a); else m = fmaxf(m, a);
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
@@ -242,9 +275,11 @@ quant_blocks_vec_kernel(const InT* __restrict__ x, Strides4 xs, int B, int KVH, 
     const int v = threadIdx.x + i * 256;
     const int r = lo + v / VPR, c = (v % VPR) * N;
     if (r < lo + kKB && r < Tpad) {                    // rows past T (padding) become zeros
+      float f[N];
+      unpack16<InT>(raw[i], f);
       int q[N];
 #pragma unroll
-      for (int k = 0; k < N; ++k) q[k] = (r < hi) ? quant8(f[i][k], (split0 && r == 0) ? sc0 : sc) : 0;
+      for (int k = 0; k < N; ++k) q[k] = (r < hi) ? quant8(f[k], (split0 && r == 0) ? sc0 : sc) : 0;
       *reinterpret_cast<typename PackOut<N>::T*>(dst + (long long)r * DH + c) = PackOut<N>::pack(q);
     }
   }
@@ -258,6 +293,35 @@ quant_blocks_vec_kernel(const InT* __restrict__ x, Strides4 xs, int B, int KVH, 
     if (mode == 2 && blk == 0) e0[b * KVH + g] = ez;
     if (mode != 0 && (e < -32 || e > 40)) atomicOr(err, kDevEvRange);
   }
+}
+
+template <typename InT, int DH>
+__global__ void __launch_bounds__(256)
+quant_blocks_vec_kernel(const InT* __restrict__ x, Strides4 xs, int B, int KVH, int T, int Tpad, int mode,
+                        int8_t* __restrict__ x8, int32_t* __restrict__ eblk, int32_t* __restrict__ e0,
+                        int* __restrict__ err) {
+  quant_blocks_vec<InT, DH>((int)blockIdx.x, (int)blockIdx.y, (int)blockIdx.z, x, xs, B, KVH, T, Tpad, mode, x8,
+                            eblk, e0, err);
+}
+
+// The prefill's K and V quantisers in one launch (P2 for K, P2 or P3 for V): CTAs [0, nk)
+// quantise K's (block, kv head, batch) tiles, CTAs [nk, 2 nk) V's.  (Q's row quantiser stays a
+// separate kernel: fused, it would run at this kernel's register count and lose occupancy.)
+template <typename InT, int DH>
+__global__ void __launch_bounds__(256)
+quant_kv_vec_kernel(const InT* __restrict__ k, Strides4 ks, const InT* __restrict__ v, Strides4 vs, int B, int KVH,
+                    int T, int Tpad, int vmode, int8_t* __restrict__ k8, int32_t* __restrict__ ek,
+                    int8_t* __restrict__ v8, int32_t* __restrict__ ev, int32_t* __restrict__ ev0,
+                    int* __restrict__ err) {
+  const int nblk = Tpad / kKB;
+  const int nk = nblk * KVH * B;
+  const int i = (int)blockIdx.x;
+  const bool isv = i >= nk;
+  const int j = isv ? i - nk : i;
+  const int blk = j % nblk, g = (j / nblk) % KVH, b = j / (nblk * KVH);
+  if (!isv) quant_blocks_vec<InT, DH>(blk, g, b, k, ks, B, KVH, T, Tpad, 0, k8, ek, ev0, err);
+  else quant_blocks_vec<InT, DH>(blk, g, b, v, vs, B, KVH, T, Tpad, vmode, v8, ev, ev0, err);
+  pdl_launch_dependents();                             // released as the CTAs finish
 }
 
 }  // namespace lssab8
