@@ -4,7 +4,8 @@
 Workload (BASELINE.json configs[1] = config 2): Llama-3.1-8B-shaped causal GQA prefill, B=4,
 32 query / 8 kv heads, dh 128, T 2048, bf16 inputs N(0,1) from seed (1% of K channels x8),
 sink off.  One step = one full drop-in prefill (PREP quantisers + the tcgen05 prefill kernel)
-over inputs resident in HBM.  L2 is flushed (a 512 MB write) before every timed step, outside
+over inputs resident in HBM (three launches: the Q row quantiser, the K/V block quantiser and the
+persistent tcgen05 prefill kernel).  L2 is flushed (a 512 MB write) before every timed step, outside
 the timed events.  Also measured: config 3 split-KV decode (KV lattice GB/s), the end-to-end
 public-API call with pinned host buffers, the dominant kernel's roofline, clocks, and the CPU
 oracle port on the host cores.
@@ -32,8 +33,8 @@ sys.path.insert(0, ROOT)
 METRIC = "LSSA-B8 attn: prefill % int8 MMA peak; decode KV GB/s; 0 bit diffs vs ref"
 # DRAM bytes (read + write) of one launch, from one `ncu --set full` capture of the same workload
 # (profiles/prefill_kernel_cfg2.md, profiles/decode_kernel_cfg3.md)
-PREFILL_TRAFFIC_BYTES = 68_740_000
-DECODE_TRAFFIC_BYTES = 569_280_000
+PREFILL_TRAFFIC_BYTES = 68_198_000
+DECODE_TRAFFIC_BYTES = 602_742_000
 CFG = dict(B=4, H=32, KVH=8, dh=128, T=2048, outliers=0.01)
 DEC = dict(B=32, H=32, KVH=8, dh=128, L=8192, nsplit=16)
 
@@ -282,7 +283,7 @@ def run_gpu(args):
         gather = {"ms_per_step": round(float(tt.item()), 4), "bytes_per_rank": out.numel() * 2}
         del bufs
 
-    launches_per_step = 4                          # quant_rows, quant_blocks x2, prefill_kernel
+    launches_per_step = 3                          # quant_rows_vec, quant_kv_vec, prefill_kernel
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": "TOPS", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(t_ms, 4), "higher_is_better": True, "scaling": "weak",
