@@ -156,6 +156,12 @@ int lssab8_decode_noalloc(const void* q, int dtype, const int64_t* qs, int B, in
  * fl(O / l) names (reference/lssab8_golden.py:333).  Device pointers, n elements. */
 int lssab8_selftest_div(const float* y, const float* l, long long n, float* out, void* stream);
 
+/* Test support, no counterpart in the reference: the prefill fold's running-maximum rescale of
+ * the pair x[2i], x[2i + 1] by D[i] (the contract's exponent-field subtraction with flush to +0,
+ * reference/lssab8_golden.py:293-301; D <= 0 is the identity), followed by the fold's add of a
+ * zero term.  Device pointers: x and out hold 2 * npairs floats, D npairs ints. */
+int lssab8_selftest_rescale(const float* x, const int32_t* D, long long npairs, float* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

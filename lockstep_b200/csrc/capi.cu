@@ -338,6 +338,21 @@ __global__ void selftest_div_kernel(const float* y, const float* l, long long n,
   }
 }
 
+// the prefill fold's rescale (rescale_channels) of the pair x[2i], x[2i + 1] by D[i], then the
+// fold's fused multiply-add of a zero term with a positive scale, one pair per thread
+__global__ void selftest_rescale_kernel(const float* x, const int* D, long long npairs, float* out) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < npairs; i += (long long)gridDim.x * blockDim.x) {
+    const int d = D[i];
+    const float sc = pow2f(-min(max(d, 0), 126));
+    uint32_t o[2] = {__float_as_uint(x[2 * i]), __float_as_uint(x[2 * i + 1])};
+    rescale_channels<2>(o, d, f2_pack(sc, sc));
+    float lo, hi;
+    f2_unpack(f2_fma(f2_pack(0.0f, 0.0f), f2_pack(1.0f, 1.0f), f2_pack(__uint_as_float(o[0]), __uint_as_float(o[1]))), lo, hi);
+    out[2 * i] = lo;
+    out[2 * i + 1] = hi;
+  }
+}
+
 // ========================================================================== extern "C"
 extern "C" {
 
@@ -660,6 +675,14 @@ int lssab8_selftest_div(const float* y, const float* l, long long n, float* out,
   if (n == 0) return kOk;
   const int blocks = (int)std::min<long long>((n + 255) / 256, 148LL * 16);
   selftest_div_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(y, l, n, out);
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
+}
+
+int lssab8_selftest_rescale(const float* x, const int32_t* D, long long npairs, float* out, void* stream) {
+  if (!x || !D || !out || npairs < 0) return kErrArg;
+  if (npairs == 0) return kOk;
+  const int blocks = (int)std::min<long long>((npairs + 255) / 256, 148LL * 16);
+  selftest_rescale_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(x, D, npairs, out);
   return cudaGetLastError() == cudaSuccess ? kOk : kErrCuda;
 }
 

@@ -34,7 +34,8 @@
 // The A accumulator is pre-loaded with the bit pattern 0x4B400000 (the float 1.5 * 2^23) and
 // the PV MMA accumulates onto it, so the fold reads 1.5 * 2^23 + A_b as a float: one subtraction
 // recovers A_b exactly (|A_b| < 2^22) and one fused multiply-add folds it (exact product, one
-// rounding).  The fold writes the bias back after reading.
+// rounding).  The MMA thread writes the bias before every PV with tcgen05.cp from a 4 KB block
+// of bias words in shared memory, so the row workers spend no instructions on it.
 //
 // Exactness: S and A_b are exact integer sums (any MMA order); everything after them is the
 // contract's integer chain and a fixed sequence of RN binary32 operations per row
@@ -80,7 +81,8 @@ struct PrefillSmem {
   static constexpr int kV = 4 * kTile;                   // 2 stages
   static constexpr int kP = 6 * kTile;                   // 2 x 16 KB, SW128 K-major u8
   static constexpr int kV0 = kP + 2 * 16384;             // 2 items x key 0's int8 value row (sink)
-  static constexpr int kBar = kV0 + 2 * 128;             // mbarriers
+  static constexpr int kMagic = kV0 + 2 * 128;           // 4 KB of the A bias words (tcgen05.cp source)
+  static constexpr int kBar = kMagic + 4096;             // mbarriers
   static constexpr int kMisc = kBar + 256;               // tmem base, abort flag
   static constexpr int kBytes = kMisc + 64;              // (+ the static T2 table)
 };
@@ -107,6 +109,29 @@ __device__ __forceinline__ bool pf_item(const PrefillArgs& p, int ntile, int rou
   return true;
 }
 constexpr uint32_t kColS = 0, kColA = 128, kColO = 384;   // TMEM column map (A: two buffers of 128)
+
+// The fold's running-maximum rescale of N channels (binary32 bit patterns) of one row by D > 0
+// (reference/lssab8_golden.py:293-301; D <= 0 leaves them alone).  sD2 = (2^-min(D, 126)) twice.
+// D <= 126: one paired multiply rounded toward zero with flush to zero per two channels -- the
+// contract's exponent-field rescale except that a flushed negative value becomes -0, not +0; the
+// caller adds a term with a positive scale next, which makes it +0.  D > 126: the
+// compare-and-select form.  Register arithmetic only, so it may sit under per-row branches.
+template <int N>
+__device__ __forceinline__ void rescale_channels(uint32_t* o, int D, uint64_t sD2) {
+  if (D > 0 && D <= 126) {
+#pragma unroll
+    for (int t = 0; t < N / 2; ++t) {
+      float lo, hi;
+      f2_unpack(f2_mul_rz_ftz(f2_pack(__uint_as_float(o[2 * t]), __uint_as_float(o[2 * t + 1])), sD2), lo, hi);
+      o[2 * t] = __float_as_uint(lo);
+      o[2 * t + 1] = __float_as_uint(hi);
+    }
+  } else if (D > 126) {
+    const RowRescale rr = row_rescale(D);
+#pragma unroll
+    for (int c = 0; c < N; ++c) o[c] = __float_as_uint(apply_rescale(__uint_as_float(o[c]), rr));
+  }
+}
 
 // store n consecutive channels, vectorised when contiguous and aligned
 template <typename OutT, int N>
@@ -161,6 +186,9 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
+  for (int w4 = threadIdx.x; w4 < 4096 / 16; w4 += blockDim.x)            // the A bias block
+    st_shared_v4(smem_u32(smem + L::kMagic) + w4 * 16, kMagicBits, kMagicBits, kMagicBits, kMagicBits);
+  fence_async_smem();                                // read by tcgen05.cp (async proxy)
   for (int k4 = threadIdx.x; k4 * 4 < kTabEntries; k4 += blockDim.x) {   // 4 entries per thread,
     const uint32_t word = (k4 * 4 < kTabLive) ? reinterpret_cast<const uint32_t*>(kT2Live)[k4] : 0u;
 #pragma unroll
@@ -182,14 +210,10 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  if (warp >= 2) {                                   // row workers: bias both A buffers, zero O
+  if (warp >= 2) {                                   // row workers: zero O
     const uint32_t rowb = tmem + ((uint32_t)((warp & 3) * 32 + ((warp - 2) >> 2) * 16) << 16);
 #pragma unroll
-    for (int cc = 0; cc < DH / 32; ++cc) {
-      tmem_fill16x2<DH / 2>(rowb + kColA + cc * 16, kMagicBits);
-      tmem_fill16x2<DH / 2>(rowb + kColA + 128 + cc * 16, kMagicBits);
-      tmem_fill16x2<DH / 2>(rowb + kColO + cc * 16, 0u);
-    }
+    for (int cc = 0; cc < DH / 32; ++cc) tmem_fill16x2<DH / 2>(rowb + kColO + cc * 16, 0u);
     tc_wait_st();
   }
   tc_fence_before();
@@ -234,6 +258,10 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
       constexpr uint32_t kRowGroup = 8 * DH;                    // bytes per 8 rows of a tile
       constexpr uint32_t idesc_qk = idesc_i8(1, 1, 0, 128, 128);
       constexpr uint32_t idesc_pv = idesc_i8(0, 1, 1, 128, DH);
+      // the bias block as a no-swizzle 128-row x 32-byte matrix: core matrices of 8 rows x 16 B,
+      // 128 B apart along a row, 256 B apart down the rows (every word is the same, so only the
+      // extent matters: the copy reads 4 KB)
+      const uint64_t desc_bias = umma_desc(smem_u32(smem + L::kMagic), 128, 256, 0);
       int jj = 0, tt = 0;                                       // global block / item counters
       bool ok = true;
       auto issue_qk = [&](int jg, uint32_t sq) -> bool {
@@ -277,6 +305,8 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
           tc_fence_after();
           const uint32_t sp = smem_u32(smem + L::kP + s * 16384);
           const uint32_t sv = smem_u32(smem + L::kV + s * L::kTile);
+#pragma unroll
+          for (int c8 = 0; c8 < DH / 8; ++c8) tmem_cp_128x256b(tmem + kColA + s * 128 + c8 * 8, desc_bias);
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
             // A = P (K-major SW128, 32 keys = 32 bytes per step); B = V (MN-major: 32 keys =
@@ -356,7 +386,9 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
         const float scO = add ? pow2f(-(sg + evj)) : 0.0f;
         const uint64_t scO2 = f2_pack(scO, scO);
         const bool resc = __any_sync(0xffffffffu, Dr > 0);  // warp-uniform
-        const RowRescale rr = row_rescale(Dr);             // identity on lanes with Dr == 0
+        // rows with D > 0 have sg == 0, so the term added after their rescale has the positive
+        // scale 2^-e_v (|e_v| <= 126 for finite inputs) and turns a flushed -0 into +0
+        const uint64_t sD2 = f2_pack(pow2f(-min(Dr, 126)), pow2f(-min(Dr, 126)));
         // DH/2 channels per lane in passes of 32 (two TMEM round trips for DH = 128)
         constexpr int kPass = HALF < 32 ? HALF : 32;
   #pragma unroll 1
@@ -370,12 +402,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
             tmem_ld16x2<HALF>(ob + cc * 16, o + cc * 16);
           }
           tc_wait_ld();
-  #pragma unroll
-          for (int cc = 0; cc < kPass / 16; ++cc) tmem_fill16x2<HALF>(abase + cc * 16, kMagicBits);   // re-bias
-          if (resc) {
-  #pragma unroll
-            for (int c = 0; c < kPass; ++c) o[c] = __float_as_uint(apply_rescale(__uint_as_float(o[c]), rr));
-          }
+          if (resc) rescale_channels<kPass>(o, Dr, sD2);
           if (SINK && jf == 0 && p.T > 1) {                  // key 0's term first (B9.1); sg == 0 here
             const float sc0 = pow2f(-ev0);
             const uint64_t sc02 = f2_pack(sc0, sc0);

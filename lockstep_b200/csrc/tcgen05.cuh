@@ -47,6 +47,14 @@ __device__ __forceinline__ void umma_i8(uint32_t d_tmem, uint64_t adesc, uint64_
       ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc) : "memory");
 }
 
+// Shared memory -> TMEM copy of a 128-lane x 256-bit (8 columns of 32 bits) matrix, issued by
+// one thread like tcgen05.mma and executed in issue order with the tcgen05.mma instructions of
+// the same thread (a pipelined pair: no fence between the copy and an MMA that accumulates onto
+// it).
+__device__ __forceinline__ void tmem_cp_128x256b(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.128x256b [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
                ::"r"(smem_u32(bar)) : "memory");
@@ -159,6 +167,17 @@ __device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
 __device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
   uint64_t d;
   asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+// Paired multiply rounded toward zero with subnormal inputs and results flushed to zero of the
+// same sign.  With b = 2^-D (D in [1, 126], a normal power of two) this is the contract's
+// exponent-field rescale of a: a product whose biased exponent stays >= 1 is exact, and any
+// other is below 2^-126 before rounding, stays below it after rounding toward zero and is
+// flushed -- to -0 for negative a, where the contract gives +0 (callers add a term next, and
+// -0 + t == +0 + t for every t other than -0).
+__device__ __forceinline__ uint64_t f2_mul_rz_ftz(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rz.ftz.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
 }
 
