@@ -330,11 +330,15 @@ bool shape_ok(int B, int H, int KVH, int T, int dh) {
 
 }  // namespace
 
-// the prefill epilogue's division (div_rn_shared with the row reciprocal), one element per thread
+// the prefill epilogue's division (div_chunk with the row reciprocal) of y[i] by l[i], one element
+// per thread: the pair (y[i], y[i]) takes the paired path when y[i] and l[i] lie in the Markstein
+// window and the scalar one otherwise
 __global__ void selftest_div_kernel(const float* y, const float* l, long long n, float* out) {
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
     const float li = l[i];
-    out[i] = div_rn_shared(y[i], li, __frcp_rn(li));
+    float q[4] = {y[i], y[i], y[i], y[i]};
+    div_chunk<4, false>(q, li, __frcp_rn(li), div_window(li));
+    out[i] = q[0];
   }
 }
 

@@ -298,6 +298,8 @@ __device__ __forceinline__ bool group_wait(uint64_t* bar, uint32_t parity, bool 
 // cannot advance again before this warp arrives on the matching release barrier), which gives
 // each lane the acquire ordering.  Every lane returns the same value.
 __device__ __forceinline__ bool warp_poll(uint64_t* bar, uint32_t parity, volatile int* abort, int* err) {
+  // common case: the phase is already complete and every lane's own test says so (one test)
+  if (__all_sync(0xffffffffu, mbar_test(bar, parity))) return true;
   int ok = 0;
   if ((threadIdx.x & 31) == 0) ok = mbar_poll(bar, parity, abort, err) ? 1 : 0;
   ok = __shfl_sync(0xffffffffu, ok, 0);

@@ -133,6 +133,37 @@ __device__ __forceinline__ void rescale_channels(uint32_t* o, int D, uint64_t sD
   }
 }
 
+// fl(y[c] / l) for N values of one row (l != 0, rl = the correctly rounded 1 / l), the epilogue's
+// one RN division per element (reference/lssab8_golden.py:333).  When l and every y[c] lie in
+// the Markstein window the N quotients are computed on pairs: each lane of the paired multiply
+// and fused multiply-adds is the scalar div_markstein step (y - q l is formed as fma(q, -l, y),
+// the same exact value), so the results are the correctly rounded quotients; the window test is
+// a min/max of |y| over the chunk.  Otherwise each value takes div_rn_shared, after the
+// contract's rescale(y, 0) (zero and subnormal -> +0) when FLUSH.
+template <int N, bool FLUSH>
+__device__ __forceinline__ void div_chunk(float* y, float l, float rl, bool l_in_window) {
+  float mn[4], mx[4];
+#pragma unroll
+  for (int g = 0; g < 4; ++g) { mn[g] = fabsf(y[g]); mx[g] = mn[g]; }
+#pragma unroll
+  for (int c = 4; c < N; ++c) { mn[c & 3] = fminf(mn[c & 3], fabsf(y[c])); mx[c & 3] = fmaxf(mx[c & 3], fabsf(y[c])); }
+  const float lo = fminf(fminf(mn[0], mn[1]), fminf(mn[2], mn[3]));
+  const float hi = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+  if (l_in_window && lo >= 0x1p-31f && hi < 0x1p32f) {
+    const uint64_t rl2 = f2_pack(rl, rl), nl2 = f2_pack(-l, -l);
+#pragma unroll
+    for (int t = 0; t < N / 2; ++t) {
+      const uint64_t y2 = f2_pack(y[2 * t], y[2 * t + 1]);
+      const uint64_t q0 = f2_mul(y2, rl2);
+      const uint64_t q1 = f2_fma(f2_fma(q0, nl2, y2), rl2, q0);
+      f2_unpack(f2_fma(f2_fma(q1, nl2, y2), rl2, q1), y[2 * t], y[2 * t + 1]);
+    }
+  } else {
+#pragma unroll
+    for (int c = 0; c < N; ++c) y[c] = div_rn_shared(FLUSH ? rescale(y[c], 0) : y[c], l, rl);
+  }
+}
+
 // store n consecutive channels, vectorised when contiguous and aligned
 template <typename OutT, int N>
 __device__ __forceinline__ void store_chunk(OutT* dst, long long os3, const float* y) {
@@ -491,10 +522,17 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
   #pragma unroll
           for (int c = 0; c < 64; ++c) if (kh * 64 + c > r) v[c] = 0x80000000u;
         }
-        int m = __vimax3_s32((int)v[0], (int)v[1], (int)v[2]);
+        // four independent 16-score maxima, then their maximum: a dependency depth of 9 instead of 32
+        int mq[4];
   #pragma unroll
-        for (int c = 3; c < 63; c += 2) m = __vimax3_s32(m, (int)v[c], (int)v[c + 1]);
-        m = max(m, (int)v[63]);
+        for (int g4 = 0; g4 < 4; ++g4) {
+          const uint32_t* vg = v + 16 * g4;
+          int a = __vimax3_s32((int)vg[0], (int)vg[1], (int)vg[2]);
+  #pragma unroll
+          for (int c = 3; c < 15; c += 2) a = __vimax3_s32(a, (int)vg[c], (int)vg[c + 1]);
+          mq[g4] = max(a, (int)vg[15]);
+        }
+        int m = max(__vimax3_s32(mq[0], mq[1], mq[2]), mq[3]);
         m = max(m, __shfl_xor_sync(0xffffffffu, m, 16));  // the row's max over both key halves
         const uint32_t G = g_fold(p.gbase, eqr + ekj);
         const int nbv = nb_of(m, G);
@@ -505,7 +543,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
         const uint32_t negG = 0u - G;
         if (!warp_poll(&bars[kBarPEmpty + s], ph ^ 1, abort_flag, p.err)) { ok = false; break; }
         const uint32_t pbase = smem_u32(smem + L::kP + s * 16384) + prow;
-        uint32_t lb = 0, eh0 = 0;
+        uint32_t lbq[2] = {0u, 0u}, eh0 = 0;               // two l_b partial sums (shorter dp4a chains)
         // pass 2: the chain and the u8 P half-row, 16 keys (one 16-byte P chunk) at a time
   #pragma unroll
         for (int cc = 0; cc < 4; ++cc) {
@@ -521,7 +559,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
               e[x] = tab[ix * p.mul_entry + lane4];            // entry ix, this lane's copy
             }
             w[qq] = e[0] + e[1] * p.mul_b1 + e[2] * p.mul_b2 + e[3] * p.mul_b3;
-            lb = __dp4a(w[qq], 0x01010101u, lb);
+            lbq[qq & 1] = __dp4a(w[qq], 0x01010101u, lbq[qq & 1]);
           }
           const int chunk = kh * 4 + cc;
           if (SINK && chunk == 0 && j == 0 && p.T > 1) { eh0 = w[0] & 0xFFu; w[0] &= ~0xFFu; }
@@ -529,6 +567,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
         }
         fence_async_smem();
         mbar_arrive(&bars[kBarPFull + s]);
+        const uint32_t lb = lbq[0] + lbq[1];
         const int lbt = (int)lb + __shfl_xor_sync(0xffffffffu, (int)lb, 16);   // the row's l_b
         if (SINK && j == 0) eh0_row = __shfl_sync(0xffffffffu, (int)eh0, lane & 15);
         if (j > 0 && !fold_block(j - 1, nb_prev, lbt_prev, ev_prev, eh0_row)) { ok = false; break; }
@@ -547,7 +586,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
         const bool live = (i < p.T);
         const bool nz = (lrow != 0.0f);
         const float rl = nz ? __frcp_rn(lrow) : 0.0f;
-        const bool row_fast = nz && div_window(lrow);
+        const bool row_fast = div_window(lrow);
         OutT* dst = reinterpret_cast<OutT*>(p.out) + b * p.os0 + (long long)i * p.os1 + h * p.os2 + kh * HALF * p.os3;
   #pragma unroll 1
         for (int cc = 0; cc < HALF / 16; ++cc) {
@@ -564,12 +603,11 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
             for (int c = 0; c < 16; ++c) q[c] = live ? orow[cc * 16 + c] : 0.0f;
           }
           if (live) {
+            // a single segment divides rescale(O_seg, 0) (identity on the Markstein window)
+            if (nz) div_chunk<16, !MULTI>(q, lrow, rl, row_fast);
+            else {
   #pragma unroll
-            for (int c = 0; c < 16; ++c) {
-              // fast path: both operands inside the Markstein window (then O_seg is normal and
-              // rescale(O_seg, 0) is O_seg itself); anything else takes the IEEE division
-              if (row_fast && div_window(q[c])) q[c] = div_markstein(q[c], lrow, rl);
-              else q[c] = nz ? div_rn_ieee(MULTI ? q[c] : rescale(q[c], 0), lrow) : 0.0f;
+              for (int c = 0; c < 16; ++c) q[c] = 0.0f;
             }
             store_chunk<OutT, 16>(dst + cc * 16 * p.os3, p.os3, q);
           }
