@@ -504,6 +504,11 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
         const int jg = jj0 + j;
         const int s = jg & 1;
         const uint32_t ph = (jg >> 1) & 1;
+        // G and the exact-window width need only the exponents: computed while S(j) is in flight
+        const uint32_t G = g_fold(p.gbase, eqr + ekj);
+        const int lg = 31 - __clz((int)G);
+        const int dm = 1 << max(0, 30 - lg);              // dm * G in [2^30, 2^31): >= 9 doublings
+        const uint32_t negG = 0u - G;
         if (!warp_poll(&bars[kBarSFull], jg & 1, abort_flag, p.err)) { ok = false; break; }
         tc_fence_after();
         const bool diag = (j == tile);                     // key c of the diagonal block visible iff c <= r
@@ -534,13 +539,9 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
         }
         int m = max(__vimax3_s32(mq[0], mq[1], mq[2]), mq[3]);
         m = max(m, __shfl_xor_sync(0xffffffffu, m, 16));  // the row's max over both key halves
-        const uint32_t G = g_fold(p.gbase, eqr + ekj);
         const int nbv = nb_of(m, G);
         const uint32_t NBlo = (uint32_t)nbv << kBHI;
-        const int lg = 31 - __clz((int)G);
-        const int dm = 1 << max(0, 30 - lg);              // dm * G in [2^30, 2^31): >= 9 doublings
         const int lo = m - dm;
-        const uint32_t negG = 0u - G;
         if (!warp_poll(&bars[kBarPEmpty + s], ph ^ 1, abort_flag, p.err)) { ok = false; break; }
         const uint32_t pbase = smem_u32(smem + L::kP + s * 16384) + prow;
         uint32_t lbq[2] = {0u, 0u}, eh0 = 0;               // two l_b partial sums (shorter dp4a chains)
