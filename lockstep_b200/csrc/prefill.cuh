@@ -420,19 +420,12 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
         // rows with D > 0 have sg == 0, so the term added after their rescale has the positive
         // scale 2^-e_v (|e_v| <= 126 for finite inputs) and turns a flushed -0 into +0
         const uint64_t sD2 = f2_pack(pow2f(-min(Dr, 126)), pow2f(-min(Dr, 126)));
-        // DH/2 channels per lane in passes of 32 (two TMEM round trips for DH = 128)
+        // DH/2 channels per lane in passes of 32 (two TMEM round trips for DH = 128); the next
+        // pass's loads are issued before this pass's stores, so their latency overlaps
         constexpr int kPass = HALF < 32 ? HALF : 32;
-  #pragma unroll 1
-        for (int c0 = 0; c0 < HALF; c0 += kPass) {
-          const uint32_t abase = rowt + kColA + sa * 128 + c0;
-          const uint32_t ob = obase + c0;
-          uint32_t a[kPass], o[kPass];
-  #pragma unroll
-          for (int cc = 0; cc < kPass / 16; ++cc) {
-            tmem_ld16x2<HALF>(abase + cc * 16, a + cc * 16);
-            tmem_ld16x2<HALF>(ob + cc * 16, o + cc * 16);
-          }
-          tc_wait_ld();
+        constexpr int kNPass = HALF / kPass;
+        const uint32_t abase = rowt + kColA + sa * 128;
+        auto fold_pass = [&](int c0, uint32_t* a, uint32_t* o) {
           if (resc) rescale_channels<kPass>(o, Dr, sD2);
           if (SINK && jf == 0 && p.T > 1) {                  // key 0's term first (B9.1); sg == 0 here
             const float sc0 = pow2f(-ev0);
@@ -455,8 +448,33 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
             o[2 * t] = __float_as_uint(lo_);
             o[2 * t + 1] = __float_as_uint(hi_);
           }
+        };
+        auto load_pass = [&](int c0, uint32_t* a, uint32_t* o) {
   #pragma unroll
-          for (int cc = 0; cc < kPass / 16; ++cc) tmem_st16x2<HALF>(ob + cc * 16, o + cc * 16);
+          for (int cc = 0; cc < kPass / 16; ++cc) {
+            tmem_ld16x2<HALF>(abase + c0 + cc * 16, a + cc * 16);
+            tmem_ld16x2<HALF>(obase + c0 + cc * 16, o + cc * 16);
+          }
+        };
+        auto store_pass = [&](int c0, const uint32_t* o) {
+  #pragma unroll
+          for (int cc = 0; cc < kPass / 16; ++cc) tmem_st16x2<HALF>(obase + c0 + cc * 16, o + cc * 16);
+        };
+        {
+          uint32_t a0[kPass], o0[kPass];
+          load_pass(0, a0, o0);
+          tc_wait_ld();
+          fold_pass(0, a0, o0);
+          if constexpr (kNPass == 2) {
+            uint32_t a1[kPass], o1[kPass];
+            load_pass(kPass, a1, o1);
+            store_pass(0, o0);
+            tc_wait_ld();
+            fold_pass(kPass, a1, o1);
+            store_pass(kPass, o1);
+          } else {
+            store_pass(0, o0);
+          }
         }
         tc_wait_st();
         tc_fence_before();
