@@ -527,6 +527,8 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
         const int lg = 31 - __clz((int)G);
         const int dm = 1 << max(0, 30 - lg);              // dm * G in [2^30, 2^31): >= 9 doublings
         const uint32_t negG = 0u - G;
+        // P buffer s is free once PV(j - 2) has finished -- long before S(j) is ready
+        if (!warp_poll(&bars[kBarPEmpty + s], ph ^ 1, abort_flag, p.err)) { ok = false; break; }
         if (!warp_poll(&bars[kBarSFull], jg & 1, abort_flag, p.err)) { ok = false; break; }
         tc_fence_after();
         const bool diag = (j == tile);                     // key c of the diagonal block visible iff c <= r
@@ -560,7 +562,6 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
         const int nbv = nb_of(m, G);
         const uint32_t NBlo = (uint32_t)nbv << kBHI;
         const int lo = m - dm;
-        if (!warp_poll(&bars[kBarPEmpty + s], ph ^ 1, abort_flag, p.err)) { ok = false; break; }
         const uint32_t pbase = smem_u32(smem + L::kP + s * 16384) + prow;
         uint32_t lbq[2] = {0u, 0u}, eh0 = 0;               // two l_b partial sums (shorter dp4a chains)
         // pass 2: the chain and the u8 P half-row, 16 keys (one 16-byte P chunk) at a time
