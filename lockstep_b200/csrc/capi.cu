@@ -254,7 +254,7 @@ int launch_decode_tc_t(const DecodeArgs& a, int max_splits, int num_sms, cudaStr
   const long long chunks = ((long long)a.B * a.KVH * a.max_blocks + kDecChunk - 1) / kDecChunk;
   const int grid = (int)std::min<long long>(chunks, 2LL * std::max(num_sms, 1));   // two CTAs per SM
   if ((rc = launch_pdl(kfn, dim3(grid), dim3(kDecThreads), smem, st, tk, tq, a))) return rc;
-  return launch_pdl(decode_merge_kernel<SINK, OutT>, dim3(a.KVH, a.B, a.group), dim3(128), 0, st, a);
+  return launch_pdl(decode_merge_kernel<SINK, OutT>, dim3(a.KVH, a.B, a.group), dim3(kMergeThreads), 0, st, a);
 }
 
 template <bool SINK>

@@ -382,20 +382,23 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
 }
 
 // The committed-order refold of every (sequence, kv head, head) from its exact block partials:
-// one CTA per (kv head, sequence, head of the group), one thread per channel.  Per 32-block
-// segment: the partial rows (32 x 512 contiguous bytes) are staged into shared memory with
-// cp.async; warp 0 derives the segment's fold schedule, which depends on the block and head only
-// (running max by a prefix-max scan, rescale distance D, skip distance s, the scale
-// 2^-(s + e_v), and l folded by one lane); then every thread folds its channel with one exact
-// multiply-add per block (reference/lssab8_golden.py:257-335, 350-394).  A block past the skip
-// window gets scale +0, which leaves O bit-identical (O is never -0).
+// one CTA per (kv head, sequence, head of the group), one thread per channel plus one warp for
+// l.  Per 32-block segment: the partial rows (32 x 512 contiguous bytes) are staged into shared
+// memory with cp.async; warp 0 derives the segment's fold schedule, which depends on the block
+// and head only (running max by a prefix-max scan, rescale distance D, skip distance s, the
+// scale 2^-(s + e_v), and the segment -> row step); then every channel thread folds its channel
+// with one exact multiply-add per block while lane 0 of warp 4 folds l, in the same order
+// (reference/lssab8_golden.py:257-335, 350-394).  A block past the skip window gets scale +0,
+// which leaves O bit-identical (O is never -0).
+constexpr int kMergeThreads = 160;
 template <bool SINK, typename OutT>
-__global__ void __launch_bounds__(128) decode_merge_kernel(const DecodeArgs p) {
+__global__ void __launch_bounds__(kMergeThreads) decode_merge_kernel(const DecodeArgs p) {
   constexpr int DH = 128;
   __shared__ __align__(16) int sA[kSEG][DH];
   __shared__ int2 sM[kSEG];
   __shared__ int sEv[kSEG];
   __shared__ int sD[kSEG];                 // rescale distance before block u (0: none)
+  __shared__ int sS[kSEG];                 // skip distance of block u
   __shared__ float sSc[kSEG];              // 2^-(s_u + e_v,u), or +0 past the skip window
   __shared__ int sSeg[4];                  // segment -> row: D2, s2 (and the segment's NB)
   __shared__ float sLrow;
@@ -408,14 +411,14 @@ __global__ void __launch_bounds__(128) decode_merge_kernel(const DecodeArgs p) {
   if (L <= 0 || nblk > p.max_blocks || (L + 15) / 16 > p.max_pages) return;   // flagged by the stream kernel
   const long long bg = (long long)b * p.KVH + g;
   int v0c = 0, evs0 = 0, eh0 = 0;
-  if (SINK && L > 1) {
+  if (SINK && L > 1 && c < DH) {
     const int pg = p.block_table[(long long)b * p.max_pages];
     v0c = (int)p.v8p[((long long)pg * p.KVH + g) * (16 * DH) + c * 16 + 0];
     evs0 = p.ev0[bg];
     eh0 = __ldcg(&p.partM[(bg * p.max_blocks) * gq + h]).z;
   }
-  float Orow = 0.0f, lrow = 0.0f;          // lrow: warp 0 lane 0 only
-  int nbrow = 0;
+  float Orow = 0.0f, lrow = 0.0f;          // lrow: warp 4 lane 0 only
+  int nbrow = 0;                           // warp 0 lane 0 only
   for (int s0 = 0; s0 < nblk; s0 += kSEG) {
     const int n = min(kSEG, nblk - s0);
     for (int i = c; i < n * (DH / 4); i += blockDim.x) {     // 16-byte pieces of the n partial rows
@@ -449,45 +452,46 @@ __global__ void __launch_bounds__(128) decode_merge_kernel(const DecodeArgs p) {
         sM[lane] = m;
         sEv[lane] = ev;
         sD[lane] = D > 0 ? D : 0;
+        sS[lane] = sg;
         sSc[lane] = add ? pow2f(-(sg + ev)) : 0.0f;
       }
-      __syncwarp();
-      if (lane == 0) {                                       // l: the same rules, in order
-        float lseg = 0.0f;
-        int nbrun = sM[0].x;
-        for (int u = 0; u < n; ++u) {
-          const int Du = sM[u].x - nbrun;
-          int su = 0;
-          if (Du > 0) { lseg = rescale(lseg, Du); nbrun = sM[u].x; }
-          else su = -Du;
-          if (su <= kSWIN) lseg = fold_term(lseg, sM[u].y, pow2f(-su));
-        }
-        // segment -> row (reference/lssab8_golden.py:317-331)
+      // segment -> row (reference/lssab8_golden.py:317-331): the segment's NB is its running max
+      const int nbrun = __shfl_sync(0xffffffffu, run, n - 1);
+      if (lane == 0) {
         if (s0 == 0) nbrow = nbrun;
         const int D2 = nbrun - nbrow;
-        int s2 = 0;
-        if (D2 > 0) { lrow = rescale(lrow, D2); nbrow = nbrun; }
-        else s2 = -D2;
-        if (s2 <= kSWIN) lrow = __fadd_rn(lrow, rescale(lseg, s2));
+        if (D2 > 0) nbrow = nbrun;
         sSeg[0] = D2 > 0 ? D2 : 0;
-        sSeg[1] = s2;
-        sLrow = lrow;
+        sSeg[1] = D2 > 0 ? 0 : -D2;
       }
     }
     asm volatile("cp.async.wait_group 0;" ::: "memory");
     __syncthreads();
-    float O = 0.0f;
-    for (int u = 0; u < n; ++u) {
-      const int Du = sD[u];
-      if (Du > 0) O = rescale(O, Du);                        // block-uniform branch
-      if (SINK && s0 + u == 0 && L > 1) O = fold_term(O, eh0 * v0c, pow2f(-evs0));
-      O = fold_term(O, sA[u][c], sSc[u]);
-    }
     const int D2 = sSeg[0], s2 = sSeg[1];
-    if (D2 > 0) Orow = rescale(Orow, D2);
-    if (s2 <= kSWIN) Orow = __fadd_rn(Orow, rescale(O, s2));
+    if (c < DH) {
+      float O = 0.0f;
+      for (int u = 0; u < n; ++u) {
+        const int Du = sD[u];
+        if (Du > 0) O = rescale(O, Du);                      // block-uniform branch
+        if (SINK && s0 + u == 0 && L > 1) O = fold_term(O, eh0 * v0c, pow2f(-evs0));
+        O = fold_term(O, sA[u][c], sSc[u]);
+      }
+      if (D2 > 0) Orow = rescale(Orow, D2);
+      if (s2 <= kSWIN) Orow = __fadd_rn(Orow, rescale(O, s2));
+    } else if (c == DH) {                                    // l: the same rules, in the same order
+      float lseg = 0.0f;
+      for (int u = 0; u < n; ++u) {
+        const int Du = sD[u];
+        if (Du > 0) lseg = rescale(lseg, Du);
+        if (sS[u] <= kSWIN) lseg = fold_term(lseg, sM[u].y, pow2f(-sS[u]));
+      }
+      if (D2 > 0) lrow = rescale(lrow, D2);
+      if (s2 <= kSWIN) lrow = __fadd_rn(lrow, rescale(lseg, s2));
+      sLrow = lrow;
+    }
     __syncthreads();                                         // the stage and schedule are refilled next
   }
+  if (c >= DH) return;
   const float lr = sLrow;
   const float y = (lr != 0.0f) ? __fdiv_rn(Orow, lr) : 0.0f;
   OutT* dst = reinterpret_cast<OutT*>(p.out) + b * p.os0 + (long long)(g * gq + h) * p.os1 + c * p.os2;
