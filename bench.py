@@ -33,8 +33,8 @@ sys.path.insert(0, ROOT)
 METRIC = "LSSA-B8 attn: prefill % int8 MMA peak; decode KV GB/s; 0 bit diffs vs ref"
 # DRAM bytes (read + write) of one launch, from one `ncu --set full` capture of the same workload
 # (profiles/prefill_kernel_cfg2.md, profiles/decode_kernel_cfg3.md)
-PREFILL_TRAFFIC_BYTES = 68_198_000
-DECODE_TRAFFIC_BYTES = 602_742_000
+PREFILL_TRAFFIC_BYTES = 68_783_000
+DECODE_TRAFFIC_BYTES = 603_341_000
 CFG = dict(B=4, H=32, KVH=8, dh=128, T=2048, outliers=0.01)
 DEC = dict(B=32, H=32, KVH=8, dh=128, L=8192, nsplit=16)
 
