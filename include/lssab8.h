@@ -90,6 +90,20 @@ int lssab8_prefill_lattice(const int8_t* q8, const int32_t* eq, const int8_t* k8
                            int dh, int Tpad, float* orow_scratch, void* out, int out_dtype, const int64_t* os,
                            void* stream);
 
+/* Block-aligned chunked prefill on an append-only lattice: query rows [T0, T) of a sequence
+ * (T0 a multiple of 128) against keys [0, T).  q8/eq hold the chunk's rows only, quantised per
+ * row as by lssab8_quant_rows ([B, H, Tq, dh] / [B, H, Tq], Tq = 128*ceil((T - T0)/128));
+ * k8/v8/ek/ev/ev0 hold the lattice of the whole prefix [0, T) as lssab8_quant_blocks writes it
+ * (Tpad = 128*ceil(T/128)), so blocks completed by earlier chunks are reused as they are; out
+ * holds the chunk's T - T0 rows (row t of the sequence at t - T0); orow_scratch as in
+ * lssab8_prefill_lattice, B*H*Tq*dh floats, needed when T > 4096.  No counterpart entry point in
+ * the reference: its 128-aligned chunk invariance (reference/lssab8_selftest.py:292-317) makes
+ * the result bit-identical to rows [T0, T) of the whole prefill of length T. */
+int lssab8_prefill_chunk_lattice(const int8_t* q8, const int32_t* eq, const int8_t* k8, const int32_t* ek,
+                                 const int8_t* v8, const int32_t* ev, const int32_t* ev0, int B, int H, int KVH,
+                                 int T0, int T, int dh, float* orow_scratch, void* out, int out_dtype,
+                                 const int64_t* os, void* stream);
+
 /* Bytes of workspace lssab8_prefill needs for this shape. */
 size_t lssab8_prefill_workspace_size(int B, int H, int KVH, int T, int dh);
 

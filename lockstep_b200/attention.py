@@ -113,6 +113,37 @@ def prefill_lattice(q8, eq, k8, ek, v8, ev, ev0, T, out=None, out_dtype=torch.bf
     return out
 
 
+def prefill_chunk_lattice(q8, eq, k8, ek, v8, ev, ev0, T0, T, out=None, out_dtype=torch.bfloat16):
+    """Block-aligned chunked prefill: query rows [T0, T) (T0 a multiple of 128) against keys [0, T).
+
+    q8/eq: the chunk's rows from quant_rows (padded to a multiple of 128 rows); k8/ek/v8/ev/ev0:
+    the key lattice of the whole prefix [0, T) from quant_blocks, whose complete blocks earlier
+    chunks have already written.  Returns out [B, T - T0, H, dh] (or writes `out`), bit-identical
+    to rows [T0, T) of the whole prefill of length T (the reference's 128-aligned chunk
+    invariance, reference/lssab8_selftest.py:292-317).
+    """
+    dev = _require_cuda(q8, eq, k8, ek, v8, ev)
+    B, H, Tq, dh = q8.shape
+    KVH = k8.shape[1]
+    if T0 % KB or not 0 <= T0 < T:
+        raise ValueError("chunk start %d must be a multiple of %d below T = %d" % (T0, KB, T))
+    if Tq != tpad(T - T0) or k8.shape[2] != tpad(T):
+        raise ValueError("lattice shapes do not match the chunk [%d, %d)" % (T0, T))
+    if out is None:
+        out = torch.empty((B, T - T0, H, dh), dtype=out_dtype, device=dev)
+    orow = None
+    if tpad(T) // KB > 32:                  # rows spanning more than one fold segment
+        orow = workspace(dev, B * H * Tq * dh * 4)
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().lssab8_prefill_chunk_lattice(
+            q8.data_ptr(), eq.data_ptr(), k8.data_ptr(), ek.data_ptr(), v8.data_ptr(), ev.data_ptr(),
+            None if ev0 is None else ev0.data_ptr(), B, H, KVH, T0, T, dh,
+            None if orow is None else orow.data_ptr(), out.data_ptr(), dtype_code(out.dtype),
+            _lib.i64x(out.stride()), _stream_handle(dev)),
+            "lssab8_prefill_chunk_lattice")
+    return out
+
+
 def prefill(query, key, value, sink=False, out=None, out_dtype=None, check=True):
     """Batched LSSA-B8 (sink=False) / B9.1 sink_alone (sink=True) causal GQA prefill.
 

@@ -357,6 +357,43 @@ __global__ void selftest_rescale_kernel(const float* x, const int* D, long long 
   }
 }
 
+// Causal prefill of query rows [T0, T) (T0 a multiple of 128) against the key lattice of [0, T):
+// q8/eq hold the chunk's rows (Tpad = tpad(T - T0)), k8/v8/ek/ev the whole prefix
+// (Tpad = tpad(T)), out the chunk's T - T0 rows.  T0 = 0 is the whole prefill.
+static int prefill_lattice_impl(const int8_t* q8, const int32_t* eq, const int8_t* k8, const int32_t* ek, const int8_t* v8,
+                         const int32_t* ev, const int32_t* ev0, int B, int H, int KVH, int T0, int T, int dh,
+                         float* orow_scratch, void* out, int out_dtype, const int64_t* os, void* stream) {
+  if (!q8 || !eq || !k8 || !ek || !v8 || !ev || !out || !shape_ok(B, H, KVH, T, dh) || !strides_ok(os, 4))
+    return kErrArg;
+  if (dh != 64 && dh != 128) return kErrUnsupported;
+  const int TpadQ = tpad_of(T - T0), TpadK = tpad_of(T);
+  DevState* ds = nullptr;
+  int rc = dev_state(&ds);
+  if (rc) return rc;
+  CUtensorMap tq, tk, tv;
+  if ((rc = make_tmap(&tq, q8, (long long)B * H * TpadQ, dh))) return rc;
+  if ((rc = make_tmap(&tk, k8, (long long)B * KVH * TpadK, dh))) return rc;
+  if ((rc = make_tmap(&tv, v8, (long long)B * KVH * TpadK, dh))) return rc;
+  PrefillArgs a{};
+  a.B = B; a.H = H; a.KVH = KVH; a.T = T; a.dh = dh; a.Tpad = TpadQ; a.nblk = TpadK / 128; a.group = H / KVH;
+  a.tile0 = T0 / 128;
+  a.eq = eq; a.ek = ek; a.ev = ev; a.ev0 = ev0; a.v8 = v8;
+  a.out = out; a.os0 = os[0]; a.os1 = os[1]; a.os2 = os[2]; a.os3 = os[3]; a.out_dtype = out_dtype;
+  a.orow = orow_scratch;
+  a.gbase = gbase_of(dh);
+  a.mul_entry = kTabCopies * 4;
+  a.mul_b1 = 1u << 8;
+  a.mul_b2 = 1u << 16;
+  a.mul_b3 = 1u << 24;
+  a.err = ds->err;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool sink = ev0 != nullptr;
+  if (dh == 128) return sink ? launch_prefill_out<128, true>(out_dtype, tq, tk, tv, a, ds->num_sms, st)
+                             : launch_prefill_out<128, false>(out_dtype, tq, tk, tv, a, ds->num_sms, st);
+  return sink ? launch_prefill_out<64, true>(out_dtype, tq, tk, tv, a, ds->num_sms, st)
+              : launch_prefill_out<64, false>(out_dtype, tq, tk, tv, a, ds->num_sms, st);
+}
+
 // ========================================================================== extern "C"
 extern "C" {
 
@@ -460,34 +497,18 @@ int lssab8_prefill_lattice(const int8_t* q8, const int32_t* eq, const int8_t* k8
                            const int8_t* v8, const int32_t* ev, const int32_t* ev0, int B, int H, int KVH, int T,
                            int dh, int Tpad, float* orow_scratch, void* out, int out_dtype, const int64_t* os,
                            void* stream) {
-  if (!q8 || !eq || !k8 || !ek || !v8 || !ev || !out || !shape_ok(B, H, KVH, T, dh) || Tpad != tpad_of(T) ||
-      !strides_ok(os, 4))
-    return kErrArg;
-  if (dh != 64 && dh != 128) return kErrUnsupported;
-  DevState* ds = nullptr;
-  int rc = dev_state(&ds);
-  if (rc) return rc;
-  CUtensorMap tq, tk, tv;
-  if ((rc = make_tmap(&tq, q8, (long long)B * H * Tpad, dh))) return rc;
-  if ((rc = make_tmap(&tk, k8, (long long)B * KVH * Tpad, dh))) return rc;
-  if ((rc = make_tmap(&tv, v8, (long long)B * KVH * Tpad, dh))) return rc;
-  PrefillArgs a{};
-  a.B = B; a.H = H; a.KVH = KVH; a.T = T; a.dh = dh; a.Tpad = Tpad; a.nblk = Tpad / 128; a.group = H / KVH;
-  a.eq = eq; a.ek = ek; a.ev = ev; a.ev0 = ev0; a.v8 = v8;
-  a.out = out; a.os0 = os[0]; a.os1 = os[1]; a.os2 = os[2]; a.os3 = os[3]; a.out_dtype = out_dtype;
-  a.orow = orow_scratch;
-  a.gbase = gbase_of(dh);
-  a.mul_entry = kTabCopies * 4;
-  a.mul_b1 = 1u << 8;
-  a.mul_b2 = 1u << 16;
-  a.mul_b3 = 1u << 24;
-  a.err = ds->err;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const bool sink = ev0 != nullptr;
-  if (dh == 128) return sink ? launch_prefill_out<128, true>(out_dtype, tq, tk, tv, a, ds->num_sms, st)
-                             : launch_prefill_out<128, false>(out_dtype, tq, tk, tv, a, ds->num_sms, st);
-  return sink ? launch_prefill_out<64, true>(out_dtype, tq, tk, tv, a, ds->num_sms, st)
-              : launch_prefill_out<64, false>(out_dtype, tq, tk, tv, a, ds->num_sms, st);
+  if (Tpad != tpad_of(T)) return kErrArg;
+  return prefill_lattice_impl(q8, eq, k8, ek, v8, ev, ev0, B, H, KVH, 0, T, dh, orow_scratch, out, out_dtype, os,
+                              stream);
+}
+
+int lssab8_prefill_chunk_lattice(const int8_t* q8, const int32_t* eq, const int8_t* k8, const int32_t* ek,
+                                 const int8_t* v8, const int32_t* ev, const int32_t* ev0, int B, int H, int KVH,
+                                 int T0, int T, int dh, float* orow_scratch, void* out, int out_dtype,
+                                 const int64_t* os, void* stream) {
+  if (T0 < 0 || T0 % 128 != 0 || T0 >= T) return kErrArg;
+  return prefill_lattice_impl(q8, eq, k8, ek, v8, ev, ev0, B, H, KVH, T0, T, dh, orow_scratch, out, out_dtype, os,
+                              stream);
 }
 
 size_t lssab8_prefill_workspace_size(int B, int H, int KVH, int T, int dh) {

@@ -6,6 +6,8 @@
 // docs/contract/BLOCK_EXPONENT_VARIANT.md B8.6).  Every pipeline (the TMA ring, S, P, A) runs on
 // counters that continue across items, so the next item's loads and QK overlap this item's
 // last folds and epilogue, and the setup (T2 copies, barriers, TMEM) is paid once per SM.
+// A block-aligned chunk of query rows [128 tile0, T) runs the same way: query tile t of the chunk
+// is key block tile0 + t of the sequence, and walks key blocks 0 .. tile0 + t.
 // Warp-specialised roles:
 //
 //   warp 0      TMA producer: per item the Q tile (double-buffered across items) and key 0's
@@ -48,6 +50,7 @@
 namespace lssab8 {
 struct PrefillArgs {
   int B, H, KVH, T, dh, Tpad, nblk, group;
+  int tile0;            // key-block index of the first query tile (a block-aligned chunk; 0: whole prefill)
   const int32_t* eq;    // [B, H, Tpad]
   const int32_t* ek;    // [B, KVH, nblk]
   const int32_t* ev;    // [B, KVH, nblk]
@@ -97,6 +100,7 @@ enum BarId : int {
 // rounds (snake order, G = gridDim.x), which balances the decreasing item sizes.
 struct PfItem {
   int tile, b, h;
+  int kt;               // the tile's key-block index: tile0 + tile (the diagonal block)
 };
 __device__ __forceinline__ bool pf_item(const PrefillArgs& p, int ntile, int round, PfItem& it) {
   const int G = gridDim.x;
@@ -104,6 +108,7 @@ __device__ __forceinline__ bool pf_item(const PrefillArgs& p, int ntile, int rou
   if (i >= ntile * p.B * p.H) return false;
   const int bh = i % (p.B * p.H);
   it.tile = ntile - 1 - i / (p.B * p.H);
+  it.kt = p.tile0 + it.tile;
   it.b = bh / p.H;
   it.h = bh % p.H;
   return true;
@@ -262,14 +267,14 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
         if (!pf_item(p, ntile, rd, it)) continue;
         const int g = it.h / p.group;
         const int qrow0 = (it.b * p.H + it.h) * p.Tpad + it.tile * 128;
-        const int krow0 = (it.b * p.KVH + g) * p.Tpad;
+        const int krow0 = (it.b * p.KVH + g) * (p.nblk * 128);
         const int qb = tt & 1;
         // buffer qb is free once item tt - 2's last QK has finished and its workers are done
         if (!mbar_wait(&bars[kBarQEmpty + qb], ((tt >> 1) & 1) ^ 1, abort_flag, p.err, 128)) { ok = false; break; }
         mbar_expect_tx(&bars[kBarQFull + qb], L::kTile + (SINK ? DH : 0));
         tma_load_2d(smem + L::kQ + qb * L::kTile, &tm_q, 0, qrow0, &bars[kBarQFull + qb]);
         if (SINK) bulk_g2s(v0row + qb * 128, p.v8 + (long long)krow0 * DH, DH, &bars[kBarQFull + qb]);
-        for (int j = 0; j <= it.tile; ++j, ++jj) {
+        for (int j = 0; j <= it.kt; ++j, ++jj) {
           const int s = jj & 1;
           const uint32_t ph = (jj >> 1) & 1;
           if (!mbar_wait(&bars[kBarKEmpty + s], ph ^ 1, abort_flag, p.err, 128)) { ok = false; break; }
@@ -316,7 +321,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
       PfItem it;
       for (int rd = 0; ok && rd < nrounds; ++rd) {
         if (!pf_item(p, ntile, rd, it)) continue;
-        const int nb = it.tile + 1;
+        const int nb = it.kt + 1;
         const int qb = tt & 1;
         if (!mbar_wait(&bars[kBarQFull + qb], (tt >> 1) & 1, abort_flag, p.err)) { ok = false; break; }
         const uint32_t sq = smem_u32(smem + L::kQ + qb * L::kTile);
@@ -379,9 +384,9 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
     PfItem it;
     for (int rd = 0; ok && rd < nrounds; ++rd) {
       if (!pf_item(p, ntile, rd, it)) continue;
-      const int tile = it.tile, b = it.b, h = it.h;
+      const int tile = it.tile, kt = it.kt, b = it.b, h = it.h;
       const int g = h / p.group;
-      const int nb = tile + 1;                           // causal: blocks 0 .. tile
+      const int nb = kt + 1;                             // causal: key blocks 0 .. kt
       const int qrow0 = (b * p.H + h) * p.Tpad + tile * 128;
       const int qb = tt & 1;
       const int8_t* v0 = v0row + qb * 128;               // key 0's value row of this item (sink)
@@ -531,7 +536,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
         if (!warp_poll(&bars[kBarPEmpty + s], ph ^ 1, abort_flag, p.err)) { ok = false; break; }
         if (!warp_poll(&bars[kBarSFull], jg & 1, abort_flag, p.err)) { ok = false; break; }
         tc_fence_after();
-        const bool diag = (j == tile);                     // key c of the diagonal block visible iff c <= r
+        const bool diag = (j == kt);                       // key c of the diagonal block visible iff c <= r
         // pass 1: this lane's 64 scores into registers (one TMEM round trip; S is free for the
         // next QK as soon as they have landed) and the exact max over its visible keys
         uint32_t v[64];
@@ -602,12 +607,13 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
       // TMEM loads run on every lane or on none; rows past T skip only the store.
       if (ok) {
         if constexpr (!MULTI) lrow = rescale(lseg, 0);   // a single segment: O_row = 0 + rescale(O_seg, 0)
-        const int i = tile * 128 + r;
+        const int i = kt * 128 + r;                      // the row's position in the sequence
         const bool live = (i < p.T);
         const bool nz = (lrow != 0.0f);
         const float rl = nz ? __frcp_rn(lrow) : 0.0f;
         const bool row_fast = div_window(lrow);
-        OutT* dst = reinterpret_cast<OutT*>(p.out) + b * p.os0 + (long long)i * p.os1 + h * p.os2 + kh * HALF * p.os3;
+        OutT* dst = reinterpret_cast<OutT*>(p.out) + b * p.os0 + (long long)(i - p.tile0 * 128) * p.os1 + h * p.os2 +
+                    kh * HALF * p.os3;                   // out holds the chunk's rows
   #pragma unroll 1
         for (int cc = 0; cc < HALF / 16; ++cc) {
           float q[16];
