@@ -77,6 +77,13 @@ int lssab8_quant_rows(const void* x, int dtype, int B, int H, int T, int dh, con
 int lssab8_quant_blocks(const void* x, int dtype, int B, int KVH, int T, int dh, const int64_t* xs, int Tpad,
                         int mode, int8_t* x8, int32_t* e, int32_t* e0, void* stream);
 
+/* P2 with the key offset: k' = fl(f32(k) - mu[g, c]) in binary32, then the B8 block quantiser
+ * (mode 0) on k'.  mu [KVH, dh] float32 on the device, one offset per kv head and channel (the
+ * reference's per-layer mu[layer], reference/lssab8_torch.py:143-144, reference/lssab_golden.py:
+ * 214-221).  k8/ek as lssab8_quant_blocks writes them. */
+int lssab8_quant_keys_offset(const void* k, int dtype, int B, int KVH, int T, int dh, const int64_t* ks, int Tpad,
+                             const float* mu, int8_t* k8, int32_t* ek, void* stream);
+
 /* --------------------------------------------------------------------------- prefill */
 
 /* Causal GQA prefill on a prepared lattice (the output of the two quantisers with

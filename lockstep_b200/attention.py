@@ -94,6 +94,25 @@ def quant_blocks(x, mode=0):
     return x8, e, e0
 
 
+def quant_keys_offset(k, mu):
+    """P2 with the key offset: k [B, KVH, T, dh], mu [KVH, dh] -> (k8 [B, KVH, Tpad, dh], ek [B, KVH, nblk])
+    of k' = fl(f32(k) - mu[g, c]) (reference/lssab8_torch.py:143-144)."""
+    dev = _require_cuda(k, mu)
+    B, KVH, T, dh = k.shape
+    mu = mu.to(device=dev, dtype=torch.float32).contiguous()
+    if tuple(mu.shape) != (KVH, dh):
+        raise ValueError("mu must be [KVH, dh] = [%d, %d], got %s" % (KVH, dh, tuple(mu.shape)))
+    Tp = tpad(T)
+    k8 = torch.empty((B, KVH, Tp, dh), dtype=torch.int8, device=dev)
+    ek = torch.empty((B, KVH, Tp // KB), dtype=torch.int32, device=dev)
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().lssab8_quant_keys_offset(k.data_ptr(), dtype_code(k.dtype), B, KVH, T, dh,
+                                                        _lib.i64x(k.stride()), Tp, mu.data_ptr(), k8.data_ptr(),
+                                                        ek.data_ptr(), _stream_handle(dev)),
+                   "lssab8_quant_keys_offset")
+    return k8, ek
+
+
 def prefill_lattice(q8, eq, k8, ek, v8, ev, ev0, T, out=None, out_dtype=torch.bfloat16):
     """Prefill on a prepared lattice; returns out [B, T, H, dh] (or writes `out`)."""
     dev = _require_cuda(q8, eq, k8, ek, v8, ev)
@@ -144,12 +163,13 @@ def prefill_chunk_lattice(q8, eq, k8, ek, v8, ev, ev0, T0, T, out=None, out_dtyp
     return out
 
 
-def prefill(query, key, value, sink=False, out=None, out_dtype=None, check=True):
+def prefill(query, key, value, sink=False, out=None, out_dtype=None, check=True, mu=None):
     """Batched LSSA-B8 (sink=False) / B9.1 sink_alone (sink=True) causal GQA prefill.
 
     query [B, H, T, dh], key/value [B, KVH, T, dh] (any strides, one dtype) -> out [B, T, H, dh]
     in out_dtype (default query.dtype).  Each batch element is the reference drop-in's function
-    (reference/lssab8_torch.py:134-271, reference/lssab9_torch.py:109-326)."""
+    (reference/lssab8_torch.py:134-271, reference/lssab9_torch.py:109-326).  mu [KVH, dh]: the
+    key offset subtracted before the key quantiser (reference/lssab8_torch.py:143-144)."""
     dev = _require_cuda(query, key, value)
     if not (query.dtype == key.dtype == value.dtype):
         raise TypeError("query, key and value must share one dtype")
@@ -161,6 +181,14 @@ def prefill(query, key, value, sink=False, out=None, out_dtype=None, check=True)
         raise ValueError("query heads must be a multiple of kv heads")
     if out is None:
         out = torch.empty((B, T, H, dh), dtype=out_dtype or query.dtype, device=dev)
+    if mu is not None:                      # the offset keys take the lattice route
+        q8, eq = quant_rows(query)
+        k8, ek = quant_keys_offset(key, mu)
+        v8, ev, ev0 = quant_blocks(value, 2 if sink else 0)
+        prefill_lattice(q8, eq, k8, ek, v8, ev, ev0 if sink else None, T, out=out)
+        if check:
+            check_device_errors(dev)
+        return out
     L = _lib.load()
     nbytes = L.lssab8_prefill_workspace_size(B, H, KVH, T, dh)
     if nbytes == 0:

@@ -488,7 +488,25 @@ int lssab8_quant_blocks(const void* x, int dtype, int B, int KVH, int T, int dh,
       return launch_rc();
     }
     quant_blocks_kernel<InT><<<grid, 256, 0, st>>>(static_cast<const InT*>(x), s, B, KVH, T, dh, Tpad, mode, x8, e, e0,
-                                                   ds->err);
+                                                   nullptr, ds->err);
+    return launch_rc();
+  });
+}
+
+int lssab8_quant_keys_offset(const void* k, int dtype, int B, int KVH, int T, int dh, const int64_t* ks, int Tpad,
+                             const float* mu, int8_t* k8, int32_t* ek, void* stream) {
+  if (!k || !mu || !k8 || !ek || !shape_ok(B, KVH, KVH, T, dh) || Tpad < tpad_of(T) || !strides_ok(ks, 4))
+    return kErrArg;
+  DevState* ds = nullptr;
+  int rc = dev_state(&ds);
+  if (rc) return rc;
+  Strides4 s{ks[0], ks[1], ks[2], ks[3]};
+  dim3 grid((T + 127) / 128, KVH, B);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return with_in_dtype(dtype, [&](auto tag) {
+    using InT = std::remove_const_t<std::remove_pointer_t<decltype(tag)>>;
+    quant_blocks_kernel<InT><<<grid, 256, 0, st>>>(static_cast<const InT*>(k), s, B, KVH, T, dh, Tpad, 0, k8, ek,
+                                                   nullptr, mu, ds->err);
     return launch_rc();
   });
 }

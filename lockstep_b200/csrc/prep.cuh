@@ -59,11 +59,13 @@ quant_rows_kernel(const InT* __restrict__ x, Strides4 xs, int B, int H, int T, i
 //   mode 1: B9 value grid, clamp [-32, 48], then e outside [-32, 40] sets kDevEvRange
 //   mode 2: B9.1 sink_alone: as mode 1, and when T > 1 key 0 is quantised alone (e0) while
 //           block 0's exponent covers keys 1 .. min(KB, T)-1.
+// mu [KVH, dh] (keys only, may be null): the key offset, subtracted in binary32 before both
+// passes, k' = fl(f32(k) - mu[g, c]) (reference/lssab_golden.py:221, reference/lssab8_torch.py:143-144).
 template <typename InT>
 __global__ void __launch_bounds__(256)
 quant_blocks_kernel(const InT* __restrict__ x, Strides4 xs, int B, int KVH, int T, int dh, int Tpad,
                     int mode, int8_t* __restrict__ x8, int32_t* __restrict__ eblk, int32_t* __restrict__ e0,
-                    int* __restrict__ err) {
+                    const float* __restrict__ mu, int* __restrict__ err) {
   const int blk = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
   const int nblk = (T + kKB - 1) / kKB;
   const int lo = blk * kKB;
@@ -77,7 +79,9 @@ quant_blocks_kernel(const InT* __restrict__ x, Strides4 xs, int B, int KVH, int 
   const int n = (hi - lo) * dh;
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
     int r = lo + i / dh, c = i % dh;
-    float a = fabsf(to_f32(src[(long long)r * xs.s2 + (long long)c * xs.s3]));
+    float a = to_f32(src[(long long)r * xs.s2 + (long long)c * xs.s3]);
+    if (mu) a = __fsub_rn(a, mu[g * dh + c]);
+    a = fabsf(a);
     if (split0 && r == 0) m0 = fmaxf(m0, a); else m = fmaxf(m, a);
   }
 #pragma unroll
@@ -97,6 +101,7 @@ quant_blocks_kernel(const InT* __restrict__ x, Strides4 xs, int B, int KVH, int 
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
     int r = lo + i / dh, c = i % dh;
     float v = to_f32(src[(long long)r * xs.s2 + (long long)c * xs.s3]);
+    if (mu) v = __fsub_rn(v, mu[g * dh + c]);
     dst[(long long)r * dh + c] = (int8_t)quant8(v, (split0 && r == 0) ? sc0 : sc);
   }
   // zero the padding rows of the last block

@@ -27,19 +27,19 @@ def make_lssab9_long_attn(kb=KB, bhi=BHI, n=NIDX, w_loc=W_LOC, weight="rn", s_wi
         Bsz, H, T, dh = query.shape
         assert Bsz == 1, "B=1 windows only"
         # B9's value grid is used even with the sink off (clamp 48, assert 40)
-        out = _A.prefill(query, key, value, sink=bool(sink_alone), out_dtype=query.dtype) if sink_alone else \
-            _prefill_b9_value_grid(query, key, value)
+        mu_l = B8._mu_for(mu, module, query.device)
+        out = _A.prefill(query, key, value, sink=True, out_dtype=query.dtype, mu=mu_l) if sink_alone else \
+            _prefill_b9_value_grid(query, key, value, mu_l)
         return out, None
     return attn
 
 
-def _prefill_b9_value_grid(query, key, value):
+def _prefill_b9_value_grid(query, key, value, mu=None):
     """Sink off under B9: the B8 result plus the B9 quantiser's e_v assert."""
-    import torch
     _, e, _ = _A.quant_blocks(value, mode=1)
     _A.check_device_errors(value.device)
     del e
-    return _A.prefill(query, key, value, sink=False, out_dtype=query.dtype)
+    return _A.prefill(query, key, value, sink=False, out_dtype=query.dtype, mu=mu)
 
 
 def make_lssab9_attn(head_chunk=16, **kw):

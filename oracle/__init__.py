@@ -114,8 +114,11 @@ def quant_blocks(x, mode=0):
     return x8, e, e0, err
 
 
-def prep(q, k, v, sink=False):
-    """PREP of reference/lssab_golden.py:214-235 (+ B9 value grid when sink is on)."""
+def prep(q, k, v, sink=False, mu=None):
+    """PREP of reference/lssab_golden.py:214-235 (+ B9 value grid when sink is on).  mu [KVH, dh]:
+    the key offset, k' = fl32(k - mu) before the key quantiser (reference/lssab_golden.py:221)."""
+    if mu is not None:
+        k = (np.asarray(k, np.float32) - np.asarray(mu, np.float32)[:, None, :]).astype(np.float32)
     q8, eq = quant_rows(q)
     k8, ek, _, _ = quant_blocks(k, 0)
     T = q.shape[1]
@@ -165,10 +168,10 @@ def core(p, causal=True, rows=None, key_lo=0, key_hi=None, debug=False, nthreads
     return out
 
 
-def attention(q, k, v, sink=False, causal=True, rows=None, nthreads=None):
+def attention(q, k, v, sink=False, causal=True, rows=None, nthreads=None, mu=None):
     """lssab8_attention / lssab9_attention(sink_alone) (reference/lssab8_golden.py:341,
     reference/lssab9_golden.py:254): q [H,T,dh], k/v [KVH,T,dh] -> f32 [H,T,dh]."""
-    p = prep(np.asarray(q, np.float32), np.asarray(k, np.float32), np.asarray(v, np.float32), sink)
+    p = prep(np.asarray(q, np.float32), np.asarray(k, np.float32), np.asarray(v, np.float32), sink, mu=mu)
     return core(p, causal=causal, rows=rows, nthreads=nthreads)
 
 

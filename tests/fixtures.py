@@ -140,3 +140,20 @@ def all_cases():
 def digest(a):
     import hashlib
     return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+def mu_cases():
+    """Inputs for the key-offset (mu) gate: keys carry a large per-channel offset, as real keys do,
+    and mu [KVH, dh] removes most of it (float32; the offset stays inexact, so the binary32
+    subtraction is exercised)."""
+    out = []
+    for tag, seed, H, KVH, T, dh in (("mu_h4kv2_t300_d64", 21, 4, 2, 300, 64),
+                                     ("mu_h4kv1_t257_d128", 22, 4, 1, 257, 128)):
+        g = np.random.RandomState(seed)
+        off = (g.standard_normal((KVH, dh)) * 6.0).astype(np.float32)
+        q = g.standard_normal((H, T, dh)).astype(np.float32)
+        k = (g.standard_normal((KVH, T, dh)) + off[:, None, :]).astype(np.float32)
+        v = g.standard_normal((KVH, T, dh)).astype(np.float32)
+        mu = (off + g.standard_normal((KVH, dh)).astype(np.float32) * np.float32(0.1)).astype(np.float32)
+        out.append(dict(tag=tag, q=q, k=k, v=v, mu=mu))
+    return out

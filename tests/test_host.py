@@ -25,9 +25,15 @@ def test_control_arms_have_no_kernel(arm):
         L8.build_arm8(arm)
 
 
-def test_mu_not_built():
-    with pytest.raises(NotImplementedError):
-        L8.make_lssab8_long_attn(mu=[torch.zeros(1, 128)])
+def test_key_offset_selected_by_layer():
+    assert callable(L8.make_lssab8_long_attn(mu=[torch.zeros(1, 128)]))
+
+    class _M:
+        layer_idx = 1
+    mu = [torch.zeros(2, 64), torch.full((2, 64), 0.5)]
+    got = L8._mu_for(mu, _M(), torch.device("cpu"))
+    assert got.dtype == torch.float32 and got.shape == (2, 64) and float(got[0, 0]) == 0.5
+    assert L8._mu_for(None, _M(), torch.device("cpu")) is None
 
 
 def test_b9_options():

@@ -105,3 +105,20 @@ def test_decode_row_equals_prefill_last_row():
         full = O.attention(q, k, v, rows=[T - 1])[:, T - 1]
         row = O.decode_rows(q[:, T - 1], k, v)
         assert np.array_equal(GD.f32bits(full), GD.f32bits(row))
+
+
+def _golden_mu():
+    import json
+    import os
+    with open(os.path.join(GD.GOLDEN_DIR, "golden_mu.json")) as f:
+        return json.load(f)
+
+
+@pytest.mark.parametrize("case", FX.mu_cases(), ids=[c["tag"] for c in FX.mu_cases()])
+def test_oracle_key_offset_equals_reference_golden(case):
+    rec = _golden_mu()[case["tag"]]
+    q, k, v, mu = case["q"], case["k"], case["v"], case["mu"]
+    assert GD.sha(np.concatenate([q.ravel(), k.ravel(), v.ravel(), mu.ravel()])) == rec["inputs"]
+    assert GD.sha(GD.f32bits(O.attention(q, k, v, mu=mu))) == rec["b8_mu"]
+    assert GD.sha(GD.f32bits(O.attention(q, k, v, sink=True, mu=mu))) == rec["b9sink_mu"]
+    assert GD.sha(GD.f32bits(O.attention(q, k, v))) == rec["b8_no_mu"]
