@@ -59,6 +59,10 @@ def test_bad_arguments_return_status_codes():
     fake = ctypes.c_void_p(256)
     rc = L.lssab8_prefill(fake, fake, fake, 2, 1, 8, 8, 128, 96, s4, s4, s4, 0, fake, 2, s4, fake, 1 << 30, None)
     assert rc == 2
+    # the key-offset quantiser needs its offset
+    ks = _lib.i64x([2 * 300 * 64, 300 * 64, 64, 1])
+    rc = L.lssab8_quant_keys_offset(fake, 2, 1, 2, 300, 64, ks, 384, None, fake, fake, None)
+    assert rc == 1
     # a chunk must start on a 128-key block boundary, below the sequence length
     for T0, T in ((100, 300), (256, 256), (-128, 300)):
         rc = L.lssab8_prefill_chunk_lattice(fake, fake, fake, fake, fake, fake, None, 1, 8, 8, T0, T, 128, None,
