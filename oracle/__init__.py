@@ -48,7 +48,7 @@ def lib():
         L.or_quant_blocks.restype = ctypes.c_int
         L.or_gbase.argtypes = [ctypes.c_int]
         L.or_gbase.restype = ctypes.c_int64
-        L.or_core.argtypes = [ctypes.c_int] * 4 + [P] * 7 + [ctypes.c_int] * 3 + [P, ctypes.c_int] + [P] * 4 + [ctypes.c_int] * 2
+        L.or_core.argtypes = [ctypes.c_int] * 4 + [P] * 8 + [ctypes.c_int] * 3 + [P, ctypes.c_int] + [P] * 4 + [ctypes.c_int] * 2
         L.or_core.restype = ctypes.c_int
         _lib = L
     return _lib
@@ -114,9 +114,12 @@ def quant_blocks(x, mode=0):
     return x8, e, e0, err
 
 
-def prep(q, k, v, sink=False, mu=None):
+def prep(q, k, v, sink=False, mu=None, v_keyshift=0):
     """PREP of reference/lssab_golden.py:214-235 (+ B9 value grid when sink is on).  mu [KVH, dh]:
-    the key offset, k' = fl32(k - mu) before the key quantiser (reference/lssab_golden.py:221)."""
+    the key offset, k' = fl32(k - mu) before the key quantiser (reference/lssab_golden.py:221).
+    v_keyshift = dmax > 0: B9.3 (reference/lssab9_golden.py:37-70), key j of block b quantised on
+    the grid e_v[b] + d_j, d_j = clamp(e_j - e_v[b], 0, dmax) with e_j the key's own exponent on
+    the B9 value grid; returns d8 [KVH, T] for the PV weight shift."""
     if mu is not None:
         k = (np.asarray(k, np.float32) - np.asarray(mu, np.float32)[:, None, :]).astype(np.float32)
     q8, eq = quant_rows(q)
@@ -127,10 +130,38 @@ def prep(q, k, v, sink=False, mu=None):
         if err:
             raise AssertionError("e_v outside the contract clamp")
         ev0 = ev0 if T > 1 else None
+    elif v_keyshift:
+        v8, ev, _, err = quant_blocks(v, 1)             # the B9 value grid, sink off
+        if err:
+            raise AssertionError("e_v outside the contract clamp")
+        ev0 = None
     else:
         v8, ev, _, _ = quant_blocks(v, 0)
         ev0 = None
-    return dict(q8=q8, eq=eq, k8=k8, ek=ek, v8=v8, ev=ev, ev0=ev0)
+    d8 = None
+    if v_keyshift:
+        v8, d8 = _keyshift(v, ev, ev0, int(v_keyshift))
+    return dict(q8=q8, eq=eq, k8=k8, ek=ek, v8=v8, ev=ev, ev0=ev0, d8=d8)
+
+
+def _keyshift(v, ev, ev0, dmax):
+    """B9.3 values and shifts (reference/lssab9_golden.py:59-69): each key's own exponent is the B9
+    value-grid exponent of that key alone (a one-key block); v8 = clamp(rint(v 2^(e_v + d)), +-127)."""
+    v = np.ascontiguousarray(v, np.float32)
+    KVH, T, dh = v.shape
+    ekey = np.zeros((KVH, T), np.int64)
+    for g in range(KVH):
+        for j in range(T):
+            _, e1, _, _ = quant_blocks(v[g:g + 1, j:j + 1], 1)
+            ekey[g, j] = e1[0, 0]
+    ev_tok = np.repeat(np.asarray(ev, np.int64), KB, axis=1)[:, :T]
+    if ev0 is not None:
+        ev_tok = ev_tok.copy()
+        ev_tok[:, 0] = np.asarray(ev0, np.int64)
+    d8 = np.clip(ekey - ev_tok, 0, dmax).astype(np.int64)
+    sc = np.ldexp(np.float32(1.0), (ev_tok + d8).astype(np.int32)).astype(np.float32)
+    v8 = np.clip(np.rint(v * sc[..., None]), -127.0, 127.0).astype(np.int8)
+    return v8, d8.astype(np.int8)
 
 
 def core(p, causal=True, rows=None, key_lo=0, key_hi=None, debug=False, nthreads=None, qrow=-1):
@@ -148,6 +179,8 @@ def core(p, causal=True, rows=None, key_lo=0, key_hi=None, debug=False, nthreads
     ev = np.ascontiguousarray(p["ev"], np.int32)
     ev0 = p.get("ev0")
     ev0 = None if ev0 is None else np.ascontiguousarray(ev0, np.int32)
+    d8 = p.get("d8")
+    d8 = None if d8 is None else np.ascontiguousarray(d8, np.int8)
     nq = 1 if qrow >= 0 else T
     out = np.zeros((H, nq, dh), np.float32)
     dO = np.zeros((H, nq, dh), np.float32) if debug else None
@@ -156,7 +189,7 @@ def core(p, causal=True, rows=None, key_lo=0, key_hi=None, debug=False, nthreads
     r = None if rows is None else np.ascontiguousarray(rows, np.int32)
     nt = nthreads or nthreads_default()
     rc = lib().or_core(H, KVH, T, dh, _p(q8), _p(eq), _p(k8), _p(ek), _p(v8), _p(ev),
-                       None if ev0 is None else _p(ev0), int(causal), int(key_lo),
+                       None if ev0 is None else _p(ev0), None if d8 is None else _p(d8), int(causal), int(key_lo),
                        int(T if key_hi is None else key_hi),
                        None if r is None else _p(r), 0 if r is None else len(r), _p(out),
                        None if dO is None else _p(dO), None if dl is None else _p(dl),
@@ -168,10 +201,11 @@ def core(p, causal=True, rows=None, key_lo=0, key_hi=None, debug=False, nthreads
     return out
 
 
-def attention(q, k, v, sink=False, causal=True, rows=None, nthreads=None, mu=None):
+def attention(q, k, v, sink=False, causal=True, rows=None, nthreads=None, mu=None, v_keyshift=0):
     """lssab8_attention / lssab9_attention(sink_alone) (reference/lssab8_golden.py:341,
     reference/lssab9_golden.py:254): q [H,T,dh], k/v [KVH,T,dh] -> f32 [H,T,dh]."""
-    p = prep(np.asarray(q, np.float32), np.asarray(k, np.float32), np.asarray(v, np.float32), sink, mu=mu)
+    p = prep(np.asarray(q, np.float32), np.asarray(k, np.float32), np.asarray(v, np.float32), sink, mu=mu,
+             v_keyshift=v_keyshift)
     return core(p, causal=causal, rows=rows, nthreads=nthreads)
 
 

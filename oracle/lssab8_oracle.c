@@ -189,6 +189,8 @@ int64_t or_floor_shift(int64_t x, int s) { return x >> s; }   /* arithmetic: flo
  *   k8, v8 [KVH, T, dh], ek, ev [KVH, nblk] (block lattice; NOTE: kv-head major, the
  *                                           golden's [nblk, KVH] transposed)
  *   ev0 [KVH] or NULL                      (B9.1 sink exponent; NULL = sink off)
+ *   d8 [KVH, T] or NULL                    (B9.3 per-key shift d_j of the PV weight,
+ *                                           reference/lssab9_golden.py:37-41, 179-186)
  *   rows: the query rows to evaluate (NULL = all T rows); the key set of row i is
  *         { j : j <= i } when causal, { j : j < T } otherwise, further restricted to
  *         [key_lo, key_hi) (the split-KV segment restriction of lssab8_row_segments,
@@ -206,6 +208,7 @@ typedef struct {
     const int8_t* k8; const int32_t* ek;
     const int8_t* v8; const int32_t* ev;
     const int32_t* ev0;
+    const int8_t* d8;    /* B9.3 per-key weight shift [KVH, T] (NULL: none) */
     int causal;
     int key_lo, key_hi;
     int qrow;            /* >= 0: q8/eq hold ONE row per head, standing for query row qrow */
@@ -281,10 +284,13 @@ static void or_row(const or_problem* P, int h, int i, float* out_row, float* dO,
             int sink = (P->ev0 != NULL) && (b == 0) && (lo == 0) && (T > 1);
             for (int c = 0; c < dh; ++c) { A0[c] = 0; A1[c] = 0; }
             for (int t = 0; t < n; ++t) {
-                if (eh[t] == 0) continue;
+                /* B9.3: the PV weight is eh >> d_j, l_b keeps the unshifted weight
+                 * (reference/lssab9_golden.py:179-186, default truncating shift) */
+                const int32_t w = P->d8 ? (eh[t] >> P->d8[(int64_t)g * T + lo + t]) : eh[t];
+                if (w == 0) continue;
                 const int8_t* vr = vg + (int64_t)(lo + t) * dh;
                 int32_t* A = (sink && t == 0) ? A0 : A1;
-                for (int c = 0; c < dh; ++c) A[c] += eh[t] * (int32_t)vr[c];
+                for (int c = 0; c < dh; ++c) A[c] += w * (int32_t)vr[c];
             }
             int nz = (lb != 0);
             for (int c = 0; c < dh && !nz; ++c) nz = (A0[c] != 0) || (A1[c] != 0);
@@ -327,7 +333,7 @@ static void or_row(const or_problem* P, int h, int i, float* out_row, float* dO,
 /* Evaluate rows (all rows when rows == NULL) of every head.  Threads over (head, row). */
 int or_core(int H, int KVH, int T, int dh,
             const int8_t* q8, const int32_t* eq, const int8_t* k8, const int32_t* ek,
-            const int8_t* v8, const int32_t* ev, const int32_t* ev0,
+            const int8_t* v8, const int32_t* ev, const int32_t* ev0, const int8_t* d8,
             int causal, int key_lo, int key_hi,
             const int32_t* rows, int nrows,
             float* out, float* dbg_O, float* dbg_l, int64_t* dbg_nb, int nthreads, int qrow) {
@@ -337,7 +343,7 @@ int or_core(int H, int KVH, int T, int dh,
     if (rows && qrow < 0) {
         for (int r = 0; r < nrows; ++r) if (rows[r] < 0 || rows[r] >= T) return -1;
     }
-    or_problem P = { H, KVH, T, dh, q8, eq, k8, ek, v8, ev, ev0, causal, key_lo, key_hi, qrow };
+    or_problem P = { H, KVH, T, dh, q8, eq, k8, ek, v8, ev, ev0, d8, causal, key_lo, key_hi, qrow };
     int nr = (qrow >= 0) ? 1 : (rows ? nrows : T);
     int64_t total = (int64_t)H * nr;
 #pragma omp parallel num_threads(nthreads > 0 ? nthreads : 1)

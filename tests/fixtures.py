@@ -157,3 +157,18 @@ def mu_cases():
         mu = (off + g.standard_normal((KVH, dh)).astype(np.float32) * np.float32(0.1)).astype(np.float32)
         out.append(dict(tag=tag, q=q, k=k, v=v, mu=mu))
     return out
+
+
+def keyshift_cases():
+    """Inputs for B9.3 v_keyshift: value rows whose magnitudes differ by up to 2^6 inside a block,
+    so the per-key shift d_j = clamp(e_j - e_v, 0, dmax) takes several values."""
+    out = []
+    for tag, seed, H, KVH, T, dh, dmax in (("ks_h4kv2_t300_d64_k3", 31, 4, 2, 300, 64, 3),
+                                           ("ks_h2kv1_t200_d128_k6", 32, 2, 1, 200, 128, 6)):
+        g = np.random.RandomState(seed)
+        q = g.standard_normal((H, T, dh)).astype(np.float32)
+        k = g.standard_normal((KVH, T, dh)).astype(np.float32)
+        scale = np.exp2(-g.randint(0, 7, size=(KVH, T, 1))).astype(np.float32)
+        v = (g.standard_normal((KVH, T, dh)).astype(np.float32) * scale).astype(np.float32)
+        out.append(dict(tag=tag, q=q, k=k, v=v, dmax=dmax))
+    return out

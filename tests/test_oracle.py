@@ -122,3 +122,18 @@ def test_oracle_key_offset_equals_reference_golden(case):
     assert GD.sha(GD.f32bits(O.attention(q, k, v, mu=mu))) == rec["b8_mu"]
     assert GD.sha(GD.f32bits(O.attention(q, k, v, sink=True, mu=mu))) == rec["b9sink_mu"]
     assert GD.sha(GD.f32bits(O.attention(q, k, v))) == rec["b8_no_mu"]
+
+
+@pytest.mark.parametrize("case", FX.keyshift_cases(), ids=[c["tag"] for c in FX.keyshift_cases()])
+def test_oracle_value_keyshift_equals_reference_golden(case):
+    import json
+    import os
+    with open(os.path.join(GD.GOLDEN_DIR, "golden_keyshift.json")) as f:
+        rec = json.load(f)[case["tag"]]
+    q, k, v, dmax = case["q"], case["k"], case["v"], case["dmax"]
+    assert GD.sha(np.concatenate([q.ravel(), k.ravel(), v.ravel()])) == rec["inputs"]
+    for sink, name in ((False, "nosink"), (True, "sink")):
+        p = O.prep(q, k, v, sink=sink, v_keyshift=dmax)
+        assert GD.sha(np.asarray(p["d8"], np.int8)) == rec["d8_" + name]
+        assert int(p["d8"].max()) == rec["d8_max_" + name] > 0
+        assert GD.sha(GD.f32bits(O.attention(q, k, v, sink=sink, v_keyshift=dmax))) == rec["out_" + name]
