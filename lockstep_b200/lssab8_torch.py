@@ -37,27 +37,30 @@ def _contract_check(kb, bhi, n, w_loc, weight, s_win, seg_keys, mu, qexp, clamp_
         raise NotImplementedError("only the LSSA-B8 contract arm (L8 = L8-RN-W9) has a B200 kernel")
 
 
-def _mu_for(mu, module, device):
-    """The layer's key offset [KVH, dh] as float32 on `device` (cached per layer and device), or None."""
+def _mu_for(mu, module, device, cache=None):
+    """The layer's key offset mu[layer_idx] [KVH, dh] as float32 on `device`, or None.  `cache`
+    (one dict per attention closure, as in reference/lssab8_torch.py:116-122) keeps the copies."""
     if mu is None:
         return None
     import torch
     li = int(getattr(module, "layer_idx", -1))
-    cache = _MU_CACHE.setdefault(id(mu), {})
     key = (li, str(device))
-    if key not in cache:
-        cache[key] = torch.as_tensor(mu[li]).to(device=device, dtype=torch.float32).contiguous()
-    return cache[key]
-
-
-_MU_CACHE = {}
+    if cache is not None and key in cache:
+        return cache[key]
+    t = torch.as_tensor(mu[li]).to(device=device, dtype=torch.float32).contiguous()
+    if cache is not None:
+        cache[key] = t
+    return t
 
 
 def _attn_closure(sink, mu=None):
+    mu_cache = {}
+
     def attn(module, query, key, value, attention_mask, *args, **kw):
         Bsz, H, T, dh = query.shape
         assert Bsz == 1, "B=1 windows only"
-        out = _A.prefill(query, key, value, sink=sink, out_dtype=query.dtype, mu=_mu_for(mu, module, query.device))
+        out = _A.prefill(query, key, value, sink=sink, out_dtype=query.dtype,
+                         mu=_mu_for(mu, module, query.device, mu_cache))
         return out, None
     return attn
 
