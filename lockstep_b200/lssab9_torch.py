@@ -23,11 +23,13 @@ def make_lssab9_long_attn(kb=KB, bhi=BHI, n=NIDX, w_loc=W_LOC, weight="rn", s_wi
     if v_planes != 1 or v_keyshift != 0 or v_sub != 1:
         raise NotImplementedError("B9.2 / B9.3 / B9.4 value options have no B200 kernel")
 
+    mu_cache = {}
+
     def attn(module, query, key, value, attention_mask, *args, **kw):
         Bsz, H, T, dh = query.shape
         assert Bsz == 1, "B=1 windows only"
         # B9's value grid is used even with the sink off (clamp 48, assert 40)
-        mu_l = B8._mu_for(mu, module, query.device)
+        mu_l = B8._mu_for(mu, module, query.device, mu_cache)
         out = _A.prefill(query, key, value, sink=True, out_dtype=query.dtype, mu=mu_l) if sink_alone else \
             _prefill_b9_value_grid(query, key, value, mu_l)
         return out, None
