@@ -137,3 +137,24 @@ def test_oracle_value_keyshift_equals_reference_golden(case):
         assert GD.sha(np.asarray(p["d8"], np.int8)) == rec["d8_" + name]
         assert int(p["d8"].max()) == rec["d8_max_" + name] > 0
         assert GD.sha(GD.f32bits(O.attention(q, k, v, sink=sink, v_keyshift=dmax))) == rec["out_" + name]
+
+
+def test_oracle_aligned_chunk_invariance():
+    """The property chunked prefill rests on (reference/lssab8_selftest.py:292-317): the prefill of a
+    128-aligned prefix equals the prefix of the whole prefill bit for bit, while a non-aligned cut
+    may differ (its last block is quantised over fewer rows)."""
+    T = 640
+    g = np.random.RandomState(11)
+    q = g.standard_normal((2, T, 128)).astype(np.float32)
+    k = g.standard_normal((1, T, 128)).astype(np.float32)
+    v = g.standard_normal((1, T, 128)).astype(np.float32)
+    full = O.attention(q, k, v)
+    for cut in (128, 256, 384, 512):
+        part = O.attention(q[:, :cut], k[:, :cut], v[:, :cut])
+        assert np.array_equal(part.view(np.uint32), full[:, :cut].view(np.uint32)), cut
+    k2, v2 = k.copy(), v.copy()
+    k2[:, 505] *= np.float32(64.0)
+    v2[:, 505] *= np.float32(64.0)
+    full2 = O.attention(q, k2, v2)
+    part2 = O.attention(q[:, :500], k2[:, :500], v2[:, :500])
+    assert not np.array_equal(part2.view(np.uint32), full2[:, :500].view(np.uint32))
