@@ -139,9 +139,11 @@ int lssab8_decode_prep_kv(const void* k, const void* v, int dtype, int B, int KV
 size_t lssab8_decode_workspace_size(int B, int H, int KVH, int dh, int max_blocks);
 
 /* Split-KV decode: one new query row per sequence, q [B, H, dh] (strides qs[0..2]), attending to
- * all seq_lens[b] keys of the lattice (the new token's own key is the last one).  Each split of
- * split_blocks 128-key blocks emits exact block partials; the last split to finish refolds
- * them in ascending order (reference/lssab8_golden.py:350-394).  Equals row L-1 of the prefill
+ * all seq_lens[b] keys of the lattice (the new token's own key is the last one).  Every
+ * 128-key block yields exact block partials in the workspace, and a refold folds them in
+ * ascending order (reference/lssab8_golden.py:350-394): at dh 128 a separate refold kernel runs
+ * after the streaming kernel; at dh 64 the last split of each (sequence, kv head) to finish does
+ * it.  split_blocks (blocks per split) changes no bit.  Equals row L-1 of the prefill
  * bit for bit (reference/lssab8_selftest.py:320-336).  out[b, h, c] at out + b*os[0] + h*os[1]
  * + c*os[2].  H/KVH <= 8, dh in {64, 128}. */
 int lssab8_decode(const void* q, int dtype, const int64_t* qs, int B, int H, int KVH, int dh, const int32_t* seq_lens,
@@ -157,8 +159,10 @@ int lssab8_decode(const void* q, int dtype, const int64_t* qs, int B, int H, int
  * lssab8_decode minus the workspace and uses a fixed scratch buffer of
  * LSSAB8_NOALLOC_SCRATCH_BYTES that the library holds in device memory on every GPU it is loaded
  * on, until the process exits.  It allocates nothing.
- *   - The problem's scratch need is lssab8_decode_workspace_size(B, H, KVH, dh, max_blocks); if it
- *     exceeds the buffer the call returns LSSAB8_ESCRATCH and launches nothing.
+ *   - The call is refused with LSSAB8_ESCRATCH, launching nothing, exactly when
+ *     lssab8_decode_workspace_size(B, H, KVH, dh, max_blocks) - 256 > LSSAB8_NOALLOC_SCRATCH_BYTES
+ *     (the workspace size includes 256 bytes of alignment slack, which the 256-aligned buffer
+ *     does not need).
  *   - The first call on a device looks up the buffer's device address for that device (with
  *     that device current); make that first call before any stream capture.
  *   - Every call on a device shares the one buffer: calls that can overlap on the GPU (other
@@ -171,6 +175,17 @@ int lssab8_decode_noalloc(const void* q, int dtype, const int64_t* qs, int B, in
                           const int64_t* os, void* stream);
 
 /* ------------------------------------------------------------------------- self-test */
+
+/* Test support, no counterpart in the reference: the failure path of the bounded waits.  Runs
+ * lssab8_prefill_lattice (sink off, float32 out, T <= 4096) with the TMA producer withholding key
+ * block `withhold_block` of its first work item -- the pipeline barrier expects the block's bytes,
+ * which never arrive -- and every wait limited to wait_us microseconds (1 .. 2,000,000) instead of
+ * the usual ~2 s.  The kernel gives up, sets LSSAB8_DEV_TIMEOUT in the device error word, releases
+ * its tensor memory and returns; the call returns LSSAB8_OK if the launch succeeded.  The next
+ * call on the same context runs normally. */
+int lssab8_selftest_timeout(const int8_t* q8, const int32_t* eq, const int8_t* k8, const int32_t* ek,
+                            const int8_t* v8, const int32_t* ev, int B, int H, int KVH, int T, int dh,
+                            int withhold_block, int wait_us, void* out, const int64_t* os, void* stream);
 
 /* Test support, no counterpart in the reference: out[i] = the prefill epilogue's division of
  * y[i] by l[i] (l[i] != 0), i.e. the correctly rounded binary32 quotient the contract's

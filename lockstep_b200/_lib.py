@@ -18,7 +18,7 @@ SYMBOLS = (
     "lssab8_quant_rows", "lssab8_quant_blocks", "lssab8_quant_keys_offset",
     "lssab8_prefill_lattice", "lssab8_prefill_chunk_lattice", "lssab8_prefill_workspace_size", "lssab8_prefill",
     "lssab8_decode_prep_kv", "lssab8_decode_workspace_size", "lssab8_decode",
-    "lssab8_decode_noalloc", "lssab8_selftest_div", "lssab8_selftest_rescale",
+    "lssab8_decode_noalloc", "lssab8_selftest_div", "lssab8_selftest_rescale", "lssab8_selftest_timeout",
 )
 
 _lib = None
@@ -59,6 +59,7 @@ def load():
     L.lssab8_decode_noalloc.argtypes = [P, I, PI64, I, I, I, I, P, P, I, I, P, P, P, P, P, I, I, I, P, I, PI64, P]
     L.lssab8_selftest_div.argtypes = [P, P, I64, P, P]
     L.lssab8_selftest_rescale.argtypes = [P, P, I64, P, P]
+    L.lssab8_selftest_timeout.argtypes = [P] * 6 + [I] * 7 + [P, PI64, P]
     for name in SYMBOLS:
         getattr(L, name).restype = getattr(L, name).restype or I
     _lib = L

@@ -362,7 +362,8 @@ __global__ void selftest_rescale_kernel(const float* x, const int* D, long long 
 // (Tpad = tpad(T)), out the chunk's T - T0 rows.  T0 = 0 is the whole prefill.
 static int prefill_lattice_impl(const int8_t* q8, const int32_t* eq, const int8_t* k8, const int32_t* ek, const int8_t* v8,
                          const int32_t* ev, const int32_t* ev0, int B, int H, int KVH, int T0, int T, int dh,
-                         float* orow_scratch, void* out, int out_dtype, const int64_t* os, void* stream) {
+                         float* orow_scratch, void* out, int out_dtype, const int64_t* os, void* stream,
+                         uint64_t wait_ns = kWaitLimitNs, int withhold = -1) {
   if (!q8 || !eq || !k8 || !ek || !v8 || !ev || !out || !shape_ok(B, H, KVH, T, dh) || !strides_ok(os, 4))
     return kErrArg;
   if (dh != 64 && dh != 128) return kErrUnsupported;
@@ -386,6 +387,8 @@ static int prefill_lattice_impl(const int8_t* q8, const int32_t* eq, const int8_
   a.mul_b2 = 1u << 16;
   a.mul_b3 = 1u << 24;
   a.err = ds->err;
+  a.wait_ns = wait_ns;
+  a.withhold = withhold;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool sink = ev0 != nullptr;
   if (dh == 128) return sink ? launch_prefill_out<128, true>(out_dtype, tq, tk, tv, a, ds->num_sms, st)
@@ -693,9 +696,10 @@ int lssab8_decode_noalloc(const void* q, int dtype, const int64_t* qs, int B, in
   int32_t* eq = reinterpret_cast<int32_t*>(base + w.eq);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int64_t q4[4] = {qs[0], qs[1], 0, qs[2]};
-  if ((rc = lssab8_quant_rows(q, dtype, B, H, 1, dh, q4, 1, q8, eq, stream))) return rc;
-  // the tickets must start at zero; the buffer keeps whatever the previous call left
+  // the tickets must start at zero (the buffer keeps whatever the previous call left); the reset
+  // comes first, as in lssab8_decode, so the query quantiser directly precedes the decode kernel
   if (cudaMemsetAsync(base + w.tickets, 0, (size_t)B * KVH * 4, s) != cudaSuccess) return kErrCuda;
+  if ((rc = lssab8_quant_rows(q, dtype, B, H, 1, dh, q4, 1, q8, eq, stream))) return rc;
   DecodeArgs a{};
   a.B = B; a.H = H; a.KVH = KVH; a.dh = dh; a.group = H / KVH; a.max_blocks = max_blocks; a.max_pages = max_pages;
   a.split_blocks = split_blocks; a.num_pages = num_pages; a.seq_lens = seq_lens; a.block_table = block_table;
@@ -711,6 +715,15 @@ int lssab8_decode_noalloc(const void* q, int dtype, const int64_t* qs, int B, in
                              : launch_decode_tc_out<false>(out_dtype, a, max_splits, ds->num_sms, s);
   return sink ? launch_decode_out<64, true>(out_dtype, a, max_splits, s)
               : launch_decode_out<64, false>(out_dtype, a, max_splits, s);
+}
+
+int lssab8_selftest_timeout(const int8_t* q8, const int32_t* eq, const int8_t* k8, const int32_t* ek,
+                            const int8_t* v8, const int32_t* ev, int B, int H, int KVH, int T, int dh,
+                            int withhold_block, int wait_us, void* out, const int64_t* os, void* stream) {
+  if (withhold_block < 0 || wait_us <= 0 || wait_us > 2000000) return kErrArg;
+  if (tpad_of(T) / 128 > kSEG) return kErrArg;                 // single-segment rows: no row scratch
+  return prefill_lattice_impl(q8, eq, k8, ek, v8, ev, nullptr, B, H, KVH, 0, T, dh, nullptr, out, kF32, os, stream,
+                              (uint64_t)wait_us * 1000ull, withhold_block);
 }
 
 int lssab8_selftest_div(const float* y, const float* l, long long n, float* out, void* stream) {

@@ -221,13 +221,17 @@ __device__ __forceinline__ bool mbar_try_suspend(uint64_t* bar, uint32_t parity)
   return ok != 0;
 }
 
-// Bounded wait on an mbarrier phase.  Gives up after ~2 s of wall time or as soon as another
+// The wall-time limit of every bounded wait (ns).  A kernel may pass a shorter one (the timeout
+// self-test does); nothing in a healthy pipeline waits longer than microseconds.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+
+// Bounded wait on an mbarrier phase.  Gives up after limit_ns of wall time or as soon as another
 // role of the CTA has raised *abort; on giving up it records kDevTimeout in *err and returns
 // false so the caller can unwind without hanging the GPU.
 // sleep_ns > 0 parks the thread between polls: roles that are not on the critical path (the
 // fold warps, the MMA and TMA threads) must not steal issue slots from the warps that are.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int* err,
-                                          uint32_t sleep_ns = 0) {
+                                          uint32_t sleep_ns = 0, uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try(bar, parity)) return true;
   uint64_t t0 = globaltimer();
   for (uint32_t it = 0;; ++it) {
@@ -241,7 +245,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     }
     if ((it & 15u) == 15u) {
       if (*abort) return false;
-      if (globaltimer() - t0 > 2000000000ull) {
+      if (globaltimer() - t0 > limit_ns) {
         *abort = 1;
         if (err) atomicOr(err, kDevTimeout);
         return false;
@@ -253,14 +257,15 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 
 // Non-blocking poll of an mbarrier phase (no hardware suspension: arrivals made by
 // tcgen05.commit are observed as soon as they land).  Same bounds as mbar_wait.
-__device__ __forceinline__ bool mbar_poll(uint64_t* bar, uint32_t parity, volatile int* abort, int* err) {
+__device__ __forceinline__ bool mbar_poll(uint64_t* bar, uint32_t parity, volatile int* abort, int* err,
+                                          uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_test(bar, parity)) return true;
   uint64_t t0 = globaltimer();
   for (uint32_t it = 0;; ++it) {
     if (mbar_test(bar, parity)) return true;
     if ((it & 1023u) == 1023u) {
       if (*abort) return false;
-      if (globaltimer() - t0 > 2000000000ull) {
+      if (globaltimer() - t0 > limit_ns) {
         *abort = 1;
         if (err) atomicOr(err, kDevTimeout);
         return false;
@@ -297,11 +302,12 @@ __device__ __forceinline__ bool group_wait(uint64_t* bar, uint32_t parity, bool 
 // the verdict is broadcast, and on success every lane observes the completed phase itself (it
 // cannot advance again before this warp arrives on the matching release barrier), which gives
 // each lane the acquire ordering.  Every lane returns the same value.
-__device__ __forceinline__ bool warp_poll(uint64_t* bar, uint32_t parity, volatile int* abort, int* err) {
+__device__ __forceinline__ bool warp_poll(uint64_t* bar, uint32_t parity, volatile int* abort, int* err,
+                                          uint64_t limit_ns = kWaitLimitNs) {
   // common case: the phase is already complete and every lane's own test says so (one test)
   if (__all_sync(0xffffffffu, mbar_test(bar, parity))) return true;
   int ok = 0;
-  if ((threadIdx.x & 31) == 0) ok = mbar_poll(bar, parity, abort, err) ? 1 : 0;
+  if ((threadIdx.x & 31) == 0) ok = mbar_poll(bar, parity, abort, err, limit_ns) ? 1 : 0;
   ok = __shfl_sync(0xffffffffu, ok, 0);
   if (ok) (void)mbar_test(bar, parity);
   return ok != 0;

@@ -66,6 +66,8 @@ struct PrefillArgs {
   // byte permutes on the ALU pipe, which the chain saturates.
   uint32_t mul_entry, mul_b1, mul_b2, mul_b3;
   int* err;
+  uint64_t wait_ns;     // limit of every bounded wait (kWaitLimitNs; shorter only in the timeout self-test)
+  int withhold;         // self-test only: the TMA producer never loads this key block of its first item (-1: none)
 };
 
 // ------------------------------------------------------------------------ smem layout
@@ -270,17 +272,19 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
         const int krow0 = (it.b * p.KVH + g) * (p.nblk * 128);
         const int qb = tt & 1;
         // buffer qb is free once item tt - 2's last QK has finished and its workers are done
-        if (!mbar_wait(&bars[kBarQEmpty + qb], ((tt >> 1) & 1) ^ 1, abort_flag, p.err, 128)) { ok = false; break; }
+        if (!mbar_wait(&bars[kBarQEmpty + qb], ((tt >> 1) & 1) ^ 1, abort_flag, p.err, 128, p.wait_ns)) { ok = false; break; }
         mbar_expect_tx(&bars[kBarQFull + qb], L::kTile + (SINK ? DH : 0));
         tma_load_2d(smem + L::kQ + qb * L::kTile, &tm_q, 0, qrow0, &bars[kBarQFull + qb]);
         if (SINK) bulk_g2s(v0row + qb * 128, p.v8 + (long long)krow0 * DH, DH, &bars[kBarQFull + qb]);
         for (int j = 0; j <= it.kt; ++j, ++jj) {
           const int s = jj & 1;
           const uint32_t ph = (jj >> 1) & 1;
-          if (!mbar_wait(&bars[kBarKEmpty + s], ph ^ 1, abort_flag, p.err, 128)) { ok = false; break; }
+          if (!mbar_wait(&bars[kBarKEmpty + s], ph ^ 1, abort_flag, p.err, 128, p.wait_ns)) { ok = false; break; }
           mbar_expect_tx(&bars[kBarKFull + s], L::kTile);
-          tma_load_2d(smem + L::kK + s * L::kTile, &tm_k, 0, krow0 + j * 128, &bars[kBarKFull + s]);
-          if (!mbar_wait(&bars[kBarVEmpty + s], ph ^ 1, abort_flag, p.err, 128)) { ok = false; break; }
+          // (the timeout self-test withholds one block: its bytes are expected but never arrive)
+          if (tt != 0 || j != p.withhold)
+            tma_load_2d(smem + L::kK + s * L::kTile, &tm_k, 0, krow0 + j * 128, &bars[kBarKFull + s]);
+          if (!mbar_wait(&bars[kBarVEmpty + s], ph ^ 1, abort_flag, p.err, 128, p.wait_ns)) { ok = false; break; }
           mbar_expect_tx(&bars[kBarVFull + s], L::kTile);
           tma_load_2d(smem + L::kV + s * L::kTile, &tm_v, 0, krow0 + j * 128, &bars[kBarVFull + s]);
         }
@@ -303,10 +307,10 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
       auto issue_qk = [&](int jg, uint32_t sq) -> bool {
         const int s = jg & 1;
         const uint32_t ph = (jg >> 1) & 1;
-        if (!mbar_wait(&bars[kBarKFull + s], ph, abort_flag, p.err)) return false;
+        if (!mbar_wait(&bars[kBarKFull + s], ph, abort_flag, p.err, 0, p.wait_ns)) return false;
         // S is single-buffered: QK(jg) waits until the chain has copied S(jg - 1) into registers
         // (the jg-th phase of S_empty, jg >= 1)
-        if (jg > 0 && !mbar_wait(&bars[kBarSEmpty], (jg - 1) & 1, abort_flag, p.err)) return false;
+        if (jg > 0 && !mbar_wait(&bars[kBarSEmpty], (jg - 1) & 1, abort_flag, p.err, 0, p.wait_ns)) return false;
         tc_fence_after();
         const uint32_t sk = smem_u32(smem + L::kK + s * L::kTile);
 #pragma unroll
@@ -323,7 +327,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
         if (!pf_item(p, ntile, rd, it)) continue;
         const int nb = it.kt + 1;
         const int qb = tt & 1;
-        if (!mbar_wait(&bars[kBarQFull + qb], (tt >> 1) & 1, abort_flag, p.err)) { ok = false; break; }
+        if (!mbar_wait(&bars[kBarQFull + qb], (tt >> 1) & 1, abort_flag, p.err, 0, p.wait_ns)) { ok = false; break; }
         const uint32_t sq = smem_u32(smem + L::kQ + qb * L::kTile);
         ok = issue_qk(jj, sq);
         if (ok && nb == 1) umma_commit(&bars[kBarQEmpty + qb]);   // the item's last QK is issued
@@ -335,9 +339,9 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
           }
           const int s = jg & 1;
           const uint32_t ph = (jg >> 1) & 1;
-          if (!mbar_wait(&bars[kBarPFull + s], ph, abort_flag, p.err)) { ok = false; break; }
-          if (!mbar_wait(&bars[kBarVFull + s], ph, abort_flag, p.err)) { ok = false; break; }
-          if (!mbar_wait(&bars[kBarAEmpty + s], ph ^ 1, abort_flag, p.err)) { ok = false; break; }   // fold of jg - 2 done
+          if (!mbar_wait(&bars[kBarPFull + s], ph, abort_flag, p.err, 0, p.wait_ns)) { ok = false; break; }
+          if (!mbar_wait(&bars[kBarVFull + s], ph, abort_flag, p.err, 0, p.wait_ns)) { ok = false; break; }
+          if (!mbar_wait(&bars[kBarAEmpty + s], ph ^ 1, abort_flag, p.err, 0, p.wait_ns)) { ok = false; break; }   // fold of jg - 2 done
           tc_fence_after();
           const uint32_t sp = smem_u32(smem + L::kP + s * 16384);
           const uint32_t sv = smem_u32(smem + L::kV + s * L::kTile);
@@ -411,9 +415,9 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
         int sg = 0, Dr = 0;
         if (D > 0) { Dr = D; lseg = rescale(lseg, D); nbrun = nbb; }
         else sg = -D;
-        if (!warp_poll(&bars[kBarAFull + sa], (jgf >> 1) & 1, abort_flag, p.err)) return false;
+        if (!warp_poll(&bars[kBarAFull + sa], (jgf >> 1) & 1, abort_flag, p.err, p.wait_ns)) return false;
         // key 0's value row arrives with the item's Q tile
-        if (SINK && jf == 0 && p.T > 1 && !warp_poll(&bars[kBarQFull + qb], (tt >> 1) & 1, abort_flag, p.err)) return false;
+        if (SINK && jf == 0 && p.T > 1 && !warp_poll(&bars[kBarQFull + qb], (tt >> 1) & 1, abort_flag, p.err, p.wait_ns)) return false;
         tc_fence_after();
         // A block beyond the exact-skip window (sg > S_WIN) is folded with scale +0 instead of being
         // skipped: O and l are never -0 (they start at +0, an RN sum that cancels exactly is +0, and
@@ -533,8 +537,8 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
         const int dm = 1 << max(0, 30 - lg);              // dm * G in [2^30, 2^31): >= 9 doublings
         const uint32_t negG = 0u - G;
         // P buffer s is free once PV(j - 2) has finished -- long before S(j) is ready
-        if (!warp_poll(&bars[kBarPEmpty + s], ph ^ 1, abort_flag, p.err)) { ok = false; break; }
-        if (!warp_poll(&bars[kBarSFull], jg & 1, abort_flag, p.err)) { ok = false; break; }
+        if (!warp_poll(&bars[kBarPEmpty + s], ph ^ 1, abort_flag, p.err, p.wait_ns)) { ok = false; break; }
+        if (!warp_poll(&bars[kBarSFull], jg & 1, abort_flag, p.err, p.wait_ns)) { ok = false; break; }
         tc_fence_after();
         const bool diag = (j == kt);                       // key c of the diagonal block visible iff c <= r
         // pass 1: this lane's 64 scores into registers (one TMEM round trip; S is free for the

@@ -1,12 +1,19 @@
 """Multi-GPU partitioning of the LSSA-B8 path (one process per GPU, torch.distributed).
 
 The path shards without any reduction: every output row is an independent recurrence.
-  * prefill: rank r of n owns kv heads [r*KVH/n, (r+1)*KVH/n) and their query heads; it runs
-    the prefill on strided views of its heads (no copies) and the outputs are gathered;
+  * prefill: rank r of n owns kv heads [r*KVH/n, (r+1)*KVH/n) and their query heads; it runs the
+    prefill on its heads and the outputs are all-gathered (prefill_shard_gather);
   * decode: sequences are partitioned longest-first (greedy on KV length) so that ranks carry
     balanced KV bytes; each rank decodes its sequences and the rows are gathered.
 The only collective is the output gather (NCCL over NVLink on GPUs; gloo works for CPU tests).
 Results are bit-identical at every rank count because no arithmetic crosses a rank.
+
+prefill_shard_gather pipelines the gather with the compute: the batch is cut into chunks, and
+while the kernel runs chunk c + 1 on the caller's stream, a second stream all-gathers chunk c's
+head shards and scatters them into the [B, T, H, dh] output.  Inputs may sit in pinned host
+memory (copied chunk by chunk on a third stream under the previous chunk's compute), and a
+pinned host tensor can receive this rank's rows of every gathered chunk on a fourth stream, so
+an end-to-end host -> device -> host call overlaps all four.
 """
 import torch
 import torch.distributed as dist
@@ -32,30 +39,129 @@ def partition_sequences(lengths, world):
     return [sorted(p) for p in parts]
 
 
-def _world():
+def _world(group=None):
     if dist.is_available() and dist.is_initialized():
-        return dist.get_world_size(), dist.get_rank()
+        return dist.get_world_size(group), dist.get_rank(group)
     return 1, 0
 
 
-def prefill_sharded(query, key, value, sink=False, compute=None, group=None):
-    """Prefill of query [B, H, T, dh], key/value [B, KVH, T, dh] (every rank holds the full
-    inputs or at least its heads) sharded by kv-head group; returns the full out [B, T, H, dh]
-    on every rank.  `compute(q, k, v, sink)` -> [B, T, h, dh] defaults to the B200 kernel."""
-    if compute is None:
-        from . import attention as A
-        compute = lambda q, k, v, s: A.prefill(q, k, v, sink=s)
-    world, rank = _world()
+def _kernel_compute(q, k, v, sink, out):
+    from . import attention as A
+    return A.prefill(q, k, v, sink=sink, out=out, check=False)
+
+
+def prefill_shard_gather(q, k, v, H, sink=False, out=None, chunk=1, group=None, compute=None,
+                         host_out=None, host_rows=None):
+    """Sharded causal GQA prefill, gathered: every rank returns the whole out [B, T, H, dh].
+
+    q [B, h, T, dh], k / v [B, kvh, T, dh]: this rank's shard, query heads [r*h, (r+1)*h) and kv
+    heads [r*kvh, (r+1)*kvh) of H = n*h and n*kvh (kv_group_range); on this rank's GPU, or in
+    pinned host memory, in which case each chunk is copied in on its own stream.  chunk: batch
+    elements per pipeline step.  compute(q, k, v, sink, out) -> out [b, T, h, dh] defaults to the
+    B200 kernel (attention.prefill).  host_out [B, T1 - T0, H, dh] (pinned) receives rows
+    host_rows = (T0, T1) of every gathered batch element.  The result's dtype is q's."""
+    world, rank = _world(group)
+    B, h, T, dh = q.shape
+    if H != h * world:
+        raise ValueError("H = %d query heads cannot be %d ranks x %d" % (H, world, h))
+    compute = compute or _kernel_compute
+    dev = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() and (
+        q.is_cuda or q.is_pinned()) else q.device
+    on_gpu = dev.type == "cuda"
+    if out is None:
+        out = torch.empty((B, T, H, dh), dtype=q.dtype, device=dev)
+    chunks = [(b0, min(b0 + chunk, B)) for b0 in range(0, B, chunk)]
+    T0, T1 = host_rows if host_rows is not None else (0, T)
+
+    if not on_gpu:                                   # CPU ranks (gloo): the same steps, in order
+        for b0, b1 in chunks:
+            loc = compute(q[b0:b1], k[b0:b1], v[b0:b1], sink, None).contiguous()
+            _gather_into(out[b0:b1], loc, world, group)
+            if host_out is not None:
+                host_out[b0:b1].copy_(out[b0:b1, T0:T1])
+        return out
+
+    cur = torch.cuda.current_stream(dev)
+    s_in = torch.cuda.Stream(dev) if not q.is_cuda else None
+    s_comm = torch.cuda.Stream(dev) if world > 1 else None
+    s_out = torch.cuda.Stream(dev) if host_out is not None else None
+    start = torch.cuda.Event()
+    start.record(cur)
+    for s in (s_in, s_comm, s_out):
+        if s is not None:
+            s.wait_event(start)
+    keep = []                                         # buffers used on the side streams
+    loaded = None
+    if s_in is not None:
+        loaded = {}
+
+        def load(c):
+            b0, b1 = chunks[c]
+            with torch.cuda.stream(s_in):
+                t = tuple(x[b0:b1].to(dev, non_blocking=True) for x in (q, k, v))
+                ev = torch.cuda.Event()
+                ev.record(s_in)
+            loaded[c] = (t, ev)
+        load(0)
+    for c, (b0, b1) in enumerate(chunks):
+        if loaded is not None:
+            if c + 1 < len(chunks):
+                load(c + 1)                           # next chunk's copy under this chunk's compute
+            (qc, kc, vc), ev = loaded.pop(c)
+            cur.wait_event(ev)
+            for t in (qc, kc, vc):                    # made on the copy stream, read on this one
+                t.record_stream(cur)
+        else:
+            qc, kc, vc = q[b0:b1], k[b0:b1], v[b0:b1]
+        if world == 1:
+            compute(qc, kc, vc, sink, out[b0:b1])
+            done = out[b0:b1]
+        else:
+            loc = torch.empty((b1 - b0, T, h, dh), dtype=out.dtype, device=dev)
+            compute(qc, kc, vc, sink, loc)
+            ev = torch.cuda.Event()
+            ev.record(cur)
+            s_comm.wait_event(ev)
+            with torch.cuda.stream(s_comm):
+                _gather_into(out[b0:b1], loc, world, group)
+            keep.append(loc)
+            done = out[b0:b1]
+        if s_out is not None:
+            ev = torch.cuda.Event()
+            ev.record(s_comm if s_comm is not None else cur)
+            s_out.wait_event(ev)
+            with torch.cuda.stream(s_out):
+                host_out[b0:b1].copy_(done[:, T0:T1], non_blocking=True)
+    for s in (s_comm, s_out):                         # the caller's stream sees the whole result
+        if s is not None:
+            cur.wait_stream(s)
+    del keep
+    return out
+
+
+def _gather_into(dst, loc, world, group):
+    """All-gather the head shards loc [b, T, h, dh] of every rank into dst [b, T, world*h, dh]."""
+    if world == 1:
+        dst.copy_(loc)
+        return
+    b, T, h, dh = loc.shape
+    g = torch.empty((world * b, T, h, dh), dtype=loc.dtype, device=loc.device)
+    dist.all_gather_into_tensor(g, loc, group=group)
+    dst.view(b, T, world, h, dh).copy_(g.view(world, b, T, h, dh).permute(1, 2, 0, 3, 4))
+
+
+def prefill_sharded(query, key, value, sink=False, compute=None, group=None, chunk=1):
+    """Prefill of query [B, H, T, dh], key/value [B, KVH, T, dh] held whole by every rank (or at
+    least its heads), sharded by kv-head group; returns the full out [B, T, H, dh] on every rank.
+    `compute(q, k, v, sink)` -> [B, T, h, dh] defaults to the B200 kernel."""
+    world, rank = _world(group)
     B, H, T, dh = query.shape
     KVH = key.shape[1]
     grp = H // KVH
     g0, g1 = kv_group_range(KVH, world, rank)
-    local = compute(query[:, g0 * grp:g1 * grp], key[:, g0:g1], value[:, g0:g1], sink)   # [B, T, h, dh]
-    if world == 1:
-        return local
-    parts = [torch.empty_like(local) for _ in range(world)]
-    dist.all_gather(parts, local.contiguous(), group=group)
-    return torch.cat(parts, dim=2)
+    fn = None if compute is None else (lambda q, k, v, s, out: compute(q, k, v, s))
+    return prefill_shard_gather(query[:, g0 * grp:g1 * grp], key[:, g0:g1], value[:, g0:g1], H, sink=sink,
+                                group=group, compute=fn, chunk=chunk)
 
 
 def decode_sharded(q, lengths, decode_local, group=None):
@@ -63,7 +169,7 @@ def decode_sharded(q, lengths, decode_local, group=None):
 
     q [B, H, dh]; lengths: host sequence of KV lengths; decode_local(indices) -> [len(indices),
     H, dh] computes the rows of those sequences on this rank.  Returns [B, H, dh] everywhere."""
-    world, rank = _world()
+    world, rank = _world(group)
     parts = partition_sequences(lengths, world)
     mine = parts[rank]
     out_local = decode_local(mine) if mine else q.new_empty((0,) + tuple(q.shape[1:]))
@@ -73,8 +179,9 @@ def decode_sharded(q, lengths, decode_local, group=None):
     nmax = max(len(p) for p in parts)
     pad = q.new_zeros((nmax,) + tuple(q.shape[1:]))
     pad[:len(mine)] = out_local
-    gathered = [torch.empty_like(pad) for _ in range(world)]
-    dist.all_gather(gathered, pad, group=group)
+    gathered = torch.empty((world * nmax,) + tuple(pad.shape[1:]), dtype=pad.dtype, device=pad.device)
+    dist.all_gather_into_tensor(gathered, pad, group=group)
+    gathered = gathered.view((world,) + tuple(pad.shape))
     out = q.new_empty(q.shape)
     for r, p in enumerate(parts):
         if p:

@@ -96,3 +96,53 @@ def page_table(lengths, page, seed=0):
         bt[b, :n] = perm[o:o + n]
         o += n
     return bt, total
+
+
+def prefill_inputs_shard(B, H, KVH, T, dh, heads, kv_heads, outliers=0.0, seed=0, pin=False):
+    """The slice [:, h0:h1] of q and [:, g0:g1] of k and v from prefill_inputs, bit for bit, as
+    bfloat16 torch tensors (heads = (h0, h1), kv_heads = (g0, g1)), without holding the whole
+    arrays: the stream is drawn in the same order, one [T, dh] piece at a time (consecutive draws
+    from one Generator continue one stream, so the pieces are the whole array's draws), and
+    only this shard's pieces are kept.  pin: allocate the results in pinned host memory."""
+    import torch
+    h0, h1 = heads
+    g0, g1 = kv_heads
+    rng = np.random.Generator(np.random.PCG64(seed))
+
+    def draw(nh, lo, hi):
+        out = torch.empty((B, hi - lo, T, dh), dtype=torch.bfloat16, pin_memory=pin)
+        for b in range(B):
+            for x in range(nh):
+                piece = rng.standard_normal((T, dh), dtype=np.float32)
+                if lo <= x < hi:
+                    out[b, x - lo] = torch.from_numpy(piece)     # float32 -> bfloat16 is RNE
+        return out
+
+    q = draw(H, h0, h1)
+    k = draw(KVH, g0, g1)
+    v = draw(KVH, g0, g1)
+    if outliers > 0:
+        n = int(np.ceil(outliers * dh))
+        for g in range(KVH):
+            ch = rng.choice(dh, size=n, replace=False)
+            if g0 <= g < g1:
+                k[:, g - g0, :, ch] *= 8.0                        # exact in bf16
+    return q, k, v
+
+
+def ragged_inputs_shard(B, H, KVH, dh, lengths, seqs, seed=0):
+    """ragged_inputs restricted to the sequences `seqs`: returns (q [B, H, dh] float32 of every
+    sequence, {b: (k_b, v_b)} float32 [KVH, L_b, dh] for b in seqs); the other sequences' draws
+    are made and dropped, so the kept values equal ragged_inputs' bit for bit."""
+    want = set(int(b) for b in seqs)
+    rng = np.random.Generator(np.random.PCG64(seed + 1))
+    q = _normal_bf16(rng, (B, H, dh))
+    kv = {}
+    for b in range(B):
+        L = int(lengths[b])
+        if b in want:
+            kv[b] = (_normal_bf16(rng, (KVH, L, dh)), _normal_bf16(rng, (KVH, L, dh)))
+        else:
+            for _ in range(2 * KVH):
+                rng.standard_normal((L, dh), dtype=np.float32)
+    return q, kv

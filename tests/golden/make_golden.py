@@ -2,7 +2,7 @@
 """Generate the golden fixtures in tests/golden/ by running the REFERENCE itself.
 
 Run once in a container where the reference project is importable (its ``reference/``
-directory on ``sys.path``; default location given by $LSSAB8_REFERENCE_DIR):
+directory on ``sys.path``; its location given by $LSSAB8_REFERENCE_DIR, which is required):
 
     PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py
 
@@ -36,7 +36,9 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, REPO)
 sys.path.insert(0, os.path.join(REPO, "tests"))
-REF = os.environ.get("LSSAB8_REFERENCE_DIR", "/root/reference/reference")
+REF = os.environ.get("LSSAB8_REFERENCE_DIR")
+if not REF:
+    sys.exit("set LSSAB8_REFERENCE_DIR to the reference project's reference/ directory")
 sys.path.insert(0, REF)
 for var in ("LSSAB8_SEG", "LSSAB8_RESCALE", "LSSAB_TABLE"):
     assert not os.environ.get(var), "%s changes the reference function; unset it" % var

@@ -1,7 +1,7 @@
 #!/usr/bin/env python3
 """Record the reference's outputs for the B9.3 v_keyshift cases in tests/golden/golden_keyshift.json.
 
-Run where the reference project is importable (its ``reference/`` directory; default location in
+Run where the reference project is importable (its ``reference/`` directory, given by the required
 $LSSAB8_REFERENCE_DIR):
 
     PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden_keyshift.py
@@ -21,7 +21,10 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, os.path.join(REPO, "tests"))
-sys.path.insert(0, os.environ.get("LSSAB8_REFERENCE_DIR", "/root/reference/reference"))
+REF = os.environ.get("LSSAB8_REFERENCE_DIR")
+if not REF:
+    sys.exit("set LSSAB8_REFERENCE_DIR to the reference project's reference/ directory")
+sys.path.insert(0, REF)
 for var in ("LSSAB8_SEG", "LSSAB8_RESCALE", "LSSAB_TABLE"):
     assert not os.environ.get(var), "%s changes the reference function; unset it" % var
 

@@ -34,9 +34,12 @@ def test_cfg3_equals_reference_golden(sink):
 
 @pytest.mark.parametrize("L", [1, 2, 100, 128, 129, 1000, 4096, 4097, 9000])
 @pytest.mark.parametrize("sink", [False, True])
-def test_decode_equals_prefill_last_row_and_oracle(L, sink):
-    rng = np.random.default_rng(L + 17 * sink)
-    H, KVH, dh = 8, 2, 128
+@pytest.mark.parametrize("dh", [128, 64])
+def test_decode_equals_prefill_last_row_and_oracle(L, sink, dh):
+    """dh 128 runs the tensor-core streaming kernel and the refold kernel; dh 64 the dp4a kernel
+    whose last split of each (sequence, kv head) refolds the block partials."""
+    rng = np.random.default_rng(L + 17 * sink + dh)
+    H, KVH = 8, 2
     q = W.bf16_round(rng.standard_normal((1, H, L, dh)).astype(np.float32))
     k = W.bf16_round(rng.standard_normal((1, KVH, L, dh)).astype(np.float32))
     v = W.bf16_round(rng.standard_normal((1, KVH, L, dh)).astype(np.float32))
@@ -49,9 +52,10 @@ def test_decode_equals_prefill_last_row_and_oracle(L, sink):
         assert np.array_equal(GD.bf16_bits_of_torch(pre[0, L - 1]), ref)
 
 
-def test_split_invariance():
+@pytest.mark.parametrize("dh", [128, 64])
+def test_split_invariance(dh):
     rng = np.random.default_rng(3)
-    B, H, KVH, L, dh = 3, 16, 4, 5000, 128
+    B, H, KVH, L = 3, 16, 4, 5000
     q = rng.standard_normal((B, H, dh)).astype(np.float32)
     k = rng.standard_normal((B, KVH, L, dh)).astype(np.float32)
     v = rng.standard_normal((B, KVH, L, dh)).astype(np.float32)
@@ -61,8 +65,9 @@ def test_split_invariance():
         assert np.array_equal(o, outs[0])
 
 
-def test_paged_ragged_sink_against_oracle():
-    B, H, KVH, dh = 6, 32, 4, 128
+@pytest.mark.parametrize("dh", [128, 64])
+def test_paged_ragged_sink_against_oracle(dh):
+    B, H, KVH = 6, 32, 4
     lens = np.array([1, 17, 128, 1500, 4097, 2222], np.int64)
     rng = np.random.default_rng(9)
     q = W.bf16_round(rng.standard_normal((B, H, dh)).astype(np.float32))

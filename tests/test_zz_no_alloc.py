@@ -31,10 +31,13 @@ def _args(q, kv, out):
             _lib.i64x(out.stride())), s
 
 
-def test_noalloc_decode_matches_workspace_decode_twice():
+@pytest.mark.parametrize("dh", [64, 128])
+def test_noalloc_decode_matches_workspace_decode_twice(dh):
+    """dh 128 runs the tensor-core streaming kernel and its refold kernel, dh 64 the dp4a kernel
+    with the last-split ticket merge; both take their partials from the shared buffer."""
     L = _lib.load()
-    torch.manual_seed(0)
-    B, H, KVH, Lmax, dh = 4, 32, 8, 3000, 128
+    torch.manual_seed(dh)
+    B, H, KVH, Lmax = 4, 32, 8, 3000
     k = torch.randn(B, KVH, Lmax, dh, device="cuda").to(torch.bfloat16)
     v = torch.randn(B, KVH, Lmax, dh, device="cuda").to(torch.bfloat16)
     lens = torch.tensor([3000, 1, 129, 2048], dtype=torch.int32, device="cuda")
@@ -57,13 +60,52 @@ def test_noalloc_decode_matches_workspace_decode_twice():
             assert torch.equal(got.view(torch.int16), ref.view(torch.int16)), (sink, call)
 
 
+def _refused(B, H, KVH, dh, max_blocks):
+    """True when the call is refused for its size: such a call launches nothing, so placeholder
+    pointers are safe here (every argument check before the size check passes)."""
+    L = _lib.load()
+    z = torch.zeros(16, dtype=torch.int32, device="cuda")
+    p = z.data_ptr()
+    return L.lssab8_decode_noalloc(p, 2, _lib.i64x([H * dh, dh, 1]), B, H, KVH, dh, p, p, 8 * max_blocks, 1, p, p, p,
+                                   p, p, max_blocks, 4, 0, p, 2, _lib.i64x([H * dh, dh, 1]), None) == ESCRATCH
+
+
+def test_noalloc_scratch_limit_is_exact():
+    """The refusal rule is workspace_size - 256 > LSSAB8_NOALLOC_SCRATCH_BYTES (the 256 bytes are
+    alignment slack the aligned buffer does not need).  max_blocks sizes the partials, whatever
+    the sequences' lengths, so the largest accepted max_blocks is run on a short real lattice
+    padded out to it (and must equal lssab8_decode), and the next one must be refused."""
+    L = _lib.load()
+    B, H, KVH, dh, Lmax = 16, 32, 8, 128, 300
+    need = lambda mb: L.lssab8_decode_workspace_size(B, H, KVH, dh, mb) - 256
+    mb = 1
+    while need(mb + 1) <= SCRATCH_BYTES:
+        mb += 1
+    assert need(mb) <= SCRATCH_BYTES < need(mb + 1)
+    assert _refused(B, H, KVH, dh, mb + 1)
+
+    torch.manual_seed(5)
+    k = torch.randn(B, KVH, Lmax, dh, device="cuda").to(torch.bfloat16)
+    v = torch.randn(B, KVH, Lmax, dh, device="cuda").to(torch.bfloat16)
+    lens = torch.randint(1, Lmax + 1, (B,), dtype=torch.int32, device="cuda")
+    bt, npages = D.identity_pages(B, Lmax, k.device)
+    kv = D.build_paged_kv(k, v, lens, bt, npages, sink=True)
+    pad = lambda x, n: torch.cat([x, x.new_zeros(x.shape[:-1] + (n - x.shape[-1],))], dim=-1).contiguous()
+    kv = D.PagedKV(k8p=kv.k8p, v8p=kv.v8p, ek=pad(kv.ek, mb), ev=pad(kv.ev, mb), ev0=kv.ev0,
+                   block_table=pad(kv.block_table, 8 * mb), seq_lens=lens, max_blocks=mb, num_pages=npages, sink=True)
+    q = torch.randn(B, H, dh, device="cuda").to(torch.bfloat16)
+    ref = D.decode(q, kv)
+    got = torch.full((B, H, dh), float("nan"), dtype=torch.bfloat16, device="cuda")
+    a, st = _args(q, kv, got)
+    _lib.check(L.lssab8_decode_noalloc(*a, st), "lssab8_decode_noalloc at the size limit")
+    torch.cuda.synchronize()
+    assert _lib.device_errors() == 0
+    assert torch.equal(got.view(torch.int16), ref.view(torch.int16))
+
+
 def test_noalloc_refuses_problems_larger_than_its_buffer():
     L = _lib.load()
     B, H, KVH, dh, max_blocks = 64, 64, 8, 128, 1024          # needs ~1 GiB of partials
     assert L.lssab8_decode_workspace_size(B, H, KVH, dh, max_blocks) > SCRATCH_BYTES
-    z = torch.zeros(16, dtype=torch.int32, device="cuda")
-    p = z.data_ptr()
-    rc = L.lssab8_decode_noalloc(p, 2, _lib.i64x([H * dh, dh, 1]), B, H, KVH, dh, p, p, 8 * max_blocks, 1, p, p, p, p,
-                                 p, max_blocks, 4, 0, p, 2, _lib.i64x([H * dh, dh, 1]), None)
-    assert rc == ESCRATCH
-    assert "scratch" in _lib.strerror(rc)
+    assert _refused(B, H, KVH, dh, max_blocks)
+    assert "scratch" in _lib.strerror(ESCRATCH)
