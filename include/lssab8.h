@@ -89,8 +89,8 @@ int lssab8_quant_keys_offset(const void* k, int dtype, int B, int KVH, int T, in
 /* Causal GQA prefill on a prepared lattice (the output of the two quantisers with
  * Tpad = 128*ceil(T/128)).  out[b, t, h, c] at out + b*os[0] + t*os[1] + h*os[2] + c*os[3] in
  * out_dtype.  ev0 = NULL: sink off (B8); non-NULL: B9.1 sink_alone.  dh in {64, 128}.
- * orow_scratch: B*H*Tpad*dh floats of caller memory, needed when Tpad > 4096 (rows spanning more
- * than one 32-block fold segment keep their row accumulator there); may be NULL otherwise.
+ * orow_scratch: unused and may be NULL (rows spanning more than one 32-block fold segment keep
+ * their row accumulator in tensor memory); the parameter stays for ABI stability.
  * The fold of reference/lssab8_torch.py:164-271 / reference/lssab9_torch.py:176-326. */
 int lssab8_prefill_lattice(const int8_t* q8, const int32_t* eq, const int8_t* k8, const int32_t* ek,
                            const int8_t* v8, const int32_t* ev, const int32_t* ev0, int B, int H, int KVH, int T,
@@ -102,8 +102,7 @@ int lssab8_prefill_lattice(const int8_t* q8, const int32_t* eq, const int8_t* k8
  * row as by lssab8_quant_rows ([B, H, Tq, dh] / [B, H, Tq], Tq = 128*ceil((T - T0)/128));
  * k8/v8/ek/ev/ev0 hold the lattice of the whole prefix [0, T) as lssab8_quant_blocks writes it
  * (Tpad = 128*ceil(T/128)), so blocks completed by earlier chunks are reused as they are; out
- * holds the chunk's T - T0 rows (row t of the sequence at t - T0); orow_scratch as in
- * lssab8_prefill_lattice, B*H*Tq*dh floats, needed when T > 4096.  No counterpart entry point in
+ * holds the chunk's T - T0 rows (row t of the sequence at t - T0); orow_scratch unused (NULL).  No counterpart entry point in
  * the reference: its 128-aligned chunk invariance (reference/lssab8_selftest.py:292-317) makes
  * the result bit-identical to rows [T0, T) of the whole prefill of length T. */
 int lssab8_prefill_chunk_lattice(const int8_t* q8, const int32_t* eq, const int8_t* k8, const int32_t* ek,
@@ -177,7 +176,7 @@ int lssab8_decode_noalloc(const void* q, int dtype, const int64_t* qs, int B, in
 /* ------------------------------------------------------------------------- self-test */
 
 /* Test support, no counterpart in the reference: the failure path of the bounded waits.  Runs
- * lssab8_prefill_lattice (sink off, float32 out, T <= 4096) with the TMA producer withholding key
+ * lssab8_prefill_lattice (sink off, float32 out) with the TMA producer withholding key
  * block `withhold_block` of its first work item -- the pipeline barrier expects the block's bytes,
  * which never arrive -- and every wait limited to wait_us microseconds (1 .. 2,000,000) instead of
  * the usual ~2 s.  The kernel gives up, sets LSSAB8_DEV_TIMEOUT in the device error word, releases

@@ -120,13 +120,10 @@ def prefill_lattice(q8, eq, k8, ek, v8, ev, ev0, T, out=None, out_dtype=torch.bf
     KVH = k8.shape[1]
     if out is None:
         out = torch.empty((B, T, H, dh), dtype=out_dtype, device=dev)
-    orow = None
-    if Tp // KB > 32:                       # rows spanning more than one fold segment
-        orow = workspace(dev, B * H * Tp * dh * 4)
     with torch.cuda.device(dev):
         _lib.check(_lib.load().lssab8_prefill_lattice(
             q8.data_ptr(), eq.data_ptr(), k8.data_ptr(), ek.data_ptr(), v8.data_ptr(), ev.data_ptr(),
-            None if ev0 is None else ev0.data_ptr(), B, H, KVH, T, dh, Tp, None if orow is None else orow.data_ptr(),
+            None if ev0 is None else ev0.data_ptr(), B, H, KVH, T, dh, Tp, None,
             out.data_ptr(), dtype_code(out.dtype), _lib.i64x(out.stride()), _stream_handle(dev)),
             "lssab8_prefill_lattice")
     return out
@@ -150,14 +147,11 @@ def prefill_chunk_lattice(q8, eq, k8, ek, v8, ev, ev0, T0, T, out=None, out_dtyp
         raise ValueError("lattice shapes do not match the chunk [%d, %d)" % (T0, T))
     if out is None:
         out = torch.empty((B, T - T0, H, dh), dtype=out_dtype, device=dev)
-    orow = None
-    if tpad(T) // KB > 32:                  # rows spanning more than one fold segment
-        orow = workspace(dev, B * H * Tq * dh * 4)
     with torch.cuda.device(dev):
         _lib.check(_lib.load().lssab8_prefill_chunk_lattice(
             q8.data_ptr(), eq.data_ptr(), k8.data_ptr(), ek.data_ptr(), v8.data_ptr(), ev.data_ptr(),
             None if ev0 is None else ev0.data_ptr(), B, H, KVH, T0, T, dh,
-            None if orow is None else orow.data_ptr(), out.data_ptr(), dtype_code(out.dtype),
+            None, out.data_ptr(), dtype_code(out.dtype),
             _lib.i64x(out.stride()), _stream_handle(dev)),
             "lssab8_prefill_chunk_lattice")
     return out

@@ -196,8 +196,7 @@ template <int DH, bool SINK, typename OutT>
 int launch_prefill_t(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const PrefillArgs& a,
                      int num_sms, cudaStream_t st) {
   using L = PrefillSmem<DH>;
-  const int multi = a.nblk > kSEG;
-  if (multi && !a.orow) return kErrWorkspace;
+  const int multi = a.nblk > kSEG;                         // rows span more than one fold segment
   // the T2 copies, the aligned tiles; at least ~116 KB so only one CTA (and one 512-column TMEM
   // allocation) lands on an SM
   int smem = kTabBytes + 1024 + L::kBytes;
@@ -286,7 +285,7 @@ bool strides_ok(const int64_t* s, int n) {
 }
 
 struct PrefillWs {
-  size_t q8, eq, k8, ek, v8, ev, ev0, orow, total;
+  size_t q8, eq, k8, ek, v8, ev, ev0, total;
 };
 
 PrefillWs prefill_ws(int B, int H, int KVH, int T, int dh) {
@@ -300,8 +299,6 @@ PrefillWs prefill_ws(int B, int H, int KVH, int T, int dh) {
   w.v8 = o; o += align256((size_t)B * KVH * Tpad * dh);
   w.ev = o; o += align256((size_t)B * KVH * nblk * 4);
   w.ev0 = o; o += align256((size_t)B * KVH * 4);
-  w.orow = o;            // rows spanning more than one 32-block segment keep O_row here
-  if (nblk > (size_t)kSEG) o += align256((size_t)B * H * Tpad * dh * 4);
   w.total = o + 256;     // slack for aligning the caller's base
   return w;
 }
@@ -576,9 +573,8 @@ int lssab8_prefill(const void* q, const void* k, const void* v, int dtype, int B
     if ((rc = lssab8_quant_blocks(k, dtype, B, KVH, T, dh, ks, Tpad, 0, k8, ek, nullptr, stream))) return rc;
     if ((rc = lssab8_quant_blocks(v, dtype, B, KVH, T, dh, vs, Tpad, vmode, v8, ev, ev0, stream))) return rc;
   }
-  float* orow = (Tpad / 128 > kSEG) ? reinterpret_cast<float*>(base + w.orow) : nullptr;
   return lssab8_prefill_lattice(q8, eq, k8, ek, v8, ev, (sink && T > 1) ? ev0 : nullptr, B, H, KVH, T, dh, Tpad,
-                                orow, out, out_dtype, os, stream);
+                                nullptr, out, out_dtype, os, stream);
 }
 
 int lssab8_decode_prep_kv(const void* k, const void* v, int dtype, int B, int KVH, int dh, const int32_t* seq_lens,
@@ -721,7 +717,6 @@ int lssab8_selftest_timeout(const int8_t* q8, const int32_t* eq, const int8_t* k
                             const int8_t* v8, const int32_t* ev, int B, int H, int KVH, int T, int dh,
                             int withhold_block, int wait_us, void* out, const int64_t* os, void* stream) {
   if (withhold_block < 0 || wait_us <= 0 || wait_us > 2000000) return kErrArg;
-  if (tpad_of(T) / 128 > kSEG) return kErrArg;                 // single-segment rows: no row scratch
   return prefill_lattice_impl(q8, eq, k8, ek, v8, ev, nullptr, B, H, KVH, 0, T, dh, nullptr, out, kF32, os, stream,
                               (uint64_t)wait_us * 1000ull, withhold_block);
 }

@@ -19,7 +19,11 @@
 //               TMEM columns: S [0, 128) (single: the chain copies a tile into registers
 //               and releases it at once, so QK(j+1) overwrites it while block j's chain
 //               runs), A double-buffered [128, 384) (PV(j+1) overlaps the fold of block j),
-//               O [384, 512).
+//               O [384, 512).  The kernel for rows that span more than one 32-block fold
+//               segment (MULTI) keeps the row accumulator O_row in TMEM instead of A's second
+//               buffer: A single [128, 256), O_row [256, 384), O_seg [384, 512); a single A
+//               suffices because PV(j) is issued as soon as the fold of j - 1 (the same
+//               iteration's second half) has released A, a whole chain before the fold of j.
 //   warps 2-9   row workers, two threads per query row (TMEM lane = row).  Iteration j:
 //               the chain of block j over this thread's 64 keys -- exact block max (the two
 //               halves meet through shared memory at one named barrier per block), G, NB, the
@@ -28,8 +32,8 @@
 //               half-row in the SW128 K-major layout the PV MMA reads -- then the fold of block
 //               j - 1 over this thread's DH/2 channels: the committed-order binary32 fold of
 //               (NB_b, l_b, A_b) into the row's O, which lives in TMEM (paired f32x2
-//               arithmetic), the segment -> row fold at 32-block boundaries (O_row in a
-//               workspace buffer when a row spans > 1 segment), and finally fl(O / l).
+//               arithmetic), the segment -> row fold at 32-block boundaries (TMEM to TMEM), and
+//               finally fl(O / l).
 //               One role per SMSP-resident warp keeps the fold from being starved of issue
 //               slots by separate chain warps, and 10 warps leave 168 registers per thread.
 //
@@ -59,7 +63,7 @@ struct PrefillArgs {
   void* out;            // output, element strides below
   long long os0, os1, os2, os3;   // out[b, t, h, c]
   int out_dtype;
-  float* orow;          // [B, H, Tpad, dh] f32: O_row of rows spanning > 1 segment (else unused)
+  float* orow;          // unused (the row accumulator lives in TMEM); kept for the ABI
   uint32_t gbase;
   // Integer multipliers passed at run time (64, 2^8, 2^16, 2^24): the table address and the P
   // byte packing then compile to integer multiply-adds on the FMA pipe instead of shifts and
@@ -115,7 +119,8 @@ __device__ __forceinline__ bool pf_item(const PrefillArgs& p, int ntile, int rou
   it.h = bh % p.H;
   return true;
 }
-constexpr uint32_t kColS = 0, kColA = 128, kColO = 384;   // TMEM column map (A: two buffers of 128)
+// TMEM column map: S, A (two buffers of 128; one in the MULTI kernel), O_row (MULTI), O (O_seg)
+constexpr uint32_t kColS = 0, kColA = 128, kColOrow = 256, kColO = 384;
 
 // The fold's running-maximum rescale of N channels (binary32 bit patterns) of one row by D > 0
 // (reference/lssab8_golden.py:293-301; D <= 0 leaves them alone).  sD2 = (2^-min(D, 126)) twice.
@@ -339,23 +344,26 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
           }
           const int s = jg & 1;
           const uint32_t ph = (jg >> 1) & 1;
+          const int sa = MULTI ? 0 : s;                             // A buffer and its use parity
+          const uint32_t pha = MULTI ? (uint32_t)(jg & 1) : ph;
           if (!mbar_wait(&bars[kBarPFull + s], ph, abort_flag, p.err, 0, p.wait_ns)) { ok = false; break; }
           if (!mbar_wait(&bars[kBarVFull + s], ph, abort_flag, p.err, 0, p.wait_ns)) { ok = false; break; }
-          if (!mbar_wait(&bars[kBarAEmpty + s], ph ^ 1, abort_flag, p.err, 0, p.wait_ns)) { ok = false; break; }   // fold of jg - 2 done
+          // the fold of the block that last used this A buffer is done (jg - 2; jg - 1 in MULTI)
+          if (!mbar_wait(&bars[kBarAEmpty + sa], pha ^ 1, abort_flag, p.err, 0, p.wait_ns)) { ok = false; break; }
           tc_fence_after();
           const uint32_t sp = smem_u32(smem + L::kP + s * 16384);
           const uint32_t sv = smem_u32(smem + L::kV + s * L::kTile);
 #pragma unroll
-          for (int c8 = 0; c8 < DH / 8; ++c8) tmem_cp_128x256b(tmem + kColA + s * 128 + c8 * 8, desc_bias);
+          for (int c8 = 0; c8 < DH / 8; ++c8) tmem_cp_128x256b(tmem + kColA + sa * 128 + c8 * 8, desc_bias);
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
             // A = P (K-major SW128, 32 keys = 32 bytes per step); B = V (MN-major: 32 keys =
             // 4 groups of 8 rows per step; LBO = MN-atom stride (one atom), SBO = 8-row stride).
             // Every step accumulates: the accumulator starts at the 1.5 * 2^23 bias.
-            umma_i8(tmem + kColA + s * 128, umma_desc(sp + kk * 32, 16, 1024, 2),
+            umma_i8(tmem + kColA + sa * 128, umma_desc(sp + kk * 32, 16, 1024, 2),
                     umma_desc(sv + kk * 32 * DH, L::kTile, kRowGroup, kSwz), idesc_pv, 1u);
           }
-          umma_commit(&bars[kBarAFull + s]);
+          umma_commit(&bars[kBarAFull + sa]);
           umma_commit(&bars[kBarVEmpty + s]);
           umma_commit(&bars[kBarPEmpty + s]);
         }
@@ -381,6 +389,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
     const uint32_t lane4 = (uint32_t)(lane & 15) << 2;
     const uint8_t* tab = reinterpret_cast<const uint8_t*>(s_t2);
     const uint32_t obase = rowt + kColO;
+    const uint32_t orbase = rowt + kColOrow;             // O_row (MULTI)
     const uint64_t negM2 = f2_pack(-12582912.0f, -12582912.0f);
     const uint32_t prow = (uint32_t)((r >> 3) * 1024 + (r & 7) * 128);
     int jj0 = 0, tt = 0;                                 // global index of the item's block 0; item count
@@ -402,20 +411,21 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
       float lseg = 0.0f, lrow = 0.0f;
       int nbrun = 0, nbrow = 0;
       bool have_seg = false, have_row = false;
-      float* orow = MULTI ? p.orow + ((long long)qrow0 + r) * DH + kh * HALF : nullptr;
+      const bool mseg = MULTI && nb > kSEG;              // this item's rows span > 1 segment
 
       // fold of block jf: O = fl(O + f32(A) 2^-(s + e_v)), l = fl(l + l_b 2^-s), with the running
       // maximum rescale first (reference/lssab8_golden.py:293-315); then, at a segment end, the
       // segment -> row fold (reference/lssab8_golden.py:317-331).
       auto fold_block = [&](int jf, int nbb, int lbt, int evj, int eh0v) -> bool {
         const int jgf = jj0 + jf;                          // global block index (pipeline parities)
-        const int sa = jgf & 1;
+        const int sa = MULTI ? 0 : (jgf & 1);
+        const uint32_t pha = MULTI ? (uint32_t)(jgf & 1) : (uint32_t)((jgf >> 1) & 1);
         if (!have_seg) { nbrun = nbb; have_seg = true; }
         const int D = nbb - nbrun;
         int sg = 0, Dr = 0;
         if (D > 0) { Dr = D; lseg = rescale(lseg, D); nbrun = nbb; }
         else sg = -D;
-        if (!warp_poll(&bars[kBarAFull + sa], (jgf >> 1) & 1, abort_flag, p.err, p.wait_ns)) return false;
+        if (!warp_poll(&bars[kBarAFull + sa], pha, abort_flag, p.err, p.wait_ns)) return false;
         // key 0's value row arrives with the item's Q tile
         if (SINK && jf == 0 && p.T > 1 && !warp_poll(&bars[kBarQFull + qb], (tt >> 1) & 1, abort_flag, p.err, p.wait_ns)) return false;
         tc_fence_after();
@@ -489,30 +499,33 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
         tc_fence_before();
         mbar_arrive(&bars[kBarAEmpty + sa]);
         lseg = fold_term(lseg, lbt, add ? pow2f(-sg) : 0.0f);
-        if (MULTI && (((jf + 1) % kSEG == 0) || (jf == nb - 1))) {
-          // segment -> row: the same three rules (reference/lssab8_golden.py:317-331)
+        if (mseg && (((jf + 1) % kSEG == 0) || (jf == nb - 1))) {
+          // segment -> row: the same three rules (reference/lssab8_golden.py:317-331), TMEM to
+          // TMEM; `first` is uniform over the item (every row's segments end at the same block),
+          // D2 and s2 are per row and stay in the arithmetic
           int D2 = 0, s2 = 0;
           const bool first = !have_row;
           if (first) { nbrow = nbrun; have_row = true; }
           else { D2 = nbrun - nbrow; if (D2 > 0) { lrow = rescale(lrow, D2); nbrow = nbrun; } else { s2 = -D2; } }
   #pragma unroll 1
           for (int cc = 0; cc < HALF / 16; ++cc) {
-            uint32_t y[16];
+            uint32_t y[16], x[16];
             tmem_ld16x2<HALF>(obase + cc * 16, y);
+            tmem_ld16x2<HALF>(orbase + cc * 16, x);
             tc_wait_ld();
   #pragma unroll
             for (int c = 0; c < 16; ++c) {
-              float* pr = orow + cc * 16 + c;
               const float seg = __uint_as_float(y[c]);
-              if (first) *pr = rescale(seg, 0);
+              float xr = __uint_as_float(x[c]);
+              if (first) xr = rescale(seg, 0);
               else {
-                float x = *pr;
-                if (D2 > 0) x = rescale(x, D2);
-                if (s2 <= kSWIN) x = __fadd_rn(x, rescale(seg, s2));
-                *pr = x;
+                if (D2 > 0) xr = rescale(xr, D2);
+                if (s2 <= kSWIN) xr = __fadd_rn(xr, rescale(seg, s2));
               }
+              x[c] = __float_as_uint(xr);
             }
-            tmem_fill16x2<HALF>(obase + cc * 16, 0u);
+            tmem_st16x2<HALF>(orbase + cc * 16, x);
+            tmem_fill16x2<HALF>(obase + cc * 16, 0u);      // O_seg starts at +0 for the next segment
           }
           tc_wait_st();
           if (first) lrow = rescale(lseg, 0);
@@ -610,7 +623,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
       // `ok` is warp-uniform (every wait is decided for the whole warp), so the warp-collective
       // TMEM loads run on every lane or on none; rows past T skip only the store.
       if (ok) {
-        if constexpr (!MULTI) lrow = rescale(lseg, 0);   // a single segment: O_row = 0 + rescale(O_seg, 0)
+        if (!mseg) lrow = rescale(lseg, 0);             // a single segment: O_row = 0 + rescale(O_seg, 0)
         const int i = kt * 128 + r;                      // the row's position in the sequence
         const bool live = (i < p.T);
         const bool nz = (lrow != 0.0f);
@@ -621,21 +634,19 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
   #pragma unroll 1
         for (int cc = 0; cc < HALF / 16; ++cc) {
           float q[16];
-          if constexpr (!MULTI) {
-            uint32_t y[16];
-            tmem_ld16x2<HALF>(obase + cc * 16, y);
-            tc_wait_ld();
-            tmem_fill16x2<HALF>(obase + cc * 16, 0u);        // O starts at +0 for the next item
+          uint32_t y[16];
+          tmem_ld16x2<HALF>((mseg ? orbase : obase) + cc * 16, y);
+          tc_wait_ld();
+          if (!mseg) tmem_fill16x2<HALF>(obase + cc * 16, 0u);   // O starts at +0 for the next item
   #pragma unroll
-            for (int c = 0; c < 16; ++c) q[c] = __uint_as_float(y[c]);
-          } else {
-  #pragma unroll
-            for (int c = 0; c < 16; ++c) q[c] = live ? orow[cc * 16 + c] : 0.0f;
-          }
+          for (int c = 0; c < 16; ++c) q[c] = __uint_as_float(y[c]);
           if (live) {
-            // a single segment divides rescale(O_seg, 0) (identity on the Markstein window)
-            if (nz) div_chunk<16, !MULTI>(q, lrow, rl, row_fast);
-            else {
+            // a single segment divides rescale(O_seg, 0) (identity on the Markstein window);
+            // O_row is already flushed by the segment -> row fold
+            if (nz) {
+              if (mseg) div_chunk<16, false>(q, lrow, rl, row_fast);
+              else div_chunk<16, true>(q, lrow, rl, row_fast);
+            } else {
   #pragma unroll
               for (int c = 0; c < 16; ++c) q[c] = 0.0f;
             }

@@ -50,9 +50,19 @@ def test_withheld_block_times_out_and_context_survives(withhold):
 
 
 def test_selftest_timeout_rejects_bad_arguments():
+    """A negative block or a wait limit outside (0, 2 s] is refused before any launch.  The
+    buffers are real and sized for the shape all the same, so nothing could read outside them."""
+    B, H, KVH, T, dh = 1, 4, 2, 512, 128
+    q8 = torch.zeros((B, H, T, dh), dtype=torch.int8, device="cuda")
+    eq = torch.zeros((B, H, T), dtype=torch.int32, device="cuda")
+    k8 = torch.zeros((B, KVH, T, dh), dtype=torch.int8, device="cuda")
+    e = torch.zeros((B, KVH, T // 128), dtype=torch.int32, device="cuda")
+    out = torch.zeros((B, T, H, dh), dtype=torch.float32, device="cuda")
     L = _lib.load()
-    p = torch.zeros(16, dtype=torch.int32, device="cuda").data_ptr()
-    os_ = _lib.i64x([512 * 4 * 128, 4 * 128, 128, 1])
-    assert L.lssab8_selftest_timeout(p, p, p, p, p, p, 1, 4, 2, 512, 128, -1, 1000, p, os_, None) == 1
-    assert L.lssab8_selftest_timeout(p, p, p, p, p, p, 1, 4, 2, 512, 128, 0, 0, p, os_, None) == 1
-    assert L.lssab8_selftest_timeout(p, p, p, p, p, p, 1, 4, 2, 8192, 128, 0, 1000, p, os_, None) == 1
+    for withhold, wait_us in ((-1, 1000), (0, 0), (0, 2000001)):
+        rc = L.lssab8_selftest_timeout(q8.data_ptr(), eq.data_ptr(), k8.data_ptr(), e.data_ptr(), k8.data_ptr(),
+                                       e.data_ptr(), B, H, KVH, T, dh, withhold, wait_us, out.data_ptr(),
+                                       _lib.i64x(out.stride()), None)
+        assert rc == 1, (withhold, wait_us)
+    torch.cuda.synchronize()
+    assert _lib.device_errors() == 0

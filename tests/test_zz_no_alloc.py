@@ -61,13 +61,23 @@ def test_noalloc_decode_matches_workspace_decode_twice(dh):
 
 
 def _refused(B, H, KVH, dh, max_blocks):
-    """True when the call is refused for its size: such a call launches nothing, so placeholder
-    pointers are safe here (every argument check before the size check passes)."""
+    """True when the call is refused for its size.  Every buffer is real and sized for the shape,
+    and every sequence is empty, so even a call that were accepted would read nothing it does not
+    own (no key page is touched for an empty sequence, and no output row is written)."""
     L = _lib.load()
-    z = torch.zeros(16, dtype=torch.int32, device="cuda")
-    p = z.data_ptr()
-    return L.lssab8_decode_noalloc(p, 2, _lib.i64x([H * dh, dh, 1]), B, H, KVH, dh, p, p, 8 * max_blocks, 1, p, p, p,
-                                   p, p, max_blocks, 4, 0, p, 2, _lib.i64x([H * dh, dh, 1]), None) == ESCRATCH
+    q = torch.zeros((B, H, dh), dtype=torch.bfloat16, device="cuda")
+    lens = torch.zeros(B, dtype=torch.int32, device="cuda")
+    bt = torch.zeros((B, 8 * max_blocks), dtype=torch.int32, device="cuda")
+    k8p = torch.zeros((1, KVH, 16, dh), dtype=torch.int8, device="cuda")
+    v8p = torch.zeros((1, KVH, dh, 16), dtype=torch.int8, device="cuda")
+    e = torch.zeros((B, KVH, max_blocks), dtype=torch.int32, device="cuda")
+    e0 = torch.zeros((B, KVH), dtype=torch.int32, device="cuda")
+    out = torch.zeros((B, H, dh), dtype=torch.bfloat16, device="cuda")
+    rc = L.lssab8_decode_noalloc(q.data_ptr(), 2, _lib.i64x(q.stride()), B, H, KVH, dh, lens.data_ptr(), bt.data_ptr(),
+                                 8 * max_blocks, 1, k8p.data_ptr(), v8p.data_ptr(), e.data_ptr(), e.data_ptr(),
+                                 e0.data_ptr(), max_blocks, 4, 0, out.data_ptr(), 2, _lib.i64x(out.stride()), None)
+    torch.cuda.synchronize()
+    return rc == ESCRATCH
 
 
 def test_noalloc_scratch_limit_is_exact():
