@@ -4,12 +4,14 @@
 Headline workload (BASELINE.json configs[3] = config 4, the configuration the north star shards):
 Qwen2.5-72B-shaped causal GQA prefill, B=8, 64 query / 8 kv heads, dh 128, T 8192, bf16 inputs
 N(0,1) from seed 0, sink off, sharded over the N ranks by kv-head group (rank r owns kv heads
-[r*8/N, (r+1)*8/N) and their query heads) with the outputs all-gathered over NCCL.  One step =
-the whole job: every rank's PREP quantisers and persistent tcgen05 prefill kernel over its heads,
-chunk by chunk, with each chunk's all-gather (and the scatter into [B, T, H, dh]) on a second
-stream under the next chunk's compute; value = 8.797e12 ops / the max-over-ranks step time
-(strong scaling: the total work is fixed).  Inputs are resident in HBM when the timed region
-starts; L2 is flushed (a 512 MB write) before every timed step, outside the timed events.
+[r*8/N, (r+1)*8/N) and their query heads) with the outputs gathered on every rank.  One step =
+the whole job: a barrier, every rank's PREP quantisers and persistent tcgen05 prefill kernel over
+its heads -- whose epilogue stores each finished output tile into its own [B, T, H, dh] buffer
+and, over NVLink, into every other rank's (CUDA IPC peer buffers: the gather fused into the
+kernel) -- and a closing barrier; value = 8.797e12 ops / the max-over-ranks step time (strong
+scaling: the total work is fixed).  The NCCL all-gather form of the same step is timed beside
+it.  Inputs are resident in HBM when the timed region starts; L2 is flushed (a 512 MB write)
+before every timed step, outside the timed events.
 
 Also in the line: the compute alone and the gather alone; the prefill kernel's roofline; the
 end-to-end public-API call (pinned host shard -> device -> gathered -> this rank's rows back to
@@ -196,12 +198,21 @@ def run_gpu(args):
     qh, kh, vh = W.prefill_inputs_shard(B, H, KVH, T, dh, (h0, h1), (g0, g1), seed=0, pin=True)
     t_gen = time.time() - t_gen
     qd, kd, vd = qh.to(dev), kh.to(dev), vh.to(dev)
-    out = torch.empty((B, T, H, dh), dtype=torch.bfloat16, device=dev)
-    chunk = B if world == 1 else args.chunk
+    peers, peer_note = None, None
+    if world > 1:
+        try:
+            peers = SH.PeerOutputs((B, T, H, dh), torch.bfloat16, dev)
+        except Exception as e:                        # GPUs that cannot reach each other: NCCL gather
+            peer_note = "peer buffers unavailable (%s); NCCL all-gather" % str(e)[:120]
+    out = peers.local if peers is not None else torch.empty((B, T, H, dh), dtype=torch.bfloat16, device=dev)
+    chunk = B if (world == 1 or peers is not None) else args.chunk
     ops4 = prefill_ops(B, H, T, dh)
 
     def step4():
-        SH.prefill_shard_gather(qd, kd, vd, H, out=out, chunk=chunk)
+        if peers is not None:
+            SH.prefill_shard_gather(qd, kd, vd, H, peers=peers, chunk=chunk)
+        else:
+            SH.prefill_shard_gather(qd, kd, vd, H, out=out, chunk=chunk)
 
     step4()                                   # correctness of this very workload, on every rank's gathered copy
     torch.cuda.synchronize()
@@ -235,9 +246,13 @@ def run_gpu(args):
 
     loc = torch.empty((B, T, h1 - h0, dh), dtype=torch.bfloat16, device=dev)
     t_comp = max_over_ranks(timer(lambda: A.prefill(qd, kd, vd, out=loc, check=False), args.steps, 1))
-    t_gath = None
+    t_gath = t_nccl = None
     if world > 1:
-        t_gath = max_over_ranks(timer(lambda: SH._gather_into(out, loc, world, None), args.steps, 1))
+        nout = torch.empty((B, T, H, dh), dtype=torch.bfloat16, device=dev)
+        t_gath = max_over_ranks(timer(lambda: SH._gather_into(nout, loc, world, None), args.steps, 1))
+        t_nccl = max_over_ranks(timer(lambda: SH.prefill_shard_gather(qd, kd, vd, H, out=nout, chunk=args.chunk),
+                                      args.steps, 1))
+        del nout
 
     # the prefill kernel alone on this rank's whole shard (one launch)
     q8, eq = A.quant_rows(qd)
@@ -259,8 +274,13 @@ def run_gpu(args):
     # output back to pinned host memory
     r0, r1 = rank * T // world, (rank + 1) * T // world
     hout = torch.empty((B, r1 - r0, H, dh), dtype=torch.bfloat16).pin_memory()
-    t_e2e = max_over_ranks(timer(lambda: SH.prefill_shard_gather(qh, kh, vh, H, out=out, chunk=1, host_out=hout,
-                                                                 host_rows=(r0, r1)), args.steps, 2))
+    if peers is not None:
+        e2e_call = lambda: SH.prefill_shard_gather(qh, kh, vh, H, peers=peers, chunk=1, host_out=hout,  # noqa: E731
+                                                   host_rows=(r0, r1))
+    else:
+        e2e_call = lambda: SH.prefill_shard_gather(qh, kh, vh, H, out=out, chunk=1, host_out=hout,  # noqa: E731
+                                                   host_rows=(r0, r1))
+    t_e2e = max_over_ranks(timer(e2e_call, args.steps, 2))
     e2e_ok = None
     if rank == 0:
         e2e_ok = bool(torch.equal(hout.view(torch.int16), out[:, r0:r1].cpu().view(torch.int16)))
@@ -340,6 +360,8 @@ def run_gpu(args):
         bit4 = bool(check4["samples"]) and check4.get("ranks_agree", True) is not False and \
             check4["n1_digest"] is not False
     launches = (B // chunk + (B % chunk > 0)) * 3                # Q quantiser, K/V quantiser, prefill per chunk
+    gather = ("fused: epilogue P2P stores into %d peer buffer(s) over NVLink (CUDA IPC), NCCL barriers around "
+              "the kernel" % (world - 1)) if peers is not None else (peer_note or "none (one GPU)")
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": "TOPS", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(t4, 4), "higher_is_better": True, "scaling": "strong",
@@ -347,13 +369,15 @@ def run_gpu(args):
         "config": {"workload": "cfg4 causal GQA prefill (Qwen2.5-72B shape), sharded by kv-head group, outputs "
                                "all-gathered (NCCL)", "B": B, "H": H, "KVH": KVH, "dh": dh, "T": T, "sink": False,
                    "l2": "flushed (512 MB write) before each timed step; inputs (1.3 GB / N per rank) exceed L2",
-                   "parallelism": "kv-group x%d" % world, "chunk": chunk,
+                   "parallelism": "kv-group x%d" % world, "chunk": chunk, "gather": "fused P2P" if peers else "NCCL",
                    "inputs": "numpy PCG64 seed 0, bf16 (generated in %.0f s)" % t_gen},
         "prefill_frac_int8_peak": round(value / world / int8_peak, 4),
         "bit_exact_vs_reference": bit4,
         "bits": check4,
-        "compute_ms": round(t_comp, 4), "gather_ms": None if t_gath is None else round(t_gath, 4),
-        "gather_exposed_ms": round(t4 - t_comp, 4),
+        "gather": gather,
+        "compute_ms": round(t_comp, 4), "gather_exposed_ms": round(t4 - t_comp, 4),
+        "nccl_allgather_ms": None if t_gath is None else round(t_gath, 4),
+        "nccl_step_ms": None if t_nccl is None else round(t_nccl, 4),
         "roofline": roofline,
         "e2e": {"value": round(ops4 / (t_e2e * 1e-3) / 1e12, 3), "unit": "TOPS", "ms_per_step": round(t_e2e, 4),
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "host_rows_match": e2e_ok,
@@ -366,6 +390,8 @@ def run_gpu(args):
     line.update(extra)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(qh, kh, vh)
+    if peers is not None:
+        peers.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

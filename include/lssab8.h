@@ -121,6 +121,34 @@ int lssab8_prefill(const void* q, const void* k, const void* v, int dtype, int B
                    const int64_t* qs, const int64_t* ks, const int64_t* vs, int sink, void* out, int out_dtype,
                    const int64_t* os, void* workspace, size_t workspace_bytes, void* stream);
 
+/* The sharded form of lssab8_prefill, with the output gather fused into the kernel.  No
+ * reference counterpart: the reference has no multi-GPU attention; the split is the one the
+ * contract allows (every row is an independent recurrence, so kv-head groups shard with no
+ * arithmetic across ranks).  Rank r of n runs lssab8_prefill on its kv heads and their query
+ * heads, writing its rows into its own output buffer out (strides os) AND, with the same element
+ * offsets, into each of the npeers (<= 7) addresses peer_out[i]: the other ranks' output buffers
+ * mapped into this process (lssab8_peer_import), each congruent to out modulo 16 bytes.  The
+ * stores go over NVLink as the tiles finish; each CTA ends with a system-scope fence, so once
+ * the kernel has completed on every rank (a barrier ordered after it on each rank's stream) every
+ * rank's buffer holds every rank's heads.  The caller also orders a barrier before the call, so
+ * that no rank writes into a buffer its owner is still reading. */
+int lssab8_prefill_peers(const void* q, const void* k, const void* v, int dtype, int B, int H, int KVH, int T, int dh,
+                         const int64_t* qs, const int64_t* ks, const int64_t* vs, int sink, void* out, int out_dtype,
+                         const int64_t* os, void* const* peer_out, int npeers, void* workspace,
+                         size_t workspace_bytes, void* stream);
+
+/* Peer buffers for lssab8_prefill_peers (CUDA IPC; no reference counterpart).
+ * lssab8_peer_export: the 64-byte IPC handle of the device allocation holding ptr (written to
+ *   handle) and ptr's byte offset in it.
+ * lssab8_peer_import: maps another process's exported buffer, owned by CUDA device owner_device
+ *   (an ordinal of this process), into this process with peer access from the current device
+ *   enabled, and returns the address of the exported ptr in *ptr.  LSSAB8_EUNSUPPORTED when the
+ *   current device cannot reach owner_device by peer access.
+ * lssab8_peer_close: unmaps an address lssab8_peer_import returned (with its offset). */
+int lssab8_peer_export(const void* ptr, void* handle, uint64_t* offset);
+int lssab8_peer_import(const void* handle, uint64_t offset, int owner_device, void** ptr);
+int lssab8_peer_close(void* ptr, uint64_t offset);
+
 /* ---------------------------------------------------------------------------- decode */
 
 /* Paged int8 lattice writer.  Sequence b has seq_lens[b] tokens; token t, kv head g, channel c

@@ -17,6 +17,7 @@ SYMBOLS = (
     "lssab8_version", "lssab8_strerror", "lssab8_device_errors",
     "lssab8_quant_rows", "lssab8_quant_blocks", "lssab8_quant_keys_offset",
     "lssab8_prefill_lattice", "lssab8_prefill_chunk_lattice", "lssab8_prefill_workspace_size", "lssab8_prefill",
+    "lssab8_prefill_peers", "lssab8_peer_export", "lssab8_peer_import", "lssab8_peer_close",
     "lssab8_decode_prep_kv", "lssab8_decode_workspace_size", "lssab8_decode",
     "lssab8_decode_noalloc", "lssab8_selftest_div", "lssab8_selftest_rescale", "lssab8_selftest_timeout",
 )
@@ -52,6 +53,10 @@ def load():
     L.lssab8_prefill_workspace_size.argtypes = [I] * 5
     L.lssab8_prefill_workspace_size.restype = SZ
     L.lssab8_prefill.argtypes = [P, P, P, I, I, I, I, I, I, PI64, PI64, PI64, I, P, I, PI64, P, SZ, P]
+    L.lssab8_prefill_peers.argtypes = [P, P, P, I, I, I, I, I, I, PI64, PI64, PI64, I, P, I, PI64, P, I, P, SZ, P]
+    L.lssab8_peer_export.argtypes = [P, P, ctypes.POINTER(ctypes.c_uint64)]
+    L.lssab8_peer_import.argtypes = [P, ctypes.c_uint64, I, ctypes.POINTER(P)]
+    L.lssab8_peer_close.argtypes = [P, ctypes.c_uint64]
     L.lssab8_decode_prep_kv.argtypes = [P, P, I, I, I, I, P, P, I64, I64, I64, P, I, I, I, I, P, P, P, P, P, P]
     L.lssab8_decode_workspace_size.argtypes = [I] * 5
     L.lssab8_decode_workspace_size.restype = SZ

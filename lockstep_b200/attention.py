@@ -4,6 +4,8 @@ PyTorch is used only for device memory and the current CUDA stream; every comput
 liblssab8_b200.so.  Tensors must be CUDA tensors of one floating dtype (float32 / float16 /
 bfloat16); anything else raises -- there is no CPU path.
 """
+import ctypes
+
 import torch
 
 from . import _lib
@@ -154,6 +156,38 @@ def prefill_chunk_lattice(q8, eq, k8, ek, v8, ev, ev0, T0, T, out=None, out_dtyp
             None, out.data_ptr(), dtype_code(out.dtype),
             _lib.i64x(out.stride()), _stream_handle(dev)),
             "lssab8_prefill_chunk_lattice")
+    return out
+
+
+def prefill_peers(query, key, value, out, peer_ptrs, sink=False, check=False):
+    """The sharded prefill with the gather fused into the kernel (lssab8_prefill_peers): this
+    rank's rows go into `out` (a view of this rank's output buffer, any strides) and, at the same
+    element offsets, into every address of peer_ptrs (other ranks' buffers mapped into this
+    process, already offset to the same place as `out`).  query [B, h, T, dh], key/value
+    [B, kvh, T, dh]: this rank's heads.  The caller orders the ranks' barriers around it."""
+    dev = _require_cuda(query, key, value, out)
+    if not (query.dtype == key.dtype == value.dtype):
+        raise TypeError("query, key and value must share one dtype")
+    B, H, T, dh = query.shape
+    KVH = key.shape[1]
+    if tuple(out.shape) != (B, T, H, dh):
+        raise ValueError("out must be [B, T, h, dh] for this rank's heads")
+    if len(peer_ptrs) > 7:
+        raise ValueError("at most 7 peers")
+    L = _lib.load()
+    nbytes = L.lssab8_prefill_workspace_size(B, H, KVH, T, dh)
+    if nbytes == 0:
+        raise ValueError("unsupported prefill shape")
+    ws = workspace(dev, nbytes)
+    arr = (ctypes.c_void_p * max(len(peer_ptrs), 1))(*[int(p) for p in peer_ptrs])
+    with torch.cuda.device(dev):
+        _lib.check(L.lssab8_prefill_peers(query.data_ptr(), key.data_ptr(), value.data_ptr(), dtype_code(query.dtype), B,
+                                          H, KVH, T, dh, _lib.i64x(query.stride()), _lib.i64x(key.stride()),
+                                          _lib.i64x(value.stride()), int(bool(sink)), out.data_ptr(),
+                                          dtype_code(out.dtype), _lib.i64x(out.stride()), arr, len(peer_ptrs),
+                                          ws.data_ptr(), ws.numel(), _stream_handle(dev)), "lssab8_prefill_peers")
+    if check:
+        check_device_errors(dev)
     return out
 
 

@@ -360,7 +360,8 @@ __global__ void selftest_rescale_kernel(const float* x, const int* D, long long 
 static int prefill_lattice_impl(const int8_t* q8, const int32_t* eq, const int8_t* k8, const int32_t* ek, const int8_t* v8,
                          const int32_t* ev, const int32_t* ev0, int B, int H, int KVH, int T0, int T, int dh,
                          float* orow_scratch, void* out, int out_dtype, const int64_t* os, void* stream,
-                         uint64_t wait_ns = kWaitLimitNs, int withhold = -1) {
+                         uint64_t wait_ns = kWaitLimitNs, int withhold = -1, int npeers = 0,
+                         void* const* peers = nullptr) {
   if (!q8 || !eq || !k8 || !ek || !v8 || !ev || !out || !shape_ok(B, H, KVH, T, dh) || !strides_ok(os, 4))
     return kErrArg;
   if (dh != 64 && dh != 128) return kErrUnsupported;
@@ -386,6 +387,13 @@ static int prefill_lattice_impl(const int8_t* q8, const int32_t* eq, const int8_
   a.err = ds->err;
   a.wait_ns = wait_ns;
   a.withhold = withhold;
+  if (npeers < 0 || npeers > kMaxPeers || (npeers > 0 && !peers)) return kErrArg;
+  a.npeers = npeers;
+  for (int i = 0; i < npeers; ++i) {
+    // same alignment as out modulo 16 bytes, so the vectorised stores apply to every copy
+    if (!peers[i] || ((reinterpret_cast<uintptr_t>(peers[i]) ^ reinterpret_cast<uintptr_t>(out)) & 15)) return kErrArg;
+    a.peers[i] = peers[i];
+  }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool sink = ev0 != nullptr;
   if (dh == 128) return sink ? launch_prefill_out<128, true>(out_dtype, tq, tk, tv, a, ds->num_sms, st)
@@ -534,9 +542,12 @@ size_t lssab8_prefill_workspace_size(int B, int H, int KVH, int T, int dh) {
   return prefill_ws(B, H, KVH, T, dh).total;
 }
 
-int lssab8_prefill(const void* q, const void* k, const void* v, int dtype, int B, int H, int KVH, int T, int dh,
-                   const int64_t* qs, const int64_t* ks, const int64_t* vs, int sink, void* out, int out_dtype,
-                   const int64_t* os, void* workspace, size_t workspace_bytes, void* stream) {
+}  // extern "C"
+
+static int prefill_impl(const void* q, const void* k, const void* v, int dtype, int B, int H, int KVH, int T, int dh,
+                        const int64_t* qs, const int64_t* ks, const int64_t* vs, int sink, void* out, int out_dtype,
+                        const int64_t* os, void* workspace, size_t workspace_bytes, void* stream, int npeers,
+                        void* const* peers) {
   if (!q || !k || !v || !out || !workspace || !shape_ok(B, H, KVH, T, dh)) return kErrArg;
   if (dh != 64 && dh != 128) return kErrUnsupported;
   const PrefillWs w = prefill_ws(B, H, KVH, T, dh);
@@ -573,8 +584,78 @@ int lssab8_prefill(const void* q, const void* k, const void* v, int dtype, int B
     if ((rc = lssab8_quant_blocks(k, dtype, B, KVH, T, dh, ks, Tpad, 0, k8, ek, nullptr, stream))) return rc;
     if ((rc = lssab8_quant_blocks(v, dtype, B, KVH, T, dh, vs, Tpad, vmode, v8, ev, ev0, stream))) return rc;
   }
-  return lssab8_prefill_lattice(q8, eq, k8, ek, v8, ev, (sink && T > 1) ? ev0 : nullptr, B, H, KVH, T, dh, Tpad,
-                                nullptr, out, out_dtype, os, stream);
+  return prefill_lattice_impl(q8, eq, k8, ek, v8, ev, (sink && T > 1) ? ev0 : nullptr, B, H, KVH, 0, T, dh, nullptr,
+                              out, out_dtype, os, stream, kWaitLimitNs, -1, npeers, peers);
+}
+
+extern "C" {
+
+int lssab8_prefill(const void* q, const void* k, const void* v, int dtype, int B, int H, int KVH, int T, int dh,
+                   const int64_t* qs, const int64_t* ks, const int64_t* vs, int sink, void* out, int out_dtype,
+                   const int64_t* os, void* workspace, size_t workspace_bytes, void* stream) {
+  return prefill_impl(q, k, v, dtype, B, H, KVH, T, dh, qs, ks, vs, sink, out, out_dtype, os, workspace,
+                      workspace_bytes, stream, 0, nullptr);
+}
+
+int lssab8_prefill_peers(const void* q, const void* k, const void* v, int dtype, int B, int H, int KVH, int T, int dh,
+                         const int64_t* qs, const int64_t* ks, const int64_t* vs, int sink, void* out, int out_dtype,
+                         const int64_t* os, void* const* peer_out, int npeers, void* workspace,
+                         size_t workspace_bytes, void* stream) {
+  if (npeers < 0 || npeers > kMaxPeers) return kErrArg;
+  return prefill_impl(q, k, v, dtype, B, H, KVH, T, dh, qs, ks, vs, sink, out, out_dtype, os, workspace,
+                      workspace_bytes, stream, npeers, peer_out);
+}
+
+// ------------------------------------------------------------ peer buffers (CUDA IPC)
+static PFN_cuMemGetAddressRange_v3020 g_range = nullptr;
+
+static int get_range_fn() {
+  static std::once_flag once;
+  static int rc = kOk;
+  std::call_once(once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !fn) {
+      rc = kErrCuda;
+      return;
+    }
+    g_range = reinterpret_cast<PFN_cuMemGetAddressRange_v3020>(fn);
+  });
+  return rc;
+}
+
+int lssab8_peer_export(const void* ptr, void* handle, uint64_t* offset) {
+  if (!ptr || !handle || !offset) return kErrArg;
+  if (get_range_fn() != kOk) return kErrCuda;
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (g_range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS) return kErrArg;
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)) != cudaSuccess) return kErrCuda;
+  std::memcpy(handle, &h, sizeof h);
+  *offset = (uint64_t)(reinterpret_cast<CUdeviceptr>(ptr) - base);
+  return kOk;
+}
+
+int lssab8_peer_import(const void* handle, uint64_t offset, int owner_device, void** ptr) {
+  if (!handle || !ptr) return kErrArg;
+  int dev = 0, can = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return kErrCuda;
+  if (owner_device == dev) return kErrArg;
+  if (cudaDeviceCanAccessPeer(&can, dev, owner_device) != cudaSuccess) return kErrCuda;
+  if (!can) return kErrUnsupported;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof h);
+  void* base = nullptr;
+  if (cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) return kErrCuda;
+  *ptr = static_cast<uint8_t*>(base) + offset;
+  return kOk;
+}
+
+int lssab8_peer_close(void* ptr, uint64_t offset) {
+  if (!ptr) return kErrArg;
+  return cuda_rc(cudaIpcCloseMemHandle(static_cast<uint8_t*>(ptr) - offset));
 }
 
 int lssab8_decode_prep_kv(const void* k, const void* v, int dtype, int B, int KVH, int dh, const int32_t* seq_lens,

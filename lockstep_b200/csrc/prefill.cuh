@@ -52,6 +52,7 @@
 #include "tcgen05.cuh"
 
 namespace lssab8 {
+constexpr int kMaxPeers = 7;                                  // other ranks of one 8-GPU node
 struct PrefillArgs {
   int B, H, KVH, T, dh, Tpad, nblk, group;
   int tile0;            // key-block index of the first query tile (a block-aligned chunk; 0: whole prefill)
@@ -72,6 +73,11 @@ struct PrefillArgs {
   int* err;
   uint64_t wait_ns;     // limit of every bounded wait (kWaitLimitNs; shorter only in the timeout self-test)
   int withhold;         // self-test only: the TMA producer never loads this key block of its first item (-1: none)
+  // Peer outputs (the sharded prefill's gather): the same output rows are also stored, with the
+  // same element strides, at each of these addresses -- other GPUs' output buffers mapped into
+  // this process (CUDA IPC, P2P over NVLink) -- so every rank ends with every rank's heads.
+  int npeers;
+  void* peers[kMaxPeers];
 };
 
 // ------------------------------------------------------------------------ smem layout
@@ -651,6 +657,10 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
               for (int c = 0; c < 16; ++c) q[c] = 0.0f;
             }
             store_chunk<OutT, 16>(dst + cc * 16 * p.os3, p.os3, q);
+            for (int pr = 0; pr < p.npeers; ++pr) {      // the gather: the same rows into every peer
+              OutT* pd = reinterpret_cast<OutT*>(p.peers[pr]) + (dst - reinterpret_cast<OutT*>(p.out));
+              store_chunk<OutT, 16>(pd + cc * 16 * p.os3, p.os3, q);
+            }
           }
         }
         tc_wait_st();
@@ -664,6 +674,9 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
   }
 
   // ---- teardown
+  // stores into peers' memory are visible system-wide before this CTA ends, hence before the
+  // kernel completes and before whatever the stream orders after it (the ranks' barrier)
+  if (p.npeers > 0) __threadfence_system();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();

@@ -8,13 +8,23 @@ The path shards without any reduction: every output row is an independent recurr
 The only collective is the output gather (NCCL over NVLink on GPUs; gloo works for CPU tests).
 Results are bit-identical at every rank count because no arithmetic crosses a rank.
 
-prefill_shard_gather pipelines the gather with the compute: the batch is cut into chunks, and
-while the kernel runs chunk c + 1 on the caller's stream, a second stream all-gathers chunk c's
-head shards and scatters them into the [B, T, H, dh] output.  Inputs may sit in pinned host
-memory (copied chunk by chunk on a third stream under the previous chunk's compute), and a
-pinned host tensor can receive this rank's rows of every gathered chunk on a fourth stream, so
-an end-to-end host -> device -> host call overlaps all four.
+On GPUs the gather is fused into the prefill kernel: every rank's output buffer is mapped into
+every other rank (PeerOutputs: CUDA IPC, P2P over NVLink), and the kernel's epilogue stores each
+finished output tile into its own buffer and, at the same place, into every peer's, so the gather
+overlaps the compute tile by tile and costs no SM time of its own.  Two barriers on the stream
+(a one-element NCCL all-reduce) bracket the kernel: before it, so no rank writes into a buffer
+its owner still reads; after it, so every rank's buffer is complete when the call returns.
+
+Without peer buffers (CPU ranks, or GPUs that cannot reach each other), prefill_shard_gather
+falls back to NCCL: the batch is cut into chunks, and while the kernel runs chunk c + 1 on the
+caller's stream, a second stream all-gathers chunk c's head shards and scatters them into the
+[B, T, H, dh] output.  Either way, inputs may sit in pinned host memory (copied chunk by chunk
+on a third stream under the previous chunk's compute), and a pinned host tensor can receive
+this rank's rows of every finished chunk on a fourth stream, so an end-to-end host -> device ->
+host call overlaps them all.
 """
+import ctypes
+
 import torch
 import torch.distributed as dist
 
@@ -45,13 +55,73 @@ def _world(group=None):
     return 1, 0
 
 
+class PeerOutputs:
+    """An output buffer on every rank of the group, mapped into every other rank (CUDA IPC).
+
+    local: this rank's tensor (shape, dtype, on `device`); peers: {rank: (address, offset)} of the
+    other ranks' buffers in this process.  Every process must see every GPU under the same
+    ordinals (as torchrun leaves them).  close() (collective) unmaps them."""
+
+    def __init__(self, shape, dtype, device, group=None):
+        from . import _lib
+        self.world, self.rank = _world(group)
+        self.group = group
+        self.local = torch.empty(shape, dtype=dtype, device=device)
+        self.flag = torch.zeros(1, dtype=torch.float32, device=device)
+        self.peers = {}
+        L = _lib.load()
+        h = ctypes.create_string_buffer(64)
+        off = ctypes.c_uint64(0)
+        _lib.check(L.lssab8_peer_export(self.local.data_ptr(), h, ctypes.byref(off)), "lssab8_peer_export")
+        infos = [None] * self.world
+        dist.all_gather_object(infos, (bytes(h.raw), int(off.value), int(self.local.device.index)), group=group)
+        err = None
+        with torch.cuda.device(self.local.device):
+            for r, (hb, o, d) in enumerate(infos):
+                if r == self.rank:
+                    continue
+                ptr = ctypes.c_void_p()
+                rc = L.lssab8_peer_import(hb, o, d, ctypes.byref(ptr))
+                if rc:
+                    err = _lib.Lssab8Error(rc, "lssab8_peer_import of rank %d" % r)
+                    break
+                self.peers[r] = (int(ptr.value), int(o))
+        # every rank takes the same branch: if any rank cannot map a peer, none uses the buffers
+        ok = torch.tensor([0.0 if err else 1.0], device=self.local.device)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
+        if ok.item() < 1.0:
+            for ptr, o in self.peers.values():
+                L.lssab8_peer_close(ptr, o)
+            self.peers = {}
+            raise err or RuntimeError("another rank could not map its peer buffers")
+
+    def barrier(self):
+        """A barrier of the ranks ordered on the current stream (a one-element NCCL all-reduce)."""
+        dist.all_reduce(self.flag, group=self.group)
+
+    def addresses(self, view):
+        """The peers' addresses of the element `view` starts at in the local buffer."""
+        off = view.data_ptr() - self.local.data_ptr()
+        return [self.peers[r][0] + off for r in sorted(self.peers)]
+
+    def close(self):
+        from . import _lib
+        torch.cuda.synchronize(self.local.device)
+        dist.barrier(group=self.group)                 # nobody writes into a buffer being unmapped
+        L = _lib.load()
+        for ptr, off in self.peers.values():
+            _lib.check(L.lssab8_peer_close(ptr, off), "lssab8_peer_close")
+        self.peers = {}
+        dist.barrier(group=self.group)                 # every mapping is gone before owners free
+
+
 def _kernel_compute(q, k, v, sink, out):
     from . import attention as A
     return A.prefill(q, k, v, sink=sink, out=out, check=False)
 
 
 def prefill_shard_gather(q, k, v, H, sink=False, out=None, chunk=1, group=None, compute=None,
-                         host_out=None, host_rows=None):
+                         host_out=None, host_rows=None, peers=None):
     """Sharded causal GQA prefill, gathered: every rank returns the whole out [B, T, H, dh].
 
     q [B, h, T, dh], k / v [B, kvh, T, dh]: this rank's shard, query heads [r*h, (r+1)*h) and kv
@@ -59,11 +129,19 @@ def prefill_shard_gather(q, k, v, H, sink=False, out=None, chunk=1, group=None, 
     pinned host memory, in which case each chunk is copied in on its own stream.  chunk: batch
     elements per pipeline step.  compute(q, k, v, sink, out) -> out [b, T, h, dh] defaults to the
     B200 kernel (attention.prefill).  host_out [B, T1 - T0, H, dh] (pinned) receives rows
-    host_rows = (T0, T1) of every gathered batch element.  The result's dtype is q's."""
+    host_rows = (T0, T1) of every gathered batch element.  The result's dtype is q's.
+    peers: a PeerOutputs of shape [B, T, H, dh]: the gather is fused into the kernel (the result
+    is peers.local; `out` and `compute` must be None)."""
     world, rank = _world(group)
     B, h, T, dh = q.shape
     if H != h * world:
         raise ValueError("H = %d query heads cannot be %d ranks x %d" % (H, world, h))
+    if peers is not None:
+        if out is not None or compute is not None:
+            raise ValueError("with peers the result is peers.local and the kernel computes it")
+        if tuple(peers.local.shape) != (B, T, H, dh) or peers.world != world:
+            raise ValueError("the peer buffers do not match this call")
+        out = peers.local
     compute = compute or _kernel_compute
     dev = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() and (
         q.is_cuda or q.is_pinned()) else q.device
@@ -82,8 +160,9 @@ def prefill_shard_gather(q, k, v, H, sink=False, out=None, chunk=1, group=None, 
         return out
 
     cur = torch.cuda.current_stream(dev)
+    fused = peers is not None and world > 1
     s_in = torch.cuda.Stream(dev) if not q.is_cuda else None
-    s_comm = torch.cuda.Stream(dev) if world > 1 else None
+    s_comm = torch.cuda.Stream(dev) if world > 1 and not fused else None
     s_out = torch.cuda.Stream(dev) if host_out is not None else None
     start = torch.cuda.Event()
     start.record(cur)
@@ -103,6 +182,8 @@ def prefill_shard_gather(q, k, v, H, sink=False, out=None, chunk=1, group=None, 
                 ev.record(s_in)
             loaded[c] = (t, ev)
         load(0)
+    if fused:
+        peers.barrier()                               # every owner is done reading its buffer
     for c, (b0, b1) in enumerate(chunks):
         if loaded is not None:
             if c + 1 < len(chunks):
@@ -115,6 +196,13 @@ def prefill_shard_gather(q, k, v, H, sink=False, out=None, chunk=1, group=None, 
             qc, kc, vc = q[b0:b1], k[b0:b1], v[b0:b1]
         if world == 1:
             compute(qc, kc, vc, sink, out[b0:b1])
+            done = out[b0:b1]
+        elif fused:
+            from . import attention as A
+            mine = out[b0:b1, :, rank * h:(rank + 1) * h]
+            A.prefill_peers(qc, kc, vc, mine, peers.addresses(mine), sink=sink)
+            if s_out is not None or c + 1 == len(chunks):
+                peers.barrier()                       # this chunk is complete on every rank
             done = out[b0:b1]
         else:
             loc = torch.empty((b1 - b0, T, h, dh), dtype=out.dtype, device=dev)

@@ -1,6 +1,7 @@
-"""The sharded path on two GPUs with NCCL, on the real kernels: kv-head-group prefill with the
-pipelined output all-gather (device inputs, and pinned host inputs with this rank's rows read
-back), and sequence-partitioned paged decode.  Every rank's gathered output must equal the
+"""The sharded path on two GPUs, on the real kernels: kv-head-group prefill with the pipelined
+NCCL output all-gather and with the gather fused into the kernel (epilogue P2P stores into the
+other rank's buffer, CUDA IPC), each from device inputs and from pinned host inputs with this
+rank's rows read back; and sequence-partitioned paged decode.  Every rank's gathered output must equal the
 pinned oracle bit for bit, which is also the single-GPU result: no arithmetic crosses a rank.
 
 Needs two GPUs in this process's view (skipped otherwise: NCCL does not run two ranks on one GPU).
@@ -55,6 +56,17 @@ def _worker(rank, world, port, ret):
         host = torch.empty((B, rows[1] - rows[0], H, DH), dtype=torch.bfloat16).pin_memory()
         out2 = SH.prefill_shard_gather(qh, kh, vh, H, chunk=2, host_out=host, host_rows=rows)
         torch.cuda.synchronize()
+        # the gather fused into the kernel: P2P stores into the other rank's mapped buffer
+        peers = SH.PeerOutputs((B, T, H, DH), torch.bfloat16, dev)
+        peers.local.fill_(float("nan"))
+        SH.prefill_shard_gather(qd, kd, vd, H, peers=peers, chunk=B)
+        out3 = peers.local.clone()
+        host3 = torch.empty_like(host).pin_memory()
+        peers.local.fill_(float("nan"))
+        SH.prefill_shard_gather(qh, kh, vh, H, peers=peers, chunk=1, host_out=host3, host_rows=rows)
+        torch.cuda.synchronize()
+        out4 = peers.local.clone()
+        peers.close()
         # decode: sequences partitioned over the ranks, each rank quantises only its own
         lens = [700, 1, 130, 511, 256]
         rng = np.random.default_rng(4)
@@ -73,8 +85,9 @@ def _worker(rank, world, port, ret):
         dec = SH.decode_sharded(dq, lens, local)
         torch.cuda.synchronize()
         dig = lambda t: hashlib.sha256(t.cpu().view(torch.int16).numpy().tobytes()).hexdigest()
-        ret[rank] = dict(out1=dig(out1), out2=dig(out2), host=host.view(torch.int16).numpy().copy(), rows=rows,
-                         dec=dec.cpu().view(torch.int16).numpy().copy())
+        ret[rank] = dict(out1=dig(out1), out2=dig(out2), out3=dig(out3), out4=dig(out4),
+                         host=host.view(torch.int16).numpy().copy(), host3=host3.view(torch.int16).numpy().copy(),
+                         rows=rows, dec=dec.cpu().view(torch.int16).numpy().copy())
         if rank == 0:
             ret["full"] = out1.cpu().view(torch.int16).numpy().copy()
             ret["dq"], ret["dk"], ret["dv"], ret["lens"] = (dq.float().cpu().numpy(), dk.float().numpy(),
@@ -94,9 +107,11 @@ def test_two_nccl_ranks_equal_oracle():
     full = ret["full"].view(np.uint16)
     assert np.array_equal(full, ref)
     for r in range(2):
-        assert ret[r]["out1"] == ret[0]["out1"] and ret[r]["out2"] == ret[0]["out1"], r
+        for key in ("out1", "out2", "out3", "out4"):
+            assert ret[r][key] == ret[0]["out1"], (r, key)
         t0, t1 = ret[r]["rows"]
         assert np.array_equal(ret[r]["host"].view(np.uint16), ref[:, t0:t1]), r
+        assert np.array_equal(ret[r]["host3"].view(np.uint16), ref[:, t0:t1]), r
         assert np.array_equal(ret[r]["dec"], ret[0]["dec"]), r
     dq, dk, dv, lens = ret["dq"], ret["dk"], ret["dv"], ret["lens"]
     dec = ret[0]["dec"].view(np.uint16)
