@@ -304,19 +304,20 @@ def run_gpu(args):
     btd = torch.tensor(bt, device=dev)
     lmd = torch.tensor(lm, dtype=torch.int32, device=dev)
     kv = D.build_paged_kv(fk.contiguous(), fv.contiguous(), lmd, btd, npages, sink=True, cu_seqlens=cu)
-    idx = torch.tensor(mine, device=dev)
+    plan5 = SH.DecodePartition(lens, world, rank, dev)
+    q5m = q5d[plan5.mine_idx].contiguous()                   # this rank's sequences' new queries
     dout5 = torch.empty((len(mine), c5["H"], c5["dh"]), dtype=torch.bfloat16, device=dev)
     split5 = 8
 
     def step5():
-        return SH.decode_sharded(q5d, lens, lambda ii: D.decode(q5d[idx], kv, split_blocks=split5, out=dout5,
-                                                                check=False))
+        return SH.decode_sharded(q5d, lens, lambda ii: D.decode(q5m, kv, split_blocks=split5, out=dout5, check=False),
+                                 plan=plan5)
 
     r5 = step5()
     torch.cuda.synchronize()
     A.check_device_errors(dev)
     t5 = max_over_ranks(timer(step5, args.steps, args.warmup))
-    t5_local = max_over_ranks(timer(lambda: D.decode(q5d[idx], kv, split_blocks=split5, out=dout5, check=False),
+    t5_local = max_over_ranks(timer(lambda: D.decode(q5m, kv, split_blocks=split5, out=dout5, check=False),
                                     args.steps, 1))
     clk.stop()
     bytes5 = int(lens.sum()) * c5["KVH"] * c5["dh"] * 2

@@ -252,26 +252,42 @@ def prefill_sharded(query, key, value, sink=False, compute=None, group=None, chu
                                 group=group, compute=fn, chunk=chunk)
 
 
-def decode_sharded(q, lengths, decode_local, group=None):
+class DecodePartition:
+    """The sequence partition of a decode batch over the ranks, with the index tensors its row
+    gather needs (built once per batch layout, reused every step).
+
+    parts[r]: the sequences rank r decodes (sorted); mine = parts[rank]; the gathered buffer holds
+    nmax rows per rank, and row r * nmax + i of it is sequence parts[r][i]."""
+
+    def __init__(self, lengths, world, rank, device=None):
+        self.world, self.rank = world, rank
+        self.parts = partition_sequences(lengths, world)
+        self.mine = self.parts[rank]
+        self.nmax = max(len(p) for p in self.parts)
+        src = [r * self.nmax + i for r, p in enumerate(self.parts) for i in range(len(p))]
+        dst = [b for p in self.parts for b in p]
+        self.src = torch.tensor(src, dtype=torch.long, device=device)
+        self.dst = torch.tensor(dst, dtype=torch.long, device=device)
+        self.mine_idx = torch.tensor(self.mine, dtype=torch.long, device=device)
+
+
+def decode_sharded(q, lengths, decode_local, group=None, plan=None):
     """Decode rows for all sequences, each rank computing its partition.
 
     q [B, H, dh]; lengths: host sequence of KV lengths; decode_local(indices) -> [len(indices),
-    H, dh] computes the rows of those sequences on this rank.  Returns [B, H, dh] everywhere."""
+    H, dh] computes the rows of those sequences on this rank.  plan: a DecodePartition of these
+    lengths (made here when None).  Returns [B, H, dh] everywhere."""
     world, rank = _world(group)
-    parts = partition_sequences(lengths, world)
-    mine = parts[rank]
-    out_local = decode_local(mine) if mine else q.new_empty((0,) + tuple(q.shape[1:]))
+    if plan is None:
+        plan = DecodePartition(lengths, world, rank, q.device)
+    out_local = decode_local(plan.mine) if plan.mine else q.new_empty((0,) + tuple(q.shape[1:]))
     if world == 1:
         return out_local
     # pad to the largest partition so the gather has equal sizes
-    nmax = max(len(p) for p in parts)
-    pad = q.new_zeros((nmax,) + tuple(q.shape[1:]))
-    pad[:len(mine)] = out_local
-    gathered = torch.empty((world * nmax,) + tuple(pad.shape[1:]), dtype=pad.dtype, device=pad.device)
+    pad = q.new_zeros((plan.nmax,) + tuple(q.shape[1:]))
+    pad[:len(plan.mine)] = out_local
+    gathered = torch.empty((world * plan.nmax,) + tuple(pad.shape[1:]), dtype=pad.dtype, device=pad.device)
     dist.all_gather_into_tensor(gathered, pad, group=group)
-    gathered = gathered.view((world,) + tuple(pad.shape))
     out = q.new_empty(q.shape)
-    for r, p in enumerate(parts):
-        if p:
-            out[torch.tensor(p, device=q.device)] = gathered[r][:len(p)]
+    out[plan.dst] = gathered[plan.src]
     return out
