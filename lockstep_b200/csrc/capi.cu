@@ -250,9 +250,10 @@ int launch_decode_tc_t(const DecodeArgs& a, int max_splits, int num_sms, cudaStr
   auto kfn = decode_tc_kernel<SINK, OutT, GQ>;
   if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return kErrCuda;
   (void)max_splits;     // exact block partials: the streaming kernel schedules blocks, not splits
+  // the live block count is known on the device only; the grid covers the most there can be
   const long long chunks = ((long long)a.B * a.KVH * a.max_blocks + kDecChunk - 1) / kDecChunk;
   const int grid = (int)std::min<long long>(chunks, 2LL * std::max(num_sms, 1));   // two CTAs per SM
-  if ((rc = launch_pdl(kfn, dim3(grid), dim3(kDecThreads), smem, st, tk, tq, a))) return rc;
+  if ((rc = launch_pdl(kfn, dim3(grid), dim3(DecWorkers<GQ>::kThreads), smem, st, tk, tq, a))) return rc;
   return launch_pdl(decode_merge_kernel<SINK, OutT>, dim3(a.KVH, a.B, a.group), dim3(kMergeThreads), 0, st, a);
 }
 
@@ -304,7 +305,7 @@ PrefillWs prefill_ws(int B, int H, int KVH, int T, int dh) {
 }
 
 struct DecodeWs {
-  size_t q8, eq, partA, partM, tickets, total;
+  size_t q8, eq, partA, partM, tickets, blk_off, total;
 };
 
 DecodeWs decode_ws(int B, int H, int KVH, int dh, int max_blocks) {
@@ -316,6 +317,7 @@ DecodeWs decode_ws(int B, int H, int KVH, int dh, int max_blocks) {
   w.partA = o; o += align256((size_t)B * KVH * max_blocks * gq * dh * 4);
   w.partM = o; o += align256((size_t)B * KVH * max_blocks * gq * 16);
   w.tickets = o; o += align256((size_t)B * KVH * 4);
+  w.blk_off = o; o += align256((size_t)(B + 1) * 4);         // the live-block plan
   w.total = o + 256;
   return w;
 }
@@ -706,9 +708,16 @@ int lssab8_decode(const void* q, int dtype, const int64_t* qs, int B, int H, int
   int32_t* eq = reinterpret_cast<int32_t*>(base + w.eq);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int64_t q4[4] = {qs[0], qs[1], 0, qs[2]};
-  // (the ticket reset comes first so the query quantiser directly precedes the decode kernel,
-  // which may then start under programmatic dependent launch)
-  if (cudaMemsetAsync(base + w.tickets, 0, (size_t)B * KVH * 4, s) != cudaSuccess) return kErrCuda;
+  // (the ticket reset and the plan come first so the query quantiser directly precedes the
+  // decode kernel, which may then start under programmatic dependent launch)
+  if (dh == 128) {                                   // the live-block plan; it also zeroes the tickets
+    decode_plan_kernel<<<1, kPlanThreads, 0, s>>>(seq_lens, B, max_blocks, max_pages,
+                                                  reinterpret_cast<int*>(base + w.blk_off),
+                                                  reinterpret_cast<unsigned int*>(base + w.tickets), B * KVH, ds->err);
+    if ((rc = launch_rc())) return rc;
+  } else if (cudaMemsetAsync(base + w.tickets, 0, (size_t)B * KVH * 4, s) != cudaSuccess) {
+    return kErrCuda;
+  }
   if ((rc = lssab8_quant_rows(q, dtype, B, H, 1, dh, q4, 1, q8, eq, stream))) return rc;
   DecodeArgs a{};
   a.B = B; a.H = H; a.KVH = KVH; a.dh = dh; a.group = H / KVH; a.max_blocks = max_blocks; a.max_pages = max_pages;
@@ -717,6 +726,7 @@ int lssab8_decode(const void* q, int dtype, const int64_t* qs, int B, int H, int
   a.partA = reinterpret_cast<int32_t*>(base + w.partA);
   a.partM = reinterpret_cast<int4*>(base + w.partM);
   a.tickets = reinterpret_cast<unsigned int*>(base + w.tickets);
+  a.blk_off = reinterpret_cast<int*>(base + w.blk_off);
   a.out = out; a.os0 = os[0]; a.os1 = os[1]; a.os2 = os[2];
   a.gbase = gbase_of(dh);
   a.err = ds->err;
@@ -774,8 +784,16 @@ int lssab8_decode_noalloc(const void* q, int dtype, const int64_t* qs, int B, in
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int64_t q4[4] = {qs[0], qs[1], 0, qs[2]};
   // the tickets must start at zero (the buffer keeps whatever the previous call left); the reset
-  // comes first, as in lssab8_decode, so the query quantiser directly precedes the decode kernel
-  if (cudaMemsetAsync(base + w.tickets, 0, (size_t)B * KVH * 4, s) != cudaSuccess) return kErrCuda;
+  // and the plan come first, as in lssab8_decode, so the query quantiser directly precedes the
+  // decode kernel
+  if (dh == 128) {                                   // the live-block plan; it also zeroes the tickets
+    decode_plan_kernel<<<1, kPlanThreads, 0, s>>>(seq_lens, B, max_blocks, max_pages,
+                                                  reinterpret_cast<int*>(base + w.blk_off),
+                                                  reinterpret_cast<unsigned int*>(base + w.tickets), B * KVH, ds->err);
+    if ((rc = launch_rc())) return rc;
+  } else if (cudaMemsetAsync(base + w.tickets, 0, (size_t)B * KVH * 4, s) != cudaSuccess) {
+    return kErrCuda;
+  }
   if ((rc = lssab8_quant_rows(q, dtype, B, H, 1, dh, q4, 1, q8, eq, stream))) return rc;
   DecodeArgs a{};
   a.B = B; a.H = H; a.KVH = KVH; a.dh = dh; a.group = H / KVH; a.max_blocks = max_blocks; a.max_pages = max_pages;
@@ -784,6 +802,7 @@ int lssab8_decode_noalloc(const void* q, int dtype, const int64_t* qs, int B, in
   a.partA = reinterpret_cast<int32_t*>(base + w.partA);
   a.partM = reinterpret_cast<int4*>(base + w.partM);
   a.tickets = reinterpret_cast<unsigned int*>(base + w.tickets);
+  a.blk_off = reinterpret_cast<int*>(base + w.blk_off);
   a.out = out; a.os0 = os[0]; a.os1 = os[1]; a.os2 = os[2];
   a.gbase = gbase_of(dh);
   a.err = ds->err;

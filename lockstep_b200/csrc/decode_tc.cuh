@@ -5,10 +5,12 @@
 // the last CTA of a (sequence, kv head) refolds all blocks in ascending order
 // (reference/lssab8_golden.py:350-394).  What changes is how the partials are produced:
 //
-//   * persistent CTAs walk the (sequence, kv head, block) list in interleaved chunks of
-//     kDecChunk blocks as ONE stream (block partials are exact, so where a split or chunk ends
-//     changes no bit): the TMA ring never drains, the one-block lag of the partial readout runs
-//     across chunk boundaries, and Q is reloaded only when (sequence, kv head) changes;
+//   * persistent CTAs walk the list of LIVE (sequence, kv head, block) triples -- numbered by a
+//     per-sequence prefix sum of block counts (decode_plan_kernel), so ragged lengths leave no
+//     dead work to skip and every CTA gets an even share -- in interleaved chunks of kDecChunk
+//     blocks as ONE stream (block partials are exact, so where a split or chunk ends changes no
+//     bit): the TMA ring never drains, the one-block lag of the partial readout runs across chunk
+//     boundaries, and Q is reloaded only when (sequence, kv head) changes;
 //   * warp 0 (one thread) streams each block's 8 key pages with cp.async.bulk.tensor (the tensor
 //     map swizzles them into the SW128 K-major layout) and its 8 transposed value pages with
 //     plain cp.async.bulk into a kDecStages-deep ring (no multicast);
@@ -18,8 +20,10 @@
 //       A^T[ch, head]  = V_b^T[128 x 128] . P^T   (s8 x u8; a value page [ch][16 keys] is exactly
 //                                                  8-row x 16-byte core matrices, so V^T is read
 //                                                  in place with no swizzle: LBO = one page)
-//   * warps 2-5 (128 threads, thread = TMEM lane = key for S, channel for A) compute the block
-//     max per head (redux.sync + one named barrier), NB, the 32-bit chain and the T2 gather from a
+//   * worker warpgroups (128 threads each, thread = TMEM lane = key for S, channel for A; one
+//     warpgroup for a group of <= 4 heads, two -- heads 0-3 and 4-7 -- for a group of 8, so the
+//     per-block path does not lengthen with the group) compute the block max per head (redux.sync
+//     + one named barrier per warpgroup), NB, the 32-bit chain and the T2 gather from a
 //     zero-padded table indexed by d >> 19, write P^T in the core-matrix layout, sum l_b with
 //     redux.sync and shared atomics, and store the partials.
 //   * the refold of each (sequence, kv head) runs afterwards as its own small kernel
@@ -31,7 +35,12 @@ namespace lssab8 {
 
 constexpr int kDecStages = 3;                      // two CTAs per SM, three stages each
 constexpr int kDecTab = 1168;                      // T2 entries 0..1152 (1152 = 0), 16-byte padded
-constexpr int kDecThreads = 192;   // warp 0 TMA, warp 1 MMA + TMEM, warps 2-5 workers
+// warp 0 TMA, warp 1 MMA + TMEM, then one worker warpgroup per 4 heads of the group
+template <int GQ> struct DecWorkers {
+  static constexpr int kGroups = GQ > 4 ? 2 : 1;     // warpgroups
+  static constexpr int kHeads = GQ / kGroups;        // heads per warpgroup (4)
+  static constexpr int kThreads = 64 + 128 * kGroups;
+};
 constexpr uint32_t kDecTmemCols = 64;
 
 struct DecTcSmem {
@@ -57,46 +66,100 @@ enum DecBar : int {
 
 constexpr int kDecChunk = 8;                       // blocks per scheduling chunk
 
-// The CTA's walk over the virtual block list v = (b * KVH + g) * max_blocks + blk, in chunks of
-// kDecChunk: chunks blockIdx.x, blockIdx.x + gridDim.x, ...  Blocks past a sequence's end are
-// skipped, and so is every block of a sequence the lattice arrays are too short for (flagged by
-// the workers).  Every role runs its own copy and sees the same sequence of blocks.
+// The CTA's walk over the live block list: v = KVH * off[b] + g * nblk_b + blk for blk < nblk_b
+// (off = the plan's prefix sum of live block counts, nblk_b = off[b + 1] - off[b]), in chunks of
+// kDecChunk: chunks blockIdx.x, blockIdx.x + gridDim.x, ...  A CTA's v only grows, so the
+// sequence of v is found by advancing one cursor over off (each CTA reads off once).  Sequences
+// the plan found too long for the lattice arrays have no live blocks (and are flagged there).
+// Every role runs its own copy and sees the same sequence of blocks.
 struct DecIter {
   int v, vend, chunk, nchunks, total;
-  int cur_b, L;
-  bool bad;
+  int cur_b, lo, hi, nb, L;                        // this sequence's live range [lo, hi) of v
   __device__ __forceinline__ void init(const DecodeArgs& p) {
-    total = p.B * p.KVH * p.max_blocks;
+    total = p.KVH * __ldg(&p.blk_off[p.B]);
     nchunks = (total + kDecChunk - 1) / kDecChunk;
     chunk = blockIdx.x;
     v = chunk * kDecChunk;
     vend = min(v + kDecChunk, total);
-    cur_b = -1;
-    L = 0;
-    bad = false;
+    cur_b = 0;
+    lo = 0;
+    nb = __ldg(&p.blk_off[1]);
+    hi = p.KVH * nb;
+    L = __ldg(&p.seq_lens[0]);
   }
   __device__ __forceinline__ bool next(const DecodeArgs& p, int& b, int& g, int& blk) {
-    for (;;) {
-      if (v >= vend) {
-        chunk += gridDim.x;
-        if (chunk >= nchunks) return false;
-        v = chunk * kDecChunk;
-        vend = min(v + kDecChunk, total);
-      }
-      const int vv = v++;
-      blk = vv % p.max_blocks;
-      const int bg = vv / p.max_blocks;
-      g = bg % p.KVH;
-      b = bg / p.KVH;
-      if (b != cur_b) {
-        cur_b = b;
-        L = p.seq_lens[b];
-        bad = ((L + kKB - 1) / kKB > p.max_blocks) || ((L + 15) / 16 > p.max_pages);
-      }
-      if (L > 0 && blk * kKB < L && !bad) return true;
+    if (v >= vend) {
+      chunk += gridDim.x;
+      if (chunk >= nchunks) return false;
+      v = chunk * kDecChunk;
+      vend = min(v + kDecChunk, total);
     }
+    while (v >= hi) {                              // v < total, so some later sequence holds it
+      ++cur_b;
+      lo = hi;
+      nb = __ldg(&p.blk_off[cur_b + 1]) - __ldg(&p.blk_off[cur_b]);
+      hi = lo + p.KVH * nb;
+      L = __ldg(&p.seq_lens[cur_b]);
+    }
+    const int r = v++ - lo;
+    b = cur_b;
+    g = r / nb;
+    blk = r - g * nb;
+    return true;
   }
 };
+
+// The live-block plan: blk_off[b] = the number of live 128-key blocks of the sequences before b
+// (blk_off[B] = all of them), one CTA, which also zeroes the refold's tickets[0 .. nticket).  A
+// sequence is live when 0 < L and its blocks and pages fit the lattice arrays; one that does not
+// fit gets no blocks and sets kDevBadPage.
+constexpr int kPlanThreads = 1024;
+__global__ void __launch_bounds__(kPlanThreads) decode_plan_kernel(const int32_t* seq_lens, int B, int max_blocks,
+                                                                    int max_pages, int* blk_off, unsigned int* tickets,
+                                                                    int nticket, int* err) {
+  __shared__ int warp_sums[kPlanThreads / 32];
+  __shared__ int carry;
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  for (int i = tid; i < nticket; i += kPlanThreads) tickets[i] = 0u;
+  if (tid == 0) carry = 0;
+  __syncthreads();
+  for (int base = 0; base < B; base += kPlanThreads) {
+    const int i = base + tid;
+    int nb = 0;
+    if (i < B) {
+      const int L = seq_lens[i];
+      nb = L > 0 ? (L + kKB - 1) / kKB : 0;
+      if (nb > max_blocks || (L + 15) / 16 > max_pages) {
+        nb = 0;
+        atomicOr(err, kDevBadPage);
+      }
+    }
+    int x = nb;                                    // inclusive warp scan
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) warp_sums[w] = x;
+    __syncthreads();
+    if (w == 0) {
+      int ws = warp_sums[lane];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, ws, o);
+        if (lane >= o) ws += y;
+      }
+      warp_sums[lane] = ws;                        // inclusive over warps
+    }
+    __syncthreads();
+    const int before = carry + (w > 0 ? warp_sums[w - 1] : 0) + x - nb;
+    if (i < B) blk_off[i] = before;
+    __syncthreads();
+    if (tid == 0) carry += warp_sums[kPlanThreads / 32 - 1];
+    __syncthreads();
+  }
+  if (tid == 0) blk_off[B] = carry;
+}
 
 __device__ __forceinline__ uint32_t redux_max_s32(int v) {
   int r;
@@ -111,11 +174,14 @@ __device__ __forceinline__ uint32_t redux_add_u32(uint32_t v) {
 
 // GQ = compile-time bound on the GQA group (4: exactly 4 heads; 8: any group <= 8, masked).
 template <bool SINK, typename OutT, int GQ>
-__global__ void __launch_bounds__(kDecThreads, 2)
+__global__ void __launch_bounds__(DecWorkers<GQ>::kThreads, 2)
 decode_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_q,
                  const DecodeArgs p) {
   using L = DecTcSmem;
+  using WK = DecWorkers<GQ>;
   constexpr int DH = 128;
+  constexpr int kWorkers = 128 * WK::kGroups;
+  constexpr int GH = WK::kHeads;                       // heads per worker warpgroup
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
@@ -136,9 +202,9 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
     for (int s = 0; s < kDecStages; ++s) { mbar_init(&bars[kDFull + s], 1); mbar_init(&bars[kDEmpty + s], 1); }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&bars[kDQFull + s], 1);  mbar_init(&bars[kDQEmpty + s], 1);
-      mbar_init(&bars[kDSFull + s], 1);  mbar_init(&bars[kDSEmpty + s], 128);
-      mbar_init(&bars[kDPFull + s], 128); mbar_init(&bars[kDPEmpty + s], 1);
-      mbar_init(&bars[kDAFull + s], 1);  mbar_init(&bars[kDAEmpty + s], 128);
+      mbar_init(&bars[kDSFull + s], 1);  mbar_init(&bars[kDSEmpty + s], kWorkers);
+      mbar_init(&bars[kDPFull + s], kWorkers); mbar_init(&bars[kDPEmpty + s], 1);
+      mbar_init(&bars[kDAFull + s], 1);  mbar_init(&bars[kDAEmpty + s], kWorkers);
     }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -153,7 +219,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   pdl_launch_dependents();                             // the refold kernel may queue up behind us
-  pdl_wait();                                          // the query quantiser's q8 / eq are complete
+  pdl_wait();                                          // the plan and the query quantiser are complete
 
   if (warp == 0) {
     // ================================================================ TMA producer
@@ -243,14 +309,20 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
     }
   } else {
     // ================================================================ workers
+    // Warpgroup wg (warps 2 + 4 wg .. 5 + 4 wg) owns heads [wg * GH, wg * GH + GH) of the group;
+    // thread t of a warpgroup is TMEM lane t: key t of S, channel t of A.  The warpgroups meet
+    // only on the pipeline barriers (which count every worker thread), never on each other.
+    const int wg = (warp - 2) >> 2;
     const int wq = warp & 3;
     const int t = wq * 32 + lane;                        // TMEM lane: key (S) / channel (A)
+    const int h0 = wg * GH;                              // first head of this warpgroup
+    const int bar_id = 1 + wg;                           // this warpgroup's named barrier
     const uint32_t lanebase = tmem + ((uint32_t)(wq * 32) << 16);
     DecIter itr;
     itr.init(p);
     int jj = 0, cur_bg = -1, b, g, blk;
     bool bad = false;                                    // this warp gave up a wait (decided at a barrier)
-    int eqh[GQ];
+    int eqh[GH];
     // the previous block: its A partial is read out one block later, its M after the next barrier
     bool have_prev = false;
     long long prev_bg = 0;
@@ -260,23 +332,24 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
       const bool okw = warp_poll(&bars[kDAFull + ab], (jb >> 1) & 1, abort_flag, p.err);
       if (okw) {
         tc_fence_after();
-        uint32_t a[8];
-        tmem_ld8(lanebase + 32 + ab * 16, a);
+        uint32_t a[GH];
+        tmem_ld4(lanebase + 32 + ab * 16 + h0, a);
         tc_wait_ld();
         tc_fence_before();
         mbar_arrive(&bars[kDAEmpty + ab]);
         int32_t* dstA = p.partA + ((bgx * p.max_blocks + blkx) * gq) * DH;
 #pragma unroll
-        for (int h = 0; h < GQ; ++h) if (h < gq) __stcg(dstA + h * DH + t, (int32_t)a[h]);
+        for (int hh = 0; hh < GH; ++hh) if (h0 + hh < gq) __stcg(dstA + (h0 + hh) * DH + t, (int32_t)a[hh]);
       }
       return okw;
     };
     auto write_M = [&](int jb, long long bgx, int blkx, int Lx) {   // after a barrier that follows jb's atomics
       const int par = jb & 1;
-      if (t < gq) {
-        const int e0 = (SINK && blkx == 0 && Lx > 1) ? eh0s[par * 8 + t] : 0;
-        __stcg(&p.partM[(bgx * p.max_blocks + blkx) * gq + t], make_int4(nbs[par * 8 + t], (int)lbsum[par * 8 + t], e0, 0));
-        lbsum[par * 8 + t] = 0u;
+      const int h = h0 + t;
+      if (t < GH && h < gq) {
+        const int e0 = (SINK && blkx == 0 && Lx > 1) ? eh0s[par * 8 + h] : 0;
+        __stcg(&p.partM[(bgx * p.max_blocks + blkx) * gq + h], make_int4(nbs[par * 8 + h], (int)lbsum[par * 8 + h], e0, 0));
+        lbsum[par * 8 + h] = 0u;
       }
     };
     while (itr.next(p, b, g, blk)) {
@@ -284,16 +357,16 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
       if (bg != cur_bg) {
         cur_bg = bg;
 #pragma unroll
-        for (int h = 0; h < GQ; ++h) eqh[h] = (h < gq) ? p.eq[(long long)b * p.H + g * gq + h] : 0;
+        for (int hh = 0; hh < GH; ++hh) eqh[hh] = (h0 + hh < gq) ? p.eq[(long long)b * p.H + g * gq + h0 + hh] : 0;
       }
       const int Lb = itr.L;
       const int sb = jj & 1, par = jj & 1;
       const int ekb = p.ek[bg * p.max_blocks + blk];
       bool okw = warp_poll(&bars[kDSFull + sb], (jj >> 1) & 1, abort_flag, p.err);
-      int S[8];
+      int S[GH];
       if (okw) {
         tc_fence_after();
-        tmem_ld8(lanebase + sb * 16, reinterpret_cast<uint32_t*>(S));
+        tmem_ld4(lanebase + sb * 16 + h0, reinterpret_cast<uint32_t*>(S));
         tc_wait_ld();
         tc_fence_before();
         mbar_arrive(&bars[kDSEmpty + sb]);
@@ -301,52 +374,54 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
       const int nkeys = min(kKB, Lb - blk * kKB);
       if (t >= nkeys) {
 #pragma unroll
-        for (int h = 0; h < 8; ++h) S[h] = INT32_MIN;  // keys past the sequence end
+        for (int hh = 0; hh < GH; ++hh) S[hh] = INT32_MIN;  // keys past the sequence end
       }
 #pragma unroll
-      for (int h = 0; h < GQ; ++h) {
-        const int wm = (int)redux_max_s32(S[h]);
-        if (lane == 0) redmax[(par * 4 + wq) * 8 + h] = wm;
+      for (int hh = 0; hh < GH; ++hh) {
+        const int wm = (int)redux_max_s32(S[hh]);
+        if (lane == 0) redmax[(par * 4 + wq) * 8 + h0 + hh] = wm;
       }
-      uint32_t Gh[GQ];
-      int dmh[GQ];
+      uint32_t Gh[GH];
+      int dmh[GH];
 #pragma unroll
-      for (int h = 0; h < GQ; ++h) {                    // independent of the block max: before the barrier
-        Gh[h] = g_fold(p.gbase, eqh[h] + ekb);
-        dmh[h] = 1 << max(0, 30 - (31 - __clz((int)Gh[h])));
+      for (int hh = 0; hh < GH; ++hh) {                  // independent of the block max: before the barrier
+        Gh[hh] = g_fold(p.gbase, eqh[hh] + ekb);
+        dmh[hh] = 1 << max(0, 30 - (31 - __clz((int)Gh[hh])));
       }
-      // every worker meets here once per block; the OR makes giving up a group decision
-      if (bar_any(1, 128, bad || !okw || *abort_flag != 0)) { have_prev = false; break; }
+      // the warpgroup meets here once per block; the OR makes giving up a group decision
+      if (bar_any(bar_id, 128, bad || !okw || *abort_flag != 0)) { have_prev = false; break; }
       if (have_prev) write_M(jj - 1, prev_bg, prev_blk, prev_L);   // the previous block's l_b atomics are complete
-      uint32_t e[GQ];
+      uint32_t e[GH];
 #pragma unroll
-      for (int h = 0; h < GQ; ++h) {
+      for (int hh = 0; hh < GH; ++hh) {
+        const int h = h0 + hh;
         const int m = max(max(redmax[(par * 4 + 0) * 8 + h], redmax[(par * 4 + 1) * 8 + h]),
                           max(redmax[(par * 4 + 2) * 8 + h], redmax[(par * 4 + 3) * 8 + h]));
-        const uint32_t G = Gh[h];
+        const uint32_t G = Gh[hh];
         const int nbv = nb_of(m, G);
-        const int sc = max(S[h], m - dmh[h]);
+        const int sc = max(S[hh], m - dmh[hh]);
         const uint32_t d = ((uint32_t)nbv << kBHI) + (uint32_t)sc * (0u - G);
-        e[h] = (h < gq && t < nkeys) ? (uint32_t)tab[min(d >> kIdxShift, (uint32_t)kTabLive)] : 0u;
+        e[hh] = (h < gq && t < nkeys) ? (uint32_t)tab[min(d >> kIdxShift, (uint32_t)kTabLive)] : 0u;
         if (t == 0) nbs[par * 8 + h] = nbv;
       }
       const bool key0 = SINK && blk == 0 && t == 0 && Lb > 1;
       if (key0) {                                        // key 0's weight stays out of the P operand
 #pragma unroll
-        for (int h = 0; h < GQ; ++h) eh0s[par * 8 + h] = (int)e[h];
+        for (int hh = 0; hh < GH; ++hh) eh0s[par * 8 + h0 + hh] = (int)e[hh];
       }
       // P^T[head][key] in 8-head x 16-key core matrices: (key / 16) * 256 + (h / 8) * 128 + (h % 8) * 16 + key % 16
       if (!warp_poll(&bars[kDPEmpty + par], ((jj >> 1) & 1) ^ 1, abort_flag, p.err)) bad = true;
       uint8_t* pd = smem + L::kP + par * 2048 + (t >> 4) * 256 + (t & 15);
 #pragma unroll
-      for (int h = 0; h < GQ; ++h) {                     // rows >= gq of P^T only feed ignored columns of A
-        if (h < gq) pd[(h >> 3) * 128 + (h & 7) * 16] = (uint8_t)(key0 ? 0u : e[h]);
+      for (int hh = 0; hh < GH; ++hh) {                  // rows >= gq of P^T only feed ignored columns of A
+        const int h = h0 + hh;
+        if (h < gq) pd[(h >> 3) * 128 + (h & 7) * 16] = (uint8_t)(key0 ? 0u : e[hh]);
       }
 #pragma unroll
-      for (int h = 0; h < GQ; ++h) {
-        if (h < gq) {
-          const uint32_t sum = redux_add_u32(e[h]);
-          if (lane == 0) atomicAdd(&lbsum[par * 8 + h], sum);
+      for (int hh = 0; hh < GH; ++hh) {
+        if (h0 + hh < gq) {
+          const uint32_t sum = redux_add_u32(e[hh]);
+          if (lane == 0) atomicAdd(&lbsum[par * 8 + h0 + hh], sum);
         }
       }
       fence_async_smem();
@@ -359,15 +434,9 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
       ++jj;
     }
     // the last block: its l_b atomics meet at one more barrier, then its partials
-    if (have_prev && !bar_any(1, 128, bad || *abort_flag != 0)) {
+    if (have_prev && !bar_any(bar_id, 128, bad || *abort_flag != 0)) {
       write_M(jj - 1, prev_bg, prev_blk, prev_L);
       readout_A(jj - 1, prev_bg, prev_blk);
-    }
-    if (t == 0) {                                        // sequences the lattice arrays are too short for
-      for (int bb = blockIdx.x; bb < p.B; bb += gridDim.x) {
-        const int Lx = p.seq_lens[bb];
-        if ((Lx + kKB - 1) / kKB > p.max_blocks || (Lx + 15) / 16 > p.max_pages) atomicOr(p.err, kDevBadPage);
-      }
     }
   }
 
@@ -408,7 +477,7 @@ __global__ void __launch_bounds__(kMergeThreads) decode_merge_kernel(const Decod
   const int gq = p.group;
   const int L = p.seq_lens[b];
   const int nblk = (L + kKB - 1) / kKB;
-  if (L <= 0 || nblk > p.max_blocks || (L + 15) / 16 > p.max_pages) return;   // flagged by the stream kernel
+  if (L <= 0 || nblk > p.max_blocks || (L + 15) / 16 > p.max_pages) return;   // flagged by the plan
   const long long bg = (long long)b * p.KVH + g;
   int v0c = 0, evs0 = 0, eh0 = 0;
   if (SINK && L > 1 && c < DH) {
