@@ -70,6 +70,12 @@ int lssab8_device_errors(int clear, void* stream, int* bits);
 int lssab8_quant_rows(const void* x, int dtype, int B, int H, int T, int dh, const int64_t* xs, int Tpad,
                       int8_t* q8, int32_t* eq, void* stream);
 
+/* P1 with one exponent per head (the golden's q_exp_mode "head", reference/lssab_golden.py:
+ * 230-232): the row rule applied to all T rows and dh channels of a head at once.  Same layout
+ * as lssab8_quant_rows; eq[b, h, t] holds the head's exponent for every t < T. */
+int lssab8_quant_heads(const void* x, int dtype, int B, int H, int T, int dh, const int64_t* xs, int Tpad,
+                       int8_t* q8, int32_t* eq, void* stream);
+
 /* P2/P3: per-(128-key block, kv head) quantiser.  x [B, KVH, T, dh] -> x8 [B, KVH, Tpad, dh],
  * e [B, KVH, ceil(T/128)], e0 [B, KVH] (mode 2 only).  mode 0 = B8 grid
  * (reference/lssab_torch.py:62-85), 1 = B9 value grid (reference/lssab9_torch.py:46-65,158),
@@ -96,6 +102,18 @@ int lssab8_prefill_lattice(const int8_t* q8, const int32_t* eq, const int8_t* k8
                            const int8_t* v8, const int32_t* ev, const int32_t* ev0, int B, int H, int KVH, int T,
                            int dh, int Tpad, float* orow_scratch, void* out, int out_dtype, const int64_t* os,
                            void* stream);
+
+/* The general form of lssab8_prefill_lattice, for the golden entry points
+ * (reference/lssab8_golden.py:341-346 lssab8_attention(..., causal, key_valid),
+ * reference/lssab9_golden.py:254-259 lssab9_attention): causal = 0 lets every query row see
+ * every key; key_mask [B, Tpad / 32] uint32 words (bit j % 32 of word j / 32 of batch element b
+ * set: key j is visible to every row of b; bits of keys >= T must be clear) is required.  A row
+ * that sees no key of a block skips it, a row that sees no key at all yields 0, exactly as the
+ * golden's visibility rule (reference/lssab8_golden.py:241-247).  out float32 [b, t, h, c]. */
+int lssab8_prefill_lattice_general(const int8_t* q8, const int32_t* eq, const int8_t* k8, const int32_t* ek,
+                                   const int8_t* v8, const int32_t* ev, const int32_t* ev0, int B, int H, int KVH,
+                                   int T, int dh, int Tpad, int causal, const uint32_t* key_mask, float* out,
+                                   const int64_t* os, void* stream);
 
 /* Block-aligned chunked prefill on an append-only lattice: query rows [T0, T) of a sequence
  * (T0 a multiple of 128) against keys [0, T).  q8/eq hold the chunk's rows only, quantised per

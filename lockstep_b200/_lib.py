@@ -15,8 +15,8 @@ DEV_EV_RANGE, DEV_TIMEOUT, DEV_BAD_PAGE = 1, 2, 4
 # every symbol include/lssab8.h declares (tests check the library exports each one)
 SYMBOLS = (
     "lssab8_version", "lssab8_strerror", "lssab8_device_errors",
-    "lssab8_quant_rows", "lssab8_quant_blocks", "lssab8_quant_keys_offset",
-    "lssab8_prefill_lattice", "lssab8_prefill_chunk_lattice", "lssab8_prefill_workspace_size", "lssab8_prefill",
+    "lssab8_quant_rows", "lssab8_quant_heads", "lssab8_quant_blocks", "lssab8_quant_keys_offset",
+    "lssab8_prefill_lattice", "lssab8_prefill_lattice_general", "lssab8_prefill_chunk_lattice", "lssab8_prefill_workspace_size", "lssab8_prefill",
     "lssab8_prefill_peers", "lssab8_peer_export", "lssab8_peer_import", "lssab8_peer_close",
     "lssab8_decode_prep_kv", "lssab8_decode_workspace_size", "lssab8_decode",
     "lssab8_decode_noalloc", "lssab8_selftest_div", "lssab8_selftest_rescale", "lssab8_selftest_timeout",
@@ -46,7 +46,9 @@ def load():
     L.lssab8_strerror.restype = ctypes.c_char_p
     L.lssab8_device_errors.argtypes = [I, P, ctypes.POINTER(I)]
     L.lssab8_quant_rows.argtypes = [P, I, I, I, I, I, PI64, I, P, P, P]
+    L.lssab8_quant_heads.argtypes = [P, I, I, I, I, I, PI64, I, P, P, P]
     L.lssab8_quant_blocks.argtypes = [P, I, I, I, I, I, PI64, I, I, P, P, P, P]
+    L.lssab8_prefill_lattice_general.argtypes = [P] * 7 + [I] * 7 + [P, P, PI64, P]
     L.lssab8_quant_keys_offset.argtypes = [P, I, I, I, I, I, PI64, I, P, P, P, P]
     L.lssab8_prefill_lattice.argtypes = [P] * 7 + [I] * 6 + [P, P, I, PI64, P]
     L.lssab8_prefill_chunk_lattice.argtypes = [P] * 7 + [I] * 6 + [P, P, I, PI64, P]

@@ -79,6 +79,50 @@ def quant_rows(x, Tpad=None):
     return q8, eq
 
 
+def quant_heads(x, Tpad=None):
+    """P1 with one exponent per head (q_exp_mode "head"): x [B, H, T, dh] -> (q8 [B, H, Tpad, dh],
+    eq [B, H, Tpad] holding the head's exponent on every row)."""
+    dev = _require_cuda(x)
+    B, H, T, dh = x.shape
+    Tp = tpad(T) if Tpad is None else Tpad
+    q8 = torch.empty((B, H, Tp, dh), dtype=torch.int8, device=dev)
+    eq = torch.empty((B, H, Tp), dtype=torch.int32, device=dev)
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().lssab8_quant_heads(x.data_ptr(), dtype_code(x.dtype), B, H, T, dh, _lib.i64x(x.stride()),
+                                                  Tp, q8.data_ptr(), eq.data_ptr(), _stream_handle(dev)),
+                   "lssab8_quant_heads")
+    return q8, eq
+
+
+def key_mask_words(key_valid, B, T, device):
+    """The general kernel's key mask: [B, Tpad / 32] int32 words, bit j % 32 of word j / 32 set when
+    key j < T is visible.  key_valid: None (every key), [T] or [B, T] bool."""
+    Tp = tpad(T)
+    kv = torch.zeros((B, Tp), dtype=torch.bool, device=device)
+    if key_valid is None:
+        kv[:, :T] = True
+    else:
+        kv[:, :T] = torch.as_tensor(key_valid, dtype=torch.bool, device=device).reshape(-1, T).expand(B, T)
+    w = torch.arange(32, device=device, dtype=torch.int64)
+    words = (kv.view(B, Tp // 32, 32).to(torch.int64) << w).sum(-1)       # < 2^32
+    return torch.where(words >= 2 ** 31, words - 2 ** 32, words).to(torch.int32).contiguous()   # same bits
+
+
+def prefill_lattice_general(q8, eq, k8, ek, v8, ev, ev0, T, causal, kmask):
+    """The general prefill on a prepared lattice (causal flag, key mask words from key_mask_words):
+    returns float32 out [B, T, H, dh]."""
+    dev = _require_cuda(q8, eq, k8, ek, v8, ev, kmask)
+    B, H, Tp, dh = q8.shape
+    KVH = k8.shape[1]
+    out = torch.empty((B, T, H, dh), dtype=torch.float32, device=dev)
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().lssab8_prefill_lattice_general(
+            q8.data_ptr(), eq.data_ptr(), k8.data_ptr(), ek.data_ptr(), v8.data_ptr(), ev.data_ptr(),
+            None if ev0 is None else ev0.data_ptr(), B, H, KVH, T, dh, Tp, int(bool(causal)), kmask.data_ptr(),
+            out.data_ptr(), _lib.i64x(out.stride()), _stream_handle(dev)), "lssab8_prefill_lattice_general")
+    return out
+
+
 def quant_blocks(x, mode=0):
     """P2/P3 on the device: x [B, KVH, T, dh] -> (x8 [B, KVH, Tpad, dh], e [B, KVH, nblk], e0 [B, KVH]).
     mode 0 = B8 grid, 1 = B9 value grid, 2 = B9.1 sink_alone value grid."""

@@ -192,7 +192,7 @@ int launch_pdl(void (*kfn)(KArgs...), dim3 grid, dim3 block, int smem, cudaStrea
   return cuda_rc(cudaLaunchKernelEx(&cfg, kfn, std::forward<Args>(args)...));
 }
 
-template <int DH, bool SINK, typename OutT>
+template <int DH, bool SINK, typename OutT, bool GEN = false>
 int launch_prefill_t(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const PrefillArgs& a,
                      int num_sms, cudaStream_t st) {
   using L = PrefillSmem<DH>;
@@ -201,7 +201,7 @@ int launch_prefill_t(const CUtensorMap& tq, const CUtensorMap& tk, const CUtenso
   // allocation) lands on an SM
   int smem = kTabBytes + 1024 + L::kBytes;
   if (smem < 116 * 1024) smem = 116 * 1024;
-  auto kfn = multi ? prefill_kernel<DH, SINK, OutT, true> : prefill_kernel<DH, SINK, OutT, false>;
+  auto kfn = multi ? prefill_kernel<DH, SINK, OutT, true, GEN> : prefill_kernel<DH, SINK, OutT, false, GEN>;
   if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return kErrCuda;
   const long long items = (long long)(a.Tpad / 128) * a.H * a.B;      // persistent: one CTA per SM
   const int grid = (int)std::min<long long>(items, (long long)std::max(num_sms, 1));
@@ -363,7 +363,8 @@ static int prefill_lattice_impl(const int8_t* q8, const int32_t* eq, const int8_
                          const int32_t* ev, const int32_t* ev0, int B, int H, int KVH, int T0, int T, int dh,
                          float* orow_scratch, void* out, int out_dtype, const int64_t* os, void* stream,
                          uint64_t wait_ns = kWaitLimitNs, int withhold = -1, int npeers = 0,
-                         void* const* peers = nullptr) {
+                         void* const* peers = nullptr, int general = 0, int causal = 1,
+                         const uint32_t* kmask = nullptr) {
   if (!q8 || !eq || !k8 || !ek || !v8 || !ev || !out || !shape_ok(B, H, KVH, T, dh) || !strides_ok(os, 4))
     return kErrArg;
   if (dh != 64 && dh != 128) return kErrUnsupported;
@@ -398,6 +399,16 @@ static int prefill_lattice_impl(const int8_t* q8, const int32_t* eq, const int8_
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool sink = ev0 != nullptr;
+  if (general) {                                     // float32 out; causal flag and key mask
+    if (out_dtype != kF32 || !kmask || T0 != 0 || npeers) return kErrArg;
+    a.causal = causal ? 1 : 0;
+    a.kmask = kmask;
+    if (dh == 128) return sink ? launch_prefill_t<128, true, float, true>(tq, tk, tv, a, ds->num_sms, st)
+                               : launch_prefill_t<128, false, float, true>(tq, tk, tv, a, ds->num_sms, st);
+    return sink ? launch_prefill_t<64, true, float, true>(tq, tk, tv, a, ds->num_sms, st)
+                : launch_prefill_t<64, false, float, true>(tq, tk, tv, a, ds->num_sms, st);
+  }
+  a.causal = 1;
   if (dh == 128) return sink ? launch_prefill_out<128, true>(out_dtype, tq, tk, tv, a, ds->num_sms, st)
                              : launch_prefill_out<128, false>(out_dtype, tq, tk, tv, a, ds->num_sms, st);
   return sink ? launch_prefill_out<64, true>(out_dtype, tq, tk, tv, a, ds->num_sms, st)
@@ -475,6 +486,19 @@ int lssab8_quant_rows(const void* x, int dtype, int B, int H, int T, int dh, con
   });
 }
 
+int lssab8_quant_heads(const void* x, int dtype, int B, int H, int T, int dh, const int64_t* xs, int Tpad,
+                       int8_t* q8, int32_t* eq, void* stream) {
+  if (!x || !q8 || !eq || !shape_ok(B, H, H, T, dh) || Tpad < T || !strides_ok(xs, 4) || H > 65535 || B > 65535)
+    return kErrArg;
+  Strides4 s{xs[0], xs[1], xs[2], xs[3]};
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return with_in_dtype(dtype, [&](auto tag) {
+    using InT = std::remove_const_t<std::remove_pointer_t<decltype(tag)>>;
+    quant_head_kernel<InT><<<dim3(H, B), 256, 0, st>>>(static_cast<const InT*>(x), s, B, H, T, dh, Tpad, q8, eq);
+    return launch_rc();
+  });
+}
+
 int lssab8_quant_blocks(const void* x, int dtype, int B, int KVH, int T, int dh, const int64_t* xs, int Tpad,
                         int mode, int8_t* x8, int32_t* e, int32_t* e0, void* stream) {
   if (!x || !x8 || !e || !shape_ok(B, KVH, KVH, T, dh) || Tpad < tpad_of(T) || !strides_ok(xs, 4) || mode < 0 ||
@@ -528,6 +552,15 @@ int lssab8_prefill_lattice(const int8_t* q8, const int32_t* eq, const int8_t* k8
   if (Tpad != tpad_of(T)) return kErrArg;
   return prefill_lattice_impl(q8, eq, k8, ek, v8, ev, ev0, B, H, KVH, 0, T, dh, orow_scratch, out, out_dtype, os,
                               stream);
+}
+
+int lssab8_prefill_lattice_general(const int8_t* q8, const int32_t* eq, const int8_t* k8, const int32_t* ek,
+                                   const int8_t* v8, const int32_t* ev, const int32_t* ev0, int B, int H, int KVH,
+                                   int T, int dh, int Tpad, int causal, const uint32_t* key_mask, float* out,
+                                   const int64_t* os, void* stream) {
+  if (Tpad != tpad_of(T) || !key_mask) return kErrArg;
+  return prefill_lattice_impl(q8, eq, k8, ek, v8, ev, ev0, B, H, KVH, 0, T, dh, nullptr, out, kF32, os, stream,
+                              kWaitLimitNs, -1, 0, nullptr, 1, causal, key_mask);
 }
 
 int lssab8_prefill_chunk_lattice(const int8_t* q8, const int32_t* eq, const int8_t* k8, const int32_t* ek,

@@ -43,6 +43,13 @@
 // rounding).  The MMA thread writes the bias before every PV with tcgen05.cp from a 4 KB block
 // of bias words in shared memory, so the row workers spend no instructions on it.
 //
+// The general form (GEN, float32 output only) serves the golden entry points: p.causal = 0 lets
+// every query tile walk every key block, and the key mask p.kmask (bit j of word j / 32 of the
+// batch element's row: key j visible) hides keys from every row, as the golden's key_valid does
+// (reference/lssab8_golden.py:241-247).  A row for which a whole block is hidden skips that block
+// (no running-maximum update, no term), and a segment without a visible block skips the
+// segment -> row step; a row that sees no key at all yields 0.
+//
 // Exactness: S and A_b are exact integer sums (any MMA order); everything after them is the
 // contract's integer chain and a fixed sequence of RN binary32 operations per row
 // (reference/lssab8_torch.py:203-271, reference/lssab8_golden.py:257-335).  B9.1 sink_alone
@@ -78,6 +85,9 @@ struct PrefillArgs {
   // this process (CUDA IPC, P2P over NVLink) -- so every rank ends with every rank's heads.
   int npeers;
   void* peers[kMaxPeers];
+  // the general form (GEN kernels): causal flag and key mask [B, nblk * 4] words
+  int causal;
+  const uint32_t* kmask;
 };
 
 // ------------------------------------------------------------------------ smem layout
@@ -200,7 +210,7 @@ __device__ __forceinline__ void store_chunk(OutT* dst, long long os3, const floa
   }
 }
 
-template <int DH, bool SINK, typename OutT, bool MULTI>
+template <int DH, bool SINK, typename OutT, bool MULTI, bool GEN = false>
 __global__ void __launch_bounds__(kPrefillThreads, 1)
 prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                const __grid_constant__ CUtensorMap tm_v, const PrefillArgs p) {
@@ -287,7 +297,8 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
         mbar_expect_tx(&bars[kBarQFull + qb], L::kTile + (SINK ? DH : 0));
         tma_load_2d(smem + L::kQ + qb * L::kTile, &tm_q, 0, qrow0, &bars[kBarQFull + qb]);
         if (SINK) bulk_g2s(v0row + qb * 128, p.v8 + (long long)krow0 * DH, DH, &bars[kBarQFull + qb]);
-        for (int j = 0; j <= it.kt; ++j, ++jj) {
+        const int nbk = (GEN && !p.causal) ? p.nblk : it.kt + 1;   // key blocks of this item
+        for (int j = 0; j < nbk; ++j, ++jj) {
           const int s = jj & 1;
           const uint32_t ph = (jj >> 1) & 1;
           if (!mbar_wait(&bars[kBarKEmpty + s], ph ^ 1, abort_flag, p.err, 128, p.wait_ns)) { ok = false; break; }
@@ -336,7 +347,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
       PfItem it;
       for (int rd = 0; ok && rd < nrounds; ++rd) {
         if (!pf_item(p, ntile, rd, it)) continue;
-        const int nb = it.kt + 1;
+        const int nb = (GEN && !p.causal) ? p.nblk : it.kt + 1;
         const int qb = tt & 1;
         if (!mbar_wait(&bars[kBarQFull + qb], (tt >> 1) & 1, abort_flag, p.err, 0, p.wait_ns)) { ok = false; break; }
         const uint32_t sq = smem_u32(smem + L::kQ + qb * L::kTile);
@@ -405,7 +416,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
       if (!pf_item(p, ntile, rd, it)) continue;
       const int tile = it.tile, kt = it.kt, b = it.b, h = it.h;
       const int g = h / p.group;
-      const int nb = kt + 1;                             // causal: key blocks 0 .. kt
+      const int nb = (GEN && !p.causal) ? p.nblk : kt + 1;   // causal: key blocks 0 .. kt
       const int qrow0 = (b * p.H + h) * p.Tpad + tile * 128;
       const int qb = tt & 1;
       const int8_t* v0 = v0row + qb * 128;               // key 0's value row of this item (sink)
@@ -422,15 +433,19 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
       // fold of block jf: O = fl(O + f32(A) 2^-(s + e_v)), l = fl(l + l_b 2^-s), with the running
       // maximum rescale first (reference/lssab8_golden.py:293-315); then, at a segment end, the
       // segment -> row fold (reference/lssab8_golden.py:317-331).
-      auto fold_block = [&](int jf, int nbb, int lbt, int evj, int eh0v) -> bool {
+      auto fold_block = [&](int jf, int nbb, int lbt, int evj, int eh0v, bool live) -> bool {
         const int jgf = jj0 + jf;                          // global block index (pipeline parities)
         const int sa = MULTI ? 0 : (jgf & 1);
         const uint32_t pha = MULTI ? (uint32_t)(jgf & 1) : (uint32_t)((jgf >> 1) & 1);
-        if (!have_seg) { nbrun = nbb; have_seg = true; }
-        const int D = nbb - nbrun;
         int sg = 0, Dr = 0;
-        if (D > 0) { Dr = D; lseg = rescale(lseg, D); nbrun = nbb; }
-        else sg = -D;
+        if (!GEN || live) {
+          if (!have_seg) { nbrun = nbb; have_seg = true; }
+          const int D = nbb - nbrun;
+          if (D > 0) { Dr = D; lseg = rescale(lseg, D); nbrun = nbb; }
+          else sg = -D;
+        } else {
+          sg = kSWIN + 1;                                  // a hidden block: no update, a zero term
+        }
         if (!warp_poll(&bars[kBarAFull + sa], pha, abort_flag, p.err, p.wait_ns)) return false;
         // key 0's value row arrives with the item's Q tile
         if (SINK && jf == 0 && p.T > 1 && !warp_poll(&bars[kBarQFull + qb], (tt >> 1) & 1, abort_flag, p.err, p.wait_ns)) return false;
@@ -507,12 +522,15 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
         lseg = fold_term(lseg, lbt, add ? pow2f(-sg) : 0.0f);
         if (mseg && (((jf + 1) % kSEG == 0) || (jf == nb - 1))) {
           // segment -> row: the same three rules (reference/lssab8_golden.py:317-331), TMEM to
-          // TMEM; `first` is uniform over the item (every row's segments end at the same block),
-          // D2 and s2 are per row and stay in the arithmetic
+          // TMEM; first, D2 and s2 are per row and stay in the arithmetic (the TMEM accesses are
+          // the warp's, unconditional); a row whose segment saw no key keeps its O_row (GEN)
           int D2 = 0, s2 = 0;
+          const bool segl = !GEN || have_seg;
           const bool first = !have_row;
-          if (first) { nbrow = nbrun; have_row = true; }
-          else { D2 = nbrun - nbrow; if (D2 > 0) { lrow = rescale(lrow, D2); nbrow = nbrun; } else { s2 = -D2; } }
+          if (segl) {
+            if (first) { nbrow = nbrun; have_row = true; }
+            else { D2 = nbrun - nbrow; if (D2 > 0) { lrow = rescale(lrow, D2); nbrow = nbrun; } else { s2 = -D2; } }
+          }
   #pragma unroll 1
           for (int cc = 0; cc < HALF / 16; ++cc) {
             uint32_t y[16], x[16];
@@ -523,7 +541,8 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
             for (int c = 0; c < 16; ++c) {
               const float seg = __uint_as_float(y[c]);
               float xr = __uint_as_float(x[c]);
-              if (first) xr = rescale(seg, 0);
+              if (!segl) { /* unchanged */ }
+              else if (first) xr = rescale(seg, 0);
               else {
                 if (D2 > 0) xr = rescale(xr, D2);
                 if (s2 <= kSWIN) xr = __fadd_rn(xr, rescale(seg, s2));
@@ -534,8 +553,10 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
             tmem_fill16x2<HALF>(obase + cc * 16, 0u);      // O_seg starts at +0 for the next segment
           }
           tc_wait_st();
-          if (first) lrow = rescale(lseg, 0);
-          else if (s2 <= kSWIN) lrow = __fadd_rn(lrow, rescale(lseg, s2));
+          if (segl) {
+            if (first) lrow = rescale(lseg, 0);
+            else if (s2 <= kSWIN) lrow = __fadd_rn(lrow, rescale(lseg, s2));
+          }
           lseg = 0.0f;
           have_seg = false;
         }
@@ -543,10 +564,18 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
       };
 
       int nb_prev = 0, ev_prev = 0, lbt_prev = 0, eh0_row = 0;
+      bool live_prev = true;
       int ek_next = ekg[0], ev_next = evg[0];            // e_k, e_v one block ahead
+      // GEN: this lane's 64 key-mask bits, one block ahead
+      const uint32_t* kmb = GEN ? p.kmask + (long long)b * p.nblk * 4 + kh * 2 : nullptr;
+      uint2 km_next = GEN ? make_uint2(kmb[0], kmb[1]) : make_uint2(0u, 0u);
       for (int j = 0; j < nb; ++j) {
         const int ekj = ek_next, evj = ev_next;
-        if (j + 1 < nb) { ek_next = ekg[j + 1]; ev_next = evg[j + 1]; }
+        const uint2 kmj = km_next;
+        if (j + 1 < nb) {
+          ek_next = ekg[j + 1]; ev_next = evg[j + 1];
+          if (GEN) km_next = make_uint2(kmb[(j + 1) * 4], kmb[(j + 1) * 4 + 1]);
+        }
         const int jg = jj0 + j;
         const int s = jg & 1;
         const uint32_t ph = (jg >> 1) & 1;
@@ -559,7 +588,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
         if (!warp_poll(&bars[kBarPEmpty + s], ph ^ 1, abort_flag, p.err, p.wait_ns)) { ok = false; break; }
         if (!warp_poll(&bars[kBarSFull], jg & 1, abort_flag, p.err, p.wait_ns)) { ok = false; break; }
         tc_fence_after();
-        const bool diag = (j == kt);                       // key c of the diagonal block visible iff c <= r
+        const bool diag = (j == kt) && (!GEN || p.causal);  // key c of the diagonal block visible iff c <= r
         // pass 1: this lane's 64 scores into registers (one TMEM round trip; S is free for the
         // next QK as soon as they have landed) and the exact max over its visible keys
         uint32_t v[64];
@@ -575,6 +604,13 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
   #pragma unroll
           for (int c = 0; c < 64; ++c) if (kh * 64 + c > r) v[c] = 0x80000000u;
         }
+        if (GEN) {                                         // hidden keys
+  #pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            if (!((kmj.x >> c) & 1u)) v[c] = 0x80000000u;
+            if (!((kmj.y >> c) & 1u)) v[32 + c] = 0x80000000u;
+          }
+        }
         // four independent 16-score maxima, then their maximum: a dependency depth of 9 instead of 32
         int mq[4];
   #pragma unroll
@@ -587,6 +623,10 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
         }
         int m = max(__vimax3_s32(mq[0], mq[1], mq[2]), mq[3]);
         m = max(m, __shfl_xor_sync(0xffffffffu, m, 16));  // the row's max over both key halves
+        // a row that sees no key of this block (GEN) gets an all-zero weight row: with m = 0 and
+        // NB = 0 every hidden key's d = dm G >= 2^30 lands past the table's live range
+        const bool live = !GEN || (m != (int)0x80000000);
+        if (GEN && !live) m = 0;
         const int nbv = nb_of(m, G);
         const uint32_t NBlo = (uint32_t)nbv << kBHI;
         const int lo = m - dm;
@@ -618,12 +658,13 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
         const uint32_t lb = lbq[0] + lbq[1];
         const int lbt = (int)lb + __shfl_xor_sync(0xffffffffu, (int)lb, 16);   // the row's l_b
         if (SINK && j == 0) eh0_row = __shfl_sync(0xffffffffu, (int)eh0, lane & 15);
-        if (j > 0 && !fold_block(j - 1, nb_prev, lbt_prev, ev_prev, eh0_row)) { ok = false; break; }
+        if (j > 0 && !fold_block(j - 1, nb_prev, lbt_prev, ev_prev, eh0_row, live_prev)) { ok = false; break; }
         nb_prev = nbv;
         lbt_prev = lbt;
         ev_prev = evj;
+        live_prev = live;
       }
-      if (ok) ok = fold_block(nb - 1, nb_prev, lbt_prev, ev_prev, eh0_row);
+      if (ok) ok = fold_block(nb - 1, nb_prev, lbt_prev, ev_prev, eh0_row, live_prev);
 
       // ---- epilogue: out = O_row / l_row (one RN division per element; l_row == 0 -> 0).
       // `ok` is warp-uniform (every wait is decided for the whole warp), so the warp-collective

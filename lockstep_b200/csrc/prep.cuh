@@ -52,6 +52,39 @@ quant_rows_kernel(const InT* __restrict__ x, Strides4 xs, int B, int H, int T, i
   if (lane == 0) eq[row] = e;
 }
 
+// P1 with one exponent per head (q_exp_mode "head", reference/lssab_golden.py:230-232): the same
+// rule over all T rows and dh channels of a head.  One CTA per (head, batch): pass 1 the head's
+// amax, pass 2 every row on that exponent; eq[b, h, t] = e_h for t < T.  Rows [T, Tpad) zero.
+template <typename InT>
+__global__ void __launch_bounds__(256)
+quant_head_kernel(const InT* __restrict__ x, Strides4 xs, int B, int H, int T, int dh, int Tpad,
+                  int8_t* __restrict__ q8, int32_t* __restrict__ eq) {
+  __shared__ float red[8];
+  const int h = blockIdx.x, b = blockIdx.y;
+  const InT* src = x + b * xs.s0 + h * xs.s1;
+  const long long n = (long long)T * dh;
+  float m = 0.0f;
+  for (long long i = threadIdx.x; i < n; i += blockDim.x) {
+    const long long t = i / dh, c = i % dh;
+    m = fmaxf(m, fabsf(to_f32(src[t * xs.s2 + c * xs.s3])));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  m = 0.0f;
+  for (int w = 0; w < (int)(blockDim.x >> 5); ++w) m = fmaxf(m, red[w]);
+  const int e = pow2_exponent(m, 40);
+  const float sc = pow2f(e);
+  const long long row0 = ((long long)b * H + h) * Tpad;
+  int8_t* dst = q8 + row0 * dh;
+  for (long long i = threadIdx.x; i < (long long)Tpad * dh; i += blockDim.x) {
+    const long long t = i / dh, c = i % dh;
+    dst[i] = t < T ? (int8_t)quant8(to_f32(src[t * xs.s2 + c * xs.s3]), sc) : (int8_t)0;
+  }
+  for (int t = threadIdx.x; t < Tpad; t += blockDim.x) eq[row0 + t] = t < T ? e : 0;
+}
+
 // P2/P3 (reference/lssab_torch.py:62-85; reference/lssab9_torch.py:46-65,121-132,158).
 // One CTA per (key block, kv head, batch).  x [B, KVH, T, dh] -> x8 [B, KVH, Tpad, dh],
 // e [B, KVH, nblk], e0 [B, KVH] (sink mode only).

@@ -48,7 +48,7 @@ def lib():
         L.or_quant_blocks.restype = ctypes.c_int
         L.or_gbase.argtypes = [ctypes.c_int]
         L.or_gbase.restype = ctypes.c_int64
-        L.or_core.argtypes = [ctypes.c_int] * 4 + [P] * 8 + [ctypes.c_int] * 3 + [P, ctypes.c_int] + [P] * 4 + [ctypes.c_int] * 2
+        L.or_core.argtypes = [ctypes.c_int] * 4 + [P] * 8 + [ctypes.c_int] * 3 + [P, ctypes.c_int] + [P] * 4 + [ctypes.c_int] * 2 + [P]
         L.or_core.restype = ctypes.c_int
         _lib = L
     return _lib
@@ -114,17 +114,25 @@ def quant_blocks(x, mode=0):
     return x8, e, e0, err
 
 
-def prep(q, k, v, sink=False, mu=None, v_keyshift=0):
+def prep(q, k, v, sink=False, mu=None, v_keyshift=0, q_exp_mode="row"):
     """PREP of reference/lssab_golden.py:214-235 (+ B9 value grid when sink is on).  mu [KVH, dh]:
     the key offset, k' = fl32(k - mu) before the key quantiser (reference/lssab_golden.py:221).
     v_keyshift = dmax > 0: B9.3 (reference/lssab9_golden.py:37-70), key j of block b quantised on
     the grid e_v[b] + d_j, d_j = clamp(e_j - e_v[b], 0, dmax) with e_j the key's own exponent on
-    the B9 value grid; returns d8 [KVH, T] for the PV weight shift."""
+    the B9 value grid; returns d8 [KVH, T] for the PV weight shift.  q_exp_mode "head": one query
+    exponent per head over all its rows and channels (reference/lssab_golden.py:230-232)."""
     if mu is not None:
         k = (np.asarray(k, np.float32) - np.asarray(mu, np.float32)[:, None, :]).astype(np.float32)
-    q8, eq = quant_rows(q)
-    k8, ek, _, _ = quant_blocks(k, 0)
     T = q.shape[1]
+    if q_exp_mode == "row":
+        q8, eq = quant_rows(q)
+    elif q_exp_mode == "head":
+        qf = np.ascontiguousarray(q, np.float32)
+        q8f, eh = quant_rows(qf.reshape(qf.shape[0], -1))     # the same rule over a whole head
+        q8, eq = q8f.reshape(qf.shape), np.repeat(eh[:, None], T, axis=1).astype(np.int32)
+    else:
+        raise ValueError(q_exp_mode)
+    k8, ek, _, _ = quant_blocks(k, 0)
     if sink:
         v8, ev, ev0, err = quant_blocks(v, 2 if T > 1 else 1)
         if err:
@@ -164,11 +172,12 @@ def _keyshift(v, ev, ev0, dmax):
     return v8, d8.astype(np.int8)
 
 
-def core(p, causal=True, rows=None, key_lo=0, key_hi=None, debug=False, nthreads=None, qrow=-1):
+def core(p, causal=True, rows=None, key_lo=0, key_hi=None, debug=False, nthreads=None, qrow=-1, key_valid=None):
     """The recurrence (reference/lssab8_golden.py:200-338, reference/lssab9_golden.py:189-224).
 
     qrow >= 0: p["q8"] is [H, 1, dh] (one query row per head standing at position qrow) and
-    the result is [H, 1, dh]."""
+    the result is [H, 1, dh].  key_valid: [T] bool mask of the keys every row may see
+    (reference/lssab8_golden.py:245-246), or None."""
     q8 = np.ascontiguousarray(p["q8"], np.int8)
     k8 = np.ascontiguousarray(p["k8"], np.int8)
     KVH, T, dh = k8.shape
@@ -187,13 +196,16 @@ def core(p, causal=True, rows=None, key_lo=0, key_hi=None, debug=False, nthreads
     dl = np.zeros((H, nq), np.float32) if debug else None
     dnb = np.zeros((H, nq), np.int64) if debug else None
     r = None if rows is None else np.ascontiguousarray(rows, np.int32)
+    kvm = None if key_valid is None else np.ascontiguousarray(np.asarray(key_valid, bool), np.uint8)
+    if kvm is not None and kvm.shape != (T,):
+        raise ValueError("key_valid must be [T]")
     nt = nthreads or nthreads_default()
     rc = lib().or_core(H, KVH, T, dh, _p(q8), _p(eq), _p(k8), _p(ek), _p(v8), _p(ev),
                        None if ev0 is None else _p(ev0), None if d8 is None else _p(d8), int(causal), int(key_lo),
                        int(T if key_hi is None else key_hi),
                        None if r is None else _p(r), 0 if r is None else len(r), _p(out),
                        None if dO is None else _p(dO), None if dl is None else _p(dl),
-                       None if dnb is None else _p(dnb), nt, int(qrow))
+                       None if dnb is None else _p(dnb), nt, int(qrow), None if kvm is None else _p(kvm))
     if rc != 0:
         raise ValueError("oracle core rejected the shapes")
     if debug:
@@ -201,12 +213,13 @@ def core(p, causal=True, rows=None, key_lo=0, key_hi=None, debug=False, nthreads
     return out
 
 
-def attention(q, k, v, sink=False, causal=True, rows=None, nthreads=None, mu=None, v_keyshift=0):
+def attention(q, k, v, sink=False, causal=True, rows=None, nthreads=None, mu=None, v_keyshift=0, key_valid=None,
+              q_exp_mode="row"):
     """lssab8_attention / lssab9_attention(sink_alone) (reference/lssab8_golden.py:341,
     reference/lssab9_golden.py:254): q [H,T,dh], k/v [KVH,T,dh] -> f32 [H,T,dh]."""
     p = prep(np.asarray(q, np.float32), np.asarray(k, np.float32), np.asarray(v, np.float32), sink, mu=mu,
-             v_keyshift=v_keyshift)
-    return core(p, causal=causal, rows=rows, nthreads=nthreads)
+             v_keyshift=v_keyshift, q_exp_mode=q_exp_mode)
+    return core(p, causal=causal, rows=rows, nthreads=nthreads, key_valid=key_valid)
 
 
 def f32_to_bf16_bits(x):

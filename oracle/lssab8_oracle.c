@@ -194,7 +194,8 @@ int64_t or_floor_shift(int64_t x, int s) { return x >> s; }   /* arithmetic: flo
  *   rows: the query rows to evaluate (NULL = all T rows); the key set of row i is
  *         { j : j <= i } when causal, { j : j < T } otherwise, further restricted to
  *         [key_lo, key_hi) (the split-KV segment restriction of lssab8_row_segments,
- *         reference/lssab8_golden.py:367-377).
+ *         reference/lssab8_golden.py:367-377) and to { j : kvalid[j] != 0 } when kvalid is
+ *         not NULL (the golden's key_valid mask, reference/lssab8_golden.py:241-247).
  *   out [H, T, dh] f32 receives fl(O_row / l_row) (0 when l_row == 0) for evaluated rows.
  *   dbg_O [H, T, dh], dbg_l [H, T], dbg_nb [H, T] (optional): the row state before the
  *         division (NB_row stored as NB / 2^26; 0 when no block was visible).
@@ -212,6 +213,7 @@ typedef struct {
     int causal;
     int key_lo, key_hi;
     int qrow;            /* >= 0: q8/eq hold ONE row per head, standing for query row qrow */
+    const uint8_t* kvalid;   /* [T] key mask (NULL: every key) */
 } or_problem;
 
 static void or_row(const or_problem* P, int h, int i, float* out_row, float* dO, float* dl, int64_t* dnb,
@@ -248,7 +250,8 @@ static void or_row(const or_problem* P, int h, int i, float* out_row, float* dO,
             int32_t mS = INT32_MIN;
             for (int t = 0; t < n; ++t) {
                 int j = lo + t;
-                int vis = (j >= P->key_lo && j < P->key_hi) && (!P->causal || j <= i);
+                int vis = (j >= P->key_lo && j < P->key_hi) && (!P->causal || j <= i) &&
+                          (!P->kvalid || P->kvalid[j]);
                 const int8_t* kr = kg + (int64_t)j * dh;
                 int32_t s = 0;
                 for (int c = 0; c < dh; ++c) s += (int32_t)qrow[c] * (int32_t)kr[c];
@@ -336,14 +339,15 @@ int or_core(int H, int KVH, int T, int dh,
             const int8_t* v8, const int32_t* ev, const int32_t* ev0, const int8_t* d8,
             int causal, int key_lo, int key_hi,
             const int32_t* rows, int nrows,
-            float* out, float* dbg_O, float* dbg_l, int64_t* dbg_nb, int nthreads, int qrow) {
+            float* out, float* dbg_O, float* dbg_l, int64_t* dbg_nb, int nthreads, int qrow,
+            const uint8_t* kvalid) {
     or_build_t2();
     if (H <= 0 || KVH <= 0 || H % KVH != 0 || T <= 0 || dh <= 0 || dh > 256) return -1;
     if (qrow >= T) return -1;
     if (rows && qrow < 0) {
         for (int r = 0; r < nrows; ++r) if (rows[r] < 0 || rows[r] >= T) return -1;
     }
-    or_problem P = { H, KVH, T, dh, q8, eq, k8, ek, v8, ev, ev0, d8, causal, key_lo, key_hi, qrow };
+    or_problem P = { H, KVH, T, dh, q8, eq, k8, ek, v8, ev, ev0, d8, causal, key_lo, key_hi, qrow, kvalid };
     int nr = (qrow >= 0) ? 1 : (rows ? nrows : T);
     int64_t total = (int64_t)H * nr;
 #pragma omp parallel num_threads(nthreads > 0 ? nthreads : 1)

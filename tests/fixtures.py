@@ -172,3 +172,43 @@ def keyshift_cases():
         v = (g.standard_normal((KVH, T, dh)).astype(np.float32) * scale).astype(np.float32)
         out.append(dict(tag=tag, q=q, k=k, v=v, dmax=dmax))
     return out
+
+
+def mask_cases():
+    """Inputs for the golden entry points' general forms: causal off, a key_valid mask (random;
+    a whole block masked; key 0 masked; rows that see no key at all), the per-head query exponent
+    (q_exp_mode "head"), and a non-causal row spanning more than one 32-block fold segment.
+    Each case: tag, q/k/v float32, causal, key_valid ([T] bool or None), q_exp_mode."""
+    out = []
+
+    def draw(seed, H, KVH, T, dh):
+        g = np.random.RandomState(seed)
+        q = g.standard_normal((H, T, dh)).astype(np.float32)
+        k = g.standard_normal((KVH, T, dh)).astype(np.float32)
+        v = g.standard_normal((KVH, T, dh)).astype(np.float32)
+        return g, q, k, v
+
+    g, q, k, v = draw(41, 4, 2, 300, 64)
+    out.append(dict(tag="noncausal_h4kv2_t300_d64", q=q, k=k, v=v, causal=False, key_valid=None, q_exp_mode="row"))
+    g, q, k, v = draw(42, 4, 2, 260, 128)
+    kv = g.rand(260) < 0.7
+    out.append(dict(tag="kvrandom_h4kv2_t260_d128", q=q, k=k, v=v, causal=True, key_valid=kv, q_exp_mode="row"))
+    g, q, k, v = draw(43, 2, 1, 400, 128)
+    kv = np.ones(400, bool)
+    kv[128:256] = False                      # block 1 fully masked
+    kv[0] = False                            # key 0 masked (the sink's key)
+    kv[300:310] = False
+    out.append(dict(tag="kvblock_h2kv1_t400_d128", q=q, k=k, v=v, causal=True, key_valid=kv, q_exp_mode="row"))
+    g, q, k, v = draw(44, 4, 1, 200, 64)
+    kv = np.ones(200, bool)
+    kv[:20] = False                          # rows 0..19 see no key (causal): output 0
+    out.append(dict(tag="kvempty_h4kv1_t200_d64", q=q, k=k, v=v, causal=True, key_valid=kv, q_exp_mode="row"))
+    g, q, k, v = draw(45, 4, 2, 333, 64)
+    kv = g.rand(333) < 0.5
+    out.append(dict(tag="noncausal_kv_h4kv2_t333_d64", q=q, k=k, v=v, causal=False, key_valid=kv, q_exp_mode="row"))
+    g, q, k, v = draw(46, 4, 2, 200, 128)
+    q[1] *= np.float32(9.0)                  # one head with a different scale
+    out.append(dict(tag="qhead_h4kv2_t200_d128", q=q, k=k, v=v, causal=True, key_valid=None, q_exp_mode="head"))
+    g, q, k, v = draw(47, 1, 1, 4200, 64)
+    out.append(dict(tag="noncausal_h1kv1_t4200_d64", q=q, k=k, v=v, causal=False, key_valid=None, q_exp_mode="row"))
+    return out

@@ -158,3 +158,21 @@ def test_oracle_aligned_chunk_invariance():
     full2 = O.attention(q, k2, v2)
     part2 = O.attention(q[:, :500], k2[:, :500], v2[:, :500])
     assert not np.array_equal(part2.view(np.uint32), full2[:, :500].view(np.uint32))
+
+
+def test_oracle_masked_and_noncausal_equal_reference():
+    """causal off, key_valid masks and the per-head query exponent, against the reference golden
+    model's recorded outputs (tests/golden/make_golden_mask.py)."""
+    import json
+    import os
+    gold = json.load(open(os.path.join(os.path.dirname(__file__), "golden", "golden_mask.json")))
+    for c in FX.mask_cases():
+        rec = gold[c["tag"]]
+        parts = [c["q"].ravel(), c["k"].ravel(), c["v"].ravel()]
+        if c["key_valid"] is not None:
+            parts.append(np.asarray(c["key_valid"], np.float32))
+        assert FX.digest(np.concatenate(parts)) == rec["inputs"], c["tag"]
+        for sink, key in ((False, "b8"), (True, "b9sink")):
+            o = O.attention(c["q"], c["k"], c["v"], sink=sink, causal=c["causal"], key_valid=c["key_valid"],
+                            q_exp_mode=c["q_exp_mode"])
+            assert FX.digest(o.view(np.uint32)) == rec[key], (c["tag"], key)
