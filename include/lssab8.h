@@ -48,7 +48,8 @@ enum {
 enum {
   LSSAB8_DEV_EV_RANGE = 1,  /* e_v outside [-32, 40]: reference/lssab9_torch.py:158 assert    */
   LSSAB8_DEV_TIMEOUT = 2,   /* a bounded pipeline wait gave up                                */
-  LSSAB8_DEV_BAD_PAGE = 4   /* a block-table entry outside [0, num_pages)                     */
+  LSSAB8_DEV_BAD_PAGE = 4,  /* a block-table entry outside [0, num_pages)                     */
+  LSSAB8_DEV_ALIGN = 8      /* lssab8_kv_append: a source row not on a 16-byte boundary        */
 };
 
 /* Library identity: writes "lssab8-b200 <version> T2=<sha256 of the T2 csv>" (NUL-terminated)
@@ -83,6 +84,17 @@ int lssab8_quant_heads(const void* x, int dtype, int B, int H, int T, int dh, co
 int lssab8_quant_blocks(const void* x, int dtype, int B, int KVH, int T, int dh, const int64_t* xs, int Tpad,
                         int mode, int8_t* x8, int32_t* e, int32_t* e0, void* stream);
 
+/* B9.3 value quantiser (v_keyshift = dmax in [1, 16]; reference/lssab9_golden.py:37-70,
+ * reference/lssab9_torch.py:145-153): the B9 value grid per 128-key block (e_v clamped to
+ * [-32, 48], LSSAB8_DEV_EV_RANGE when outside [-32, 40]; sink = 1 and T > 1: key 0 alone on ev0 as in
+ * mode 2 of lssab8_quant_blocks), then key j on the finer grid e_tok + d_j with
+ * d_j = clamp(e_j - e_tok, 0, dmax), e_j the key row's own exponent on the B9 grid and e_tok the
+ * exponent its block gives it.  v8 [B, KVH, Tpad, dh], ev [B, KVH, nblk], ev0 [B, KVH] (sink),
+ * d8 [B, KVH, Tpad] int8 (d_j; padding keys 0). */
+int lssab8_quant_values_keyshift(const void* v, int dtype, int B, int KVH, int T, int dh, const int64_t* vs,
+                                 int Tpad, int sink, int dmax, int8_t* v8, int32_t* ev, int32_t* ev0, int8_t* d8,
+                                 void* stream);
+
 /* P2 with the key offset: k' = fl(f32(k) - mu[g, c]) in binary32, then the B8 block quantiser
  * (mode 0) on k'.  mu [KVH, dh] float32 on the device, one offset per kv head and channel (the
  * reference's per-layer mu[layer], reference/lssab8_torch.py:143-144, reference/lssab_golden.py:
@@ -114,6 +126,15 @@ int lssab8_prefill_lattice_general(const int8_t* q8, const int32_t* eq, const in
                                    const int8_t* v8, const int32_t* ev, const int32_t* ev0, int B, int H, int KVH,
                                    int T, int dh, int Tpad, int causal, const uint32_t* key_mask, float* out,
                                    const int64_t* os, void* stream);
+
+/* Causal prefill with B9.3 (v_keyshift): as lssab8_prefill_lattice on a lattice whose values and
+ * per-key shifts d8 [B, KVH, Tpad] come from lssab8_quant_values_keyshift; key j's PV weight is
+ * eh_j >> d_j while l_b sums the unshifted eh_j (reference/lssab9_golden.py:179-186).  out_dtype
+ * float32 or bfloat16. */
+int lssab8_prefill_lattice_keyshift(const int8_t* q8, const int32_t* eq, const int8_t* k8, const int32_t* ek,
+                                    const int8_t* v8, const int32_t* ev, const int32_t* ev0, const int8_t* d8, int B,
+                                    int H, int KVH, int T, int dh, int Tpad, void* out, int out_dtype,
+                                    const int64_t* os, void* stream);
 
 /* Block-aligned chunked prefill on an append-only lattice: query rows [T0, T) of a sequence
  * (T0 a multiple of 128) against keys [0, T).  q8/eq hold the chunk's rows only, quantised per
@@ -179,6 +200,24 @@ int lssab8_decode_prep_kv(const void* k, const void* v, int dtype, int B, int KV
                           const int64_t* seq_off, int64_t st, int64_t sg, int64_t sc, const int32_t* block_table,
                           int max_pages, int max_blocks, int num_pages, int sink, int8_t* k8p, int8_t* v8p,
                           int32_t* ek, int32_t* ev, int32_t* ev0, void* stream);
+
+/* Append to the paged int8 lattice (the engine's per-step lattice update; no counterpart entry
+ * point in the reference, whose engine fuses it into decode: docs/contract/
+ * BLOCK_EXPONENT_VARIANT.md:53-55, 212-215, docs/SPEC.md:2396-2412).  Sequence b grew from
+ * start_lens[b] to seq_lens[b] tokens; the blocks complete before the append (index <
+ * start_lens[b] / 128) are left untouched -- their values and exponents never change -- and the
+ * open block and every new block are (re)quantised over their present rows from the caller's
+ * float cache, so the lattice equals lssab8_decode_prep_kv's over all seq_lens[b] tokens bit for
+ * bit.  The float cache: token t, kv head g, channel c at k + seq_off[b] + t*st + g*sg + c
+ * (src_block_table NULL), or, for a paged cache, at
+ * k + src_block_table[b, t / 16] * src_page_stride + (t % 16) * st + g*sg + c
+ * (src_block_table [B, max_pages], 16-token pages, e.g. the same table as the lattice's).
+ * Channels contiguous, every row 16-byte aligned, dh in {64, 128}; lattice arguments as in
+ * lssab8_decode_prep_kv. */
+int lssab8_kv_append(const void* k, const void* v, int dtype, int B, int KVH, int dh, const int32_t* seq_lens,
+                     const int32_t* start_lens, const int64_t* seq_off, int64_t st, int64_t sg, const int32_t* src_block_table,
+                     int64_t src_page_stride, const int32_t* block_table, int max_pages, int max_blocks, int num_pages,
+                     int sink, int8_t* k8p, int8_t* v8p, int32_t* ek, int32_t* ev, int32_t* ev0, void* stream);
 
 /* Bytes of workspace lssab8_decode needs. */
 size_t lssab8_decode_workspace_size(int B, int H, int KVH, int dh, int max_blocks);

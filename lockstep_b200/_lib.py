@@ -10,15 +10,17 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 LIBPATH = os.path.join(_HERE, "liblssab8_b200.so")
 
 DT_F32, DT_F16, DT_BF16 = 0, 1, 2
-DEV_EV_RANGE, DEV_TIMEOUT, DEV_BAD_PAGE = 1, 2, 4
+DEV_EV_RANGE, DEV_TIMEOUT, DEV_BAD_PAGE, DEV_ALIGN = 1, 2, 4, 8
 
 # every symbol include/lssab8.h declares (tests check the library exports each one)
 SYMBOLS = (
     "lssab8_version", "lssab8_strerror", "lssab8_device_errors",
     "lssab8_quant_rows", "lssab8_quant_heads", "lssab8_quant_blocks", "lssab8_quant_keys_offset",
-    "lssab8_prefill_lattice", "lssab8_prefill_lattice_general", "lssab8_prefill_chunk_lattice", "lssab8_prefill_workspace_size", "lssab8_prefill",
+    "lssab8_quant_values_keyshift",
+    "lssab8_prefill_lattice", "lssab8_prefill_lattice_general", "lssab8_prefill_lattice_keyshift",
+    "lssab8_prefill_chunk_lattice", "lssab8_prefill_workspace_size", "lssab8_prefill",
     "lssab8_prefill_peers", "lssab8_peer_export", "lssab8_peer_import", "lssab8_peer_close",
-    "lssab8_decode_prep_kv", "lssab8_decode_workspace_size", "lssab8_decode",
+    "lssab8_decode_prep_kv", "lssab8_kv_append", "lssab8_decode_workspace_size", "lssab8_decode",
     "lssab8_decode_noalloc", "lssab8_selftest_div", "lssab8_selftest_rescale", "lssab8_selftest_timeout",
 )
 
@@ -49,6 +51,8 @@ def load():
     L.lssab8_quant_heads.argtypes = [P, I, I, I, I, I, PI64, I, P, P, P]
     L.lssab8_quant_blocks.argtypes = [P, I, I, I, I, I, PI64, I, I, P, P, P, P]
     L.lssab8_prefill_lattice_general.argtypes = [P] * 7 + [I] * 7 + [P, P, PI64, P]
+    L.lssab8_quant_values_keyshift.argtypes = [P, I, I, I, I, I, PI64, I, I, I, P, P, P, P, P]
+    L.lssab8_prefill_lattice_keyshift.argtypes = [P] * 8 + [I] * 6 + [P, I, PI64, P]
     L.lssab8_quant_keys_offset.argtypes = [P, I, I, I, I, I, PI64, I, P, P, P, P]
     L.lssab8_prefill_lattice.argtypes = [P] * 7 + [I] * 6 + [P, P, I, PI64, P]
     L.lssab8_prefill_chunk_lattice.argtypes = [P] * 7 + [I] * 6 + [P, P, I, PI64, P]
@@ -60,6 +64,7 @@ def load():
     L.lssab8_peer_import.argtypes = [P, ctypes.c_uint64, I, ctypes.POINTER(P)]
     L.lssab8_peer_close.argtypes = [P, ctypes.c_uint64]
     L.lssab8_decode_prep_kv.argtypes = [P, P, I, I, I, I, P, P, I64, I64, I64, P, I, I, I, I, P, P, P, P, P, P]
+    L.lssab8_kv_append.argtypes = [P, P, I, I, I, I, P, P, P, I64, I64, P, I64, P, I, I, I, I, P, P, P, P, P, P]
     L.lssab8_decode_workspace_size.argtypes = [I] * 5
     L.lssab8_decode_workspace_size.restype = SZ
     L.lssab8_decode.argtypes = [P, I, PI64, I, I, I, I, P, P, I, I, P, P, P, P, P, I, I, I, P, I, PI64, P, SZ, P]

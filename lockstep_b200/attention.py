@@ -49,7 +49,7 @@ def check_device_errors(device=None):
     if bits & _lib.DEV_EV_RANGE:
         raise AssertionError("e_v outside the contract clamp")
     if bits:
-        raise RuntimeError("LSSA-B8 device error bits 0x%x (timeout=2, bad page=4)" % bits)
+        raise RuntimeError("LSSA-B8 device error bits 0x%x (timeout=2, bad page=4, misaligned row=8)" % bits)
 
 
 _WS = {}
@@ -235,13 +235,50 @@ def prefill_peers(query, key, value, out, peer_ptrs, sink=False, check=False):
     return out
 
 
-def prefill(query, key, value, sink=False, out=None, out_dtype=None, check=True, mu=None):
+def quant_values_keyshift(x, dmax, sink=False):
+    """B9.3 value PREP: x [B, KVH, T, dh] -> (v8 [B, KVH, Tpad, dh], ev [B, KVH, nblk], ev0 [B, KVH],
+    d8 [B, KVH, Tpad] int8), v_keyshift = dmax (reference/lssab9_torch.py:145-153)."""
+    dev = _require_cuda(x)
+    B, KVH, T, dh = x.shape
+    Tp = tpad(T)
+    v8 = torch.empty((B, KVH, Tp, dh), dtype=torch.int8, device=dev)
+    ev = torch.empty((B, KVH, Tp // KB), dtype=torch.int32, device=dev)
+    ev0 = torch.zeros((B, KVH), dtype=torch.int32, device=dev)
+    d8 = torch.empty((B, KVH, Tp), dtype=torch.int8, device=dev)
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().lssab8_quant_values_keyshift(
+            x.data_ptr(), dtype_code(x.dtype), B, KVH, T, dh, _lib.i64x(x.stride()), Tp, int(bool(sink)), int(dmax),
+            v8.data_ptr(), ev.data_ptr(), ev0.data_ptr(), d8.data_ptr(), _stream_handle(dev)),
+            "lssab8_quant_values_keyshift")
+    return v8, ev, ev0, d8
+
+
+def prefill_lattice_keyshift(q8, eq, k8, ek, v8, ev, ev0, d8, T, out=None, out_dtype=torch.bfloat16):
+    """B9.3 prefill on a prepared lattice (values and shifts from quant_values_keyshift)."""
+    dev = _require_cuda(q8, eq, k8, ek, v8, ev, d8)
+    B, H, Tp, dh = q8.shape
+    KVH = k8.shape[1]
+    if out is None:
+        out = torch.empty((B, T, H, dh), dtype=out_dtype, device=dev)
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().lssab8_prefill_lattice_keyshift(
+            q8.data_ptr(), eq.data_ptr(), k8.data_ptr(), ek.data_ptr(), v8.data_ptr(), ev.data_ptr(),
+            None if ev0 is None else ev0.data_ptr(), d8.data_ptr(), B, H, KVH, T, dh, Tp, out.data_ptr(),
+            dtype_code(out.dtype), _lib.i64x(out.stride()), _stream_handle(dev)), "lssab8_prefill_lattice_keyshift")
+    return out
+
+
+def prefill(query, key, value, sink=False, out=None, out_dtype=None, check=True, mu=None, qexp="row",
+            v_keyshift=0, b9grid=False):
     """Batched LSSA-B8 (sink=False) / B9.1 sink_alone (sink=True) causal GQA prefill.
 
     query [B, H, T, dh], key/value [B, KVH, T, dh] (any strides, one dtype) -> out [B, T, H, dh]
     in out_dtype (default query.dtype).  Each batch element is the reference drop-in's function
     (reference/lssab8_torch.py:134-271, reference/lssab9_torch.py:109-326).  mu [KVH, dh]: the
-    key offset subtracted before the key quantiser (reference/lssab8_torch.py:143-144)."""
+    key offset subtracted before the key quantiser (reference/lssab8_torch.py:143-144).  qexp
+    "head": one query exponent per head.  v_keyshift = dmax: B9.3 (the B9 value grid, key j on
+    e_v + d_j, PV weight eh >> d_j).  b9grid: the B9 value grid (exponent clamp 48, assert 40) with
+    the sink off."""
     dev = _require_cuda(query, key, value)
     if not (query.dtype == key.dtype == value.dtype):
         raise TypeError("query, key and value must share one dtype")
@@ -253,11 +290,21 @@ def prefill(query, key, value, sink=False, out=None, out_dtype=None, check=True,
         raise ValueError("query heads must be a multiple of kv heads")
     if out is None:
         out = torch.empty((B, T, H, dh), dtype=out_dtype or query.dtype, device=dev)
-    if mu is not None:                      # the offset keys take the lattice route
-        q8, eq = quant_rows(query)
-        k8, ek = quant_keys_offset(key, mu)
-        v8, ev, ev0 = quant_blocks(value, 2 if sink else 0)
-        prefill_lattice(q8, eq, k8, ek, v8, ev, ev0 if sink else None, T, out=out)
+    if mu is not None or qexp != "row" or v_keyshift or b9grid:    # the lattice route
+        if qexp not in ("row", "head"):
+            raise ValueError(qexp)
+        q8, eq = quant_rows(query) if qexp == "row" else quant_heads(query)
+        k8, ek = quant_keys_offset(key, mu) if mu is not None else quant_blocks(key, 0)[:2]
+        if v_keyshift:
+            v8, ev, ev0, d8 = quant_values_keyshift(value, v_keyshift, sink)
+            if out.dtype in (torch.float32, torch.bfloat16):
+                prefill_lattice_keyshift(q8, eq, k8, ek, v8, ev, ev0 if (sink and T > 1) else None, d8, T, out=out)
+            else:
+                out.copy_(prefill_lattice_keyshift(q8, eq, k8, ek, v8, ev, ev0 if (sink and T > 1) else None, d8, T,
+                                                   out_dtype=torch.float32))
+        else:
+            v8, ev, ev0 = quant_blocks(value, 2 if sink else (1 if b9grid else 0))
+            prefill_lattice(q8, eq, k8, ek, v8, ev, ev0 if sink else None, T, out=out)
         if check:
             check_device_errors(dev)
         return out

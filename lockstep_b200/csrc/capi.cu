@@ -192,7 +192,7 @@ int launch_pdl(void (*kfn)(KArgs...), dim3 grid, dim3 block, int smem, cudaStrea
   return cuda_rc(cudaLaunchKernelEx(&cfg, kfn, std::forward<Args>(args)...));
 }
 
-template <int DH, bool SINK, typename OutT, bool GEN = false>
+template <int DH, bool SINK, typename OutT, bool GEN = false, bool KS = false>
 int launch_prefill_t(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const PrefillArgs& a,
                      int num_sms, cudaStream_t st) {
   using L = PrefillSmem<DH>;
@@ -201,7 +201,7 @@ int launch_prefill_t(const CUtensorMap& tq, const CUtensorMap& tk, const CUtenso
   // allocation) lands on an SM
   int smem = kTabBytes + 1024 + L::kBytes;
   if (smem < 116 * 1024) smem = 116 * 1024;
-  auto kfn = multi ? prefill_kernel<DH, SINK, OutT, true, GEN> : prefill_kernel<DH, SINK, OutT, false, GEN>;
+  auto kfn = multi ? prefill_kernel<DH, SINK, OutT, true, GEN, KS> : prefill_kernel<DH, SINK, OutT, false, GEN, KS>;
   if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return kErrCuda;
   const long long items = (long long)(a.Tpad / 128) * a.H * a.B;      // persistent: one CTA per SM
   const int grid = (int)std::min<long long>(items, (long long)std::max(num_sms, 1));
@@ -364,7 +364,7 @@ static int prefill_lattice_impl(const int8_t* q8, const int32_t* eq, const int8_
                          float* orow_scratch, void* out, int out_dtype, const int64_t* os, void* stream,
                          uint64_t wait_ns = kWaitLimitNs, int withhold = -1, int npeers = 0,
                          void* const* peers = nullptr, int general = 0, int causal = 1,
-                         const uint32_t* kmask = nullptr) {
+                         const uint32_t* kmask = nullptr, const int8_t* d8 = nullptr) {
   if (!q8 || !eq || !k8 || !ek || !v8 || !ev || !out || !shape_ok(B, H, KVH, T, dh) || !strides_ok(os, 4))
     return kErrArg;
   if (dh != 64 && dh != 128) return kErrUnsupported;
@@ -399,6 +399,22 @@ static int prefill_lattice_impl(const int8_t* q8, const int32_t* eq, const int8_
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool sink = ev0 != nullptr;
+  if (d8) {                                          // B9.3: the shifted PV weights (bf16 / f32 out)
+    if (general || npeers || (out_dtype != kF32 && out_dtype != kBF16)) return kErrArg;
+    a.causal = 1;
+    a.d8 = d8;
+    if (out_dtype == kF32) {
+      if (dh == 128) return sink ? launch_prefill_t<128, true, float, false, true>(tq, tk, tv, a, ds->num_sms, st)
+                                 : launch_prefill_t<128, false, float, false, true>(tq, tk, tv, a, ds->num_sms, st);
+      return sink ? launch_prefill_t<64, true, float, false, true>(tq, tk, tv, a, ds->num_sms, st)
+                  : launch_prefill_t<64, false, float, false, true>(tq, tk, tv, a, ds->num_sms, st);
+    }
+    if (dh == 128)
+      return sink ? launch_prefill_t<128, true, __nv_bfloat16, false, true>(tq, tk, tv, a, ds->num_sms, st)
+                  : launch_prefill_t<128, false, __nv_bfloat16, false, true>(tq, tk, tv, a, ds->num_sms, st);
+    return sink ? launch_prefill_t<64, true, __nv_bfloat16, false, true>(tq, tk, tv, a, ds->num_sms, st)
+                : launch_prefill_t<64, false, __nv_bfloat16, false, true>(tq, tk, tv, a, ds->num_sms, st);
+  }
   if (general) {                                     // float32 out; causal flag and key mask
     if (out_dtype != kF32 || !kmask || T0 != 0 || npeers) return kErrArg;
     a.causal = causal ? 1 : 0;
@@ -527,6 +543,27 @@ int lssab8_quant_blocks(const void* x, int dtype, int B, int KVH, int T, int dh,
   });
 }
 
+int lssab8_quant_values_keyshift(const void* v, int dtype, int B, int KVH, int T, int dh, const int64_t* vs,
+                                 int Tpad, int sink, int dmax, int8_t* v8, int32_t* ev, int32_t* ev0, int8_t* d8,
+                                 void* stream) {
+  if (!v || !v8 || !ev || !d8 || (sink && !ev0) || !shape_ok(B, KVH, KVH, T, dh) || Tpad < tpad_of(T) ||
+      !strides_ok(vs, 4) || dmax < 1 || dmax > 16)
+    return kErrArg;
+  DevState* ds = nullptr;
+  int rc = dev_state(&ds);
+  if (rc) return rc;
+  Strides4 s{vs[0], vs[1], vs[2], vs[3]};
+  dim3 grid((T + 127) / 128, KVH, B);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int mode = (sink && T > 1) ? 2 : 1;
+  return with_in_dtype(dtype, [&](auto tag) {
+    using InT = std::remove_const_t<std::remove_pointer_t<decltype(tag)>>;
+    quant_values_keyshift_kernel<InT><<<grid, 256, 0, st>>>(static_cast<const InT*>(v), s, B, KVH, T, dh, Tpad, mode,
+                                                           dmax, v8, ev, ev0, d8, ds->err);
+    return launch_rc();
+  });
+}
+
 int lssab8_quant_keys_offset(const void* k, int dtype, int B, int KVH, int T, int dh, const int64_t* ks, int Tpad,
                              const float* mu, int8_t* k8, int32_t* ek, void* stream) {
   if (!k || !mu || !k8 || !ek || !shape_ok(B, KVH, KVH, T, dh) || Tpad < tpad_of(T) || !strides_ok(ks, 4))
@@ -561,6 +598,15 @@ int lssab8_prefill_lattice_general(const int8_t* q8, const int32_t* eq, const in
   if (Tpad != tpad_of(T) || !key_mask) return kErrArg;
   return prefill_lattice_impl(q8, eq, k8, ek, v8, ev, ev0, B, H, KVH, 0, T, dh, nullptr, out, kF32, os, stream,
                               kWaitLimitNs, -1, 0, nullptr, 1, causal, key_mask);
+}
+
+int lssab8_prefill_lattice_keyshift(const int8_t* q8, const int32_t* eq, const int8_t* k8, const int32_t* ek,
+                                    const int8_t* v8, const int32_t* ev, const int32_t* ev0, const int8_t* d8, int B,
+                                    int H, int KVH, int T, int dh, int Tpad, void* out, int out_dtype,
+                                    const int64_t* os, void* stream) {
+  if (Tpad != tpad_of(T) || !d8) return kErrArg;
+  return prefill_lattice_impl(q8, eq, k8, ek, v8, ev, ev0, B, H, KVH, 0, T, dh, nullptr, out, out_dtype, os, stream,
+                              kWaitLimitNs, -1, 0, nullptr, 0, 1, nullptr, d8);
 }
 
 int lssab8_prefill_chunk_lattice(const int8_t* q8, const int32_t* eq, const int8_t* k8, const int32_t* ek,
@@ -693,6 +739,59 @@ int lssab8_peer_close(void* ptr, uint64_t offset) {
   return cuda_rc(cudaIpcCloseMemHandle(static_cast<uint8_t*>(ptr) - offset));
 }
 
+}  // extern "C"
+
+// the vectorised lattice writer applies when channels are contiguous, dh is 64 or 128, and every
+// row start is 16-byte aligned (base, the row / head / page strides and, for a contiguous source,
+// each sequence offset a multiple of 16 bytes)
+static int kv_lattice_launch(const void* k, const void* v, int dtype, int B, int KVH, int dh, const int32_t* seq_lens,
+                             const int32_t* start_lens, const int64_t* seq_off, int64_t st, int64_t sg, int64_t sc,
+                             const int32_t* src_bt, int64_t src_ps, const int32_t* block_table, int max_pages,
+                             int max_blocks, int num_pages, int sink, int8_t* k8p, int8_t* v8p, int32_t* ek,
+                             int32_t* ev, int32_t* ev0, int* err, cudaStream_t s, bool* done) {
+  *done = false;
+  if ((dh != 64 && dh != 128) || sc != 1) return kOk;
+  return with_in_dtype(dtype, [&](auto tag) -> int {
+    using InT = std::remove_const_t<std::remove_pointer_t<decltype(tag)>>;
+    const long long e = (long long)sizeof(InT);
+    if ((reinterpret_cast<uintptr_t>(k) & 15) || (reinterpret_cast<uintptr_t>(v) & 15) || (st * e) % 16 ||
+        (sg * e) % 16 || (src_bt && (src_ps * e) % 16))
+      return kOk;
+    if (B > 32767) return kOk;
+    dim3 grid(max_blocks, KVH, 2 * B);                  // K and V blocks in separate CTAs
+    const int vmode = sink ? 2 : 0;
+    auto kfn = dh == 128 ? kv_lattice_kernel<InT, 128> : kv_lattice_kernel<InT, 64>;
+    kfn<<<grid, 256, 0, s>>>(static_cast<const InT*>(k), static_cast<const InT*>(v),
+                             reinterpret_cast<const long long*>(seq_off), st, sg, src_bt, src_ps, B, KVH, seq_lens,
+                             start_lens, block_table, max_pages, max_blocks, num_pages, vmode, k8p, v8p, ek, ev, ev0,
+                             err);
+    *done = true;
+    return launch_rc();
+  });
+}
+
+extern "C" {
+
+int lssab8_kv_append(const void* k, const void* v, int dtype, int B, int KVH, int dh, const int32_t* seq_lens,
+                     const int32_t* start_lens, const int64_t* seq_off, int64_t st, int64_t sg, const int32_t* src_block_table,
+                     int64_t src_page_stride, const int32_t* block_table, int max_pages, int max_blocks, int num_pages,
+                     int sink, int8_t* k8p, int8_t* v8p, int32_t* ek, int32_t* ev, int32_t* ev0, void* stream) {
+  if (!k || !v || !seq_lens || !start_lens || (!seq_off && !src_block_table) || !block_table || !k8p || !v8p || !ek ||
+      !ev || (sink && !ev0) || B <= 0 || KVH <= 0 || max_pages <= 0 || max_blocks <= 0 || num_pages <= 0 || st < 0 ||
+      sg < 0 || src_page_stride < 0 || max_pages < max_blocks * 8 - 7)
+    return kErrArg;
+  if (dh != 64 && dh != 128) return kErrUnsupported;
+  DevState* ds = nullptr;
+  int rc = dev_state(&ds);
+  if (rc) return rc;
+  bool done = false;
+  rc = kv_lattice_launch(k, v, dtype, B, KVH, dh, seq_lens, start_lens, seq_off, st, sg, 1, src_block_table,
+                         src_page_stride, block_table, max_pages, max_blocks, num_pages, sink, k8p, v8p, ek, ev, ev0,
+                         ds->err, static_cast<cudaStream_t>(stream), &done);
+  if (rc) return rc;
+  return done ? kOk : kErrArg;                       // unaligned rows: the append needs 16-byte rows
+}
+
 int lssab8_decode_prep_kv(const void* k, const void* v, int dtype, int B, int KVH, int dh, const int32_t* seq_lens,
                           const int64_t* seq_off, int64_t st, int64_t sg, int64_t sc, const int32_t* block_table,
                           int max_pages, int max_blocks, int num_pages, int sink, int8_t* k8p, int8_t* v8p,
@@ -707,6 +806,12 @@ int lssab8_decode_prep_kv(const void* k, const void* v, int dtype, int B, int KV
   dim3 grid(max_blocks, KVH, B);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int vmode = sink ? 2 : 0;
+  bool done = false;
+  if ((rc = kv_lattice_launch(k, v, dtype, B, KVH, dh, seq_lens, nullptr, seq_off, st, sg, sc, nullptr, 0,
+                              block_table, max_pages, max_blocks, num_pages, sink, k8p, v8p, ek, ev, ev0, ds->err, s,
+                              &done)))
+    return rc;
+  if (done) return kOk;
   return with_in_dtype(dtype, [&](auto tag) {
     using InT = std::remove_const_t<std::remove_pointer_t<decltype(tag)>>;
     decode_prep_kernel<InT><<<grid, 256, 0, s>>>(static_cast<const InT*>(k), static_cast<const InT*>(v),

@@ -35,6 +35,7 @@ enum : int {
   kDevEvRange = 1,        // e_v outside [-32, 40] (reference/lssab9_torch.py:158)
   kDevTimeout = 2,        // a bounded wait gave up (pipeline stalled)
   kDevBadPage = 4,        // block table entry out of range
+  kDevAlign = 8,          // a source row off the 16-byte grid a vectorised kernel needs
 };
 
 // dtype codes used across the C ABI

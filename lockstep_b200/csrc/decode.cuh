@@ -396,4 +396,126 @@ decode_prep_kernel(const InT* __restrict__ ksrc, const InT* __restrict__ vsrc, c
   }
 }
 
+// The paged lattice writer, vectorised, with append-only semantics (the engine's per-step prep,
+// docs/contract/BLOCK_EXPONENT_VARIANT.md:53-55, 212-215: a complete 128-key block never changes;
+// the open block's exponents and values are recomputed from its present rows).  One CTA of 256
+// threads per (128-key block, kv head, sequence, tensor): K and V blocks are separate CTAs (their
+// exponents are independent), which keeps a CTA's registers low enough for several per SM.  Blocks
+// below start_lens[b] / 128 (complete before this append) are left as they are.  The float source
+// is read once in 16-byte vectors (channels contiguous) and kept in registers for the amax and the
+// quantisation; K rows go straight to their pages, V is transposed per page through shared memory,
+// and both are written in 16-byte (K: 8-byte) stores.  Token t of sequence b, kv head g, channel c
+// is read at
+//   src + seq_off[b] + t * st + g * sg + c                 (src_bt == nullptr), or
+//   src + src_bt[b, t / 16] * src_ps + (t % 16) * st + g * sg + c  (a paged source cache).
+// Rows past the sequence end inside its last page are written as zeros.
+template <typename InT, int DH>
+__global__ void __launch_bounds__(256)
+kv_lattice_kernel(const InT* __restrict__ ksrc, const InT* __restrict__ vsrc, const long long* __restrict__ seq_off,
+                  long long st, long long sg, const int32_t* __restrict__ src_bt, long long src_ps, int B, int KVH,
+                  const int32_t* __restrict__ seq_lens, const int32_t* __restrict__ start_lens,
+                  const int32_t* __restrict__ block_table, int max_pages, int max_blocks, int num_pages, int vmode,
+                  int8_t* __restrict__ k8p, int8_t* __restrict__ v8p, int32_t* __restrict__ ek,
+                  int32_t* __restrict__ ev, int32_t* __restrict__ ev0, int* __restrict__ err) {
+  constexpr int EPV = 16 / sizeof(InT);                  // elements per 16-byte vector
+  constexpr int VPR = DH / EPV;                          // vectors per row
+  constexpr int NV = 128 * VPR / 256;                    // vectors per thread
+  const int blk = blockIdx.x, g = blockIdx.y, b = blockIdx.z >> 1;
+  const bool isv = (blockIdx.z & 1) != 0;                // this CTA's tensor: K (0) or V (1)
+  const int L = seq_lens[b];
+  const int nblk = (L + kKB - 1) / kKB;
+  if (blk >= nblk) return;
+  if (nblk > max_blocks || (L + 15) / 16 > max_pages) {
+    if (threadIdx.x == 0 && !isv) atomicOr(err, kDevBadPage);
+    return;
+  }
+  if (start_lens && blk < start_lens[b] / kKB) return;   // complete before this append: unchanged
+  const int lo = blk * kKB;
+  const int npages = min(8, ((L + 15) / 16) - blk * 8);  // pages of this block that exist
+  const int32_t* bt = block_table + (long long)b * max_pages;
+  const InT* src = isv ? vsrc : ksrc;
+  __shared__ float red[2][8];
+  __shared__ __align__(16) int8_t vt[DH][128 + 16];      // V^T of the block, one row per channel
+  const bool split0 = isv && (vmode == 2) && (blk == 0) && (L > 1);
+  uint4 x[NV];
+  float m = 0.0f, m0 = 0.0f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int u = threadIdx.x + 256 * i;
+    const int r = u / VPR, cv = u % VPR;
+    const int t = lo + r;
+    x[i] = make_uint4(0u, 0u, 0u, 0u);
+    if (t < L) {
+      const long long row = src_bt ? (long long)src_bt[(long long)b * max_pages + t / 16] * src_ps + (long long)(t % 16) * st
+                                   : seq_off[b] + (long long)t * st;
+      const long long o = row + (long long)g * sg + cv * EPV;
+      if (o & (EPV - 1)) atomicOr(err, kDevAlign);       // a row off the 16-byte grid: refuse it
+      else x[i] = *reinterpret_cast<const uint4*>(src + o);
+    }
+    const InT* xe = reinterpret_cast<const InT*>(&x[i]);
+#pragma unroll
+    for (int e = 0; e < EPV; ++e) {
+      const float a = fabsf(to_f32(xe[e]));
+      if (split0 && t == 0) m0 = fmaxf(m0, a); else m = fmaxf(m, a);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, o));
+  }
+  const int w = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) == 0) { red[0][w] = m; red[1][w] = m0; }
+  __syncthreads();
+  m = 0.0f; m0 = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) { m = fmaxf(m, red[0][i]); m0 = fmaxf(m0, red[1][i]); }
+  const int e1 = pow2_exponent(m, (!isv || vmode == 0) ? 40 : 48);
+  const int e0 = split0 ? pow2_exponent(m0, 48) : e1;
+  const float s1 = pow2f(e1), s0 = pow2f(e0);
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int u = threadIdx.x + 256 * i;
+    const int r = u / VPR, cv = u % VPR;
+    const int t = lo + r;
+    const InT* xe = reinterpret_cast<const InT*>(&x[i]);
+    if (isv) {                                           // V: into the transposed tile
+#pragma unroll
+      for (int e = 0; e < EPV; ++e) vt[cv * EPV + e][r] = (int8_t)quant8(to_f32(xe[e]), (split0 && t == 0) ? s0 : s1);
+    } else if (r / 16 < npages) {                        // K: straight to the row's page
+      uint32_t kq[EPV / 4 > 0 ? EPV / 4 : 1] = {};
+#pragma unroll
+      for (int e = 0; e < EPV; ++e) kq[e / 4] |= (uint32_t)(uint8_t)(int8_t)quant8(to_f32(xe[e]), s1) << (8 * (e % 4));
+      const int pg = bt[blk * 8 + r / 16];
+      if (pg < 0 || pg >= num_pages) { atomicOr(err, kDevBadPage); continue; }
+      int8_t* kd = k8p + (((long long)pg * KVH + g) * 16 + (r % 16)) * DH + cv * EPV;
+      if constexpr (EPV == 8) *reinterpret_cast<uint2*>(kd) = make_uint2(kq[0], kq[1]);
+      else if constexpr (EPV == 4) *reinterpret_cast<uint32_t*>(kd) = kq[0];
+      else *reinterpret_cast<uint4*>(kd) = make_uint4(kq[0], kq[1], kq[2], kq[3]);
+    }
+  }
+  if (isv) {
+    __syncthreads();
+    // V pages: [page][g][channel][16 keys], one 16-byte store per (page, channel)
+    for (int i = threadIdx.x; i < npages * DH; i += 256) {
+      const int pl = i / DH, c = i % DH;
+      const int pg = bt[blk * 8 + pl];
+      if (pg < 0 || pg >= num_pages) { atomicOr(err, kDevBadPage); continue; }
+      const uint32_t* srow = reinterpret_cast<const uint32_t*>(&vt[c][pl * 16]);
+      *reinterpret_cast<uint4*>(v8p + (((long long)pg * KVH + g) * DH + c) * 16) =
+          make_uint4(srow[0], srow[1], srow[2], srow[3]);
+    }
+  }
+  if (threadIdx.x == 0) {
+    const long long o = ((long long)b * KVH + g) * max_blocks + blk;
+    if (!isv) {
+      ek[o] = e1;
+    } else {
+      ev[o] = e1;
+      if (vmode == 2 && blk == 0) ev0[(long long)b * KVH + g] = e0;
+      if (vmode != 0 && (e1 < -32 || e1 > 40)) atomicOr(err, kDevEvRange);
+    }
+  }
+}
+
 }  // namespace lssab8

@@ -50,6 +50,10 @@
 // (no running-maximum update, no term), and a segment without a visible block skips the
 // segment -> row step; a row that sees no key at all yields 0.
 //
+// B9.3 (KS kernels, v_keyshift; reference/lssab9_golden.py:179-186, reference/lssab9_torch.py:
+// 145-153): key j's value row sits on the finer grid e_v + d_j (p.d8), so its PV weight is
+// eh_j >> d_j while l_b keeps the unshifted eh_j; the chain packs both byte vectors.
+//
 // Exactness: S and A_b are exact integer sums (any MMA order); everything after them is the
 // contract's integer chain and a fixed sequence of RN binary32 operations per row
 // (reference/lssab8_torch.py:203-271, reference/lssab8_golden.py:257-335).  B9.1 sink_alone
@@ -88,6 +92,7 @@ struct PrefillArgs {
   // the general form (GEN kernels): causal flag and key mask [B, nblk * 4] words
   int causal;
   const uint32_t* kmask;
+  const int8_t* d8;     // B9.3 (KS kernels): per-key weight shift [B, KVH, nblk * 128]
 };
 
 // ------------------------------------------------------------------------ smem layout
@@ -210,7 +215,7 @@ __device__ __forceinline__ void store_chunk(OutT* dst, long long os3, const floa
   }
 }
 
-template <int DH, bool SINK, typename OutT, bool MULTI, bool GEN = false>
+template <int DH, bool SINK, typename OutT, bool MULTI, bool GEN = false, bool KS = false>
 __global__ void __launch_bounds__(kPrefillThreads, 1)
 prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                const __grid_constant__ CUtensorMap tm_v, const PrefillArgs p) {
@@ -569,12 +574,28 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
       // GEN: this lane's 64 key-mask bits, one block ahead
       const uint32_t* kmb = GEN ? p.kmask + (long long)b * p.nblk * 4 + kh * 2 : nullptr;
       uint2 km_next = GEN ? make_uint2(kmb[0], kmb[1]) : make_uint2(0u, 0u);
+      // KS: this lane's 64 weight shifts (one byte per key), one block ahead
+      const uint4* dsb = KS ? reinterpret_cast<const uint4*>(p.d8 + (long long)(b * p.KVH + g) * p.nblk * 128 + kh * 64)
+                            : nullptr;
+      uint4 ds_next[4], ds_cur[4];
+      if (KS) {
+  #pragma unroll
+        for (int i = 0; i < 4; ++i) ds_next[i] = dsb[i];
+      }
       for (int j = 0; j < nb; ++j) {
         const int ekj = ek_next, evj = ev_next;
         const uint2 kmj = km_next;
+        if (KS) {
+  #pragma unroll
+          for (int i = 0; i < 4; ++i) ds_cur[i] = ds_next[i];
+        }
         if (j + 1 < nb) {
           ek_next = ekg[j + 1]; ev_next = evg[j + 1];
           if (GEN) km_next = make_uint2(kmb[(j + 1) * 4], kmb[(j + 1) * 4 + 1]);
+          if (KS) {
+  #pragma unroll
+            for (int i = 0; i < 4; ++i) ds_next[i] = dsb[(j + 1) * 8 + i];   // 128 keys = 8 x 16 bytes
+          }
         }
         const int jg = jj0 + j;
         const int s = jg & 1;
@@ -647,7 +668,12 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__
               e[x] = tab[ix * p.mul_entry + lane4];            // entry ix, this lane's copy
             }
             w[qq] = e[0] + e[1] * p.mul_b1 + e[2] * p.mul_b2 + e[3] * p.mul_b3;
-            lbq[qq & 1] = __dp4a(w[qq], 0x01010101u, lbq[qq & 1]);
+            lbq[qq & 1] = __dp4a(w[qq], 0x01010101u, lbq[qq & 1]);   // l_b: the unshifted weights
+            if (KS) {                                        // the PV weights eh >> d
+              const uint32_t dw = qq == 0 ? ds_cur[cc].x : qq == 1 ? ds_cur[cc].y : qq == 2 ? ds_cur[cc].z : ds_cur[cc].w;
+              w[qq] = (e[0] >> (dw & 0xFFu)) | ((e[1] >> ((dw >> 8) & 0xFFu)) << 8) |
+                      ((e[2] >> ((dw >> 16) & 0xFFu)) << 16) | ((e[3] >> (dw >> 24)) << 24);
+            }
           }
           const int chunk = kh * 4 + cc;
           if (SINK && chunk == 0 && j == 0 && p.T > 1) { eh0 = w[0] & 0xFFu; w[0] &= ~0xFFu; }

@@ -85,6 +85,69 @@ quant_head_kernel(const InT* __restrict__ x, Strides4 xs, int B, int H, int T, i
   for (int t = threadIdx.x; t < Tpad; t += blockDim.x) eq[row0 + t] = t < T ? e : 0;
 }
 
+// B9.3 value quantiser (v_keyshift = dmax, reference/lssab9_golden.py:37-70; reference/
+// lssab9_torch.py:145-153).  One CTA per (key block, kv head, batch).  The block exponent e_v is
+// the B9 value grid's (modes 1 / 2 of quant_blocks_kernel: clamp [-32, 48], then outside [-32, 40]
+// sets kDevEvRange; mode 2 quantises key 0 alone, e0, when T > 1).  Key j then sits on the grid
+// e_tok + d_j, e_tok = e_v (e0 for key 0 in mode 2), d_j = clamp(e_j - e_tok, 0, dmax) with e_j the
+// key's own exponent on the B9 grid (its row alone); x8 = clamp(rint(x 2^(e_tok + d_j)), +-127)
+// and d8[b, g, j] = d_j (padding keys 0).  One warp per key row in pass 2.
+template <typename InT>
+__global__ void __launch_bounds__(256)
+quant_values_keyshift_kernel(const InT* __restrict__ x, Strides4 xs, int B, int KVH, int T, int dh, int Tpad,
+                             int mode, int dmax, int8_t* __restrict__ x8, int32_t* __restrict__ eblk,
+                             int32_t* __restrict__ e0, int8_t* __restrict__ d8, int* __restrict__ err) {
+  const int blk = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+  const int nblk = (T + kKB - 1) / kKB;
+  const int lo = blk * kKB;
+  const int hi = min(T, lo + kKB);
+  const InT* src = x + b * xs.s0 + g * xs.s1;
+  const long long rowbase = (long long)(b * KVH + g) * Tpad;
+  int8_t* dst = x8 + rowbase * dh;
+  const bool split0 = (mode == 2) && (blk == 0) && (T > 1);
+  __shared__ float red[2][8];
+  float m = 0.0f, m0 = 0.0f;
+  const int n = (hi - lo) * dh;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const int r = lo + i / dh, c = i % dh;
+    const float a = fabsf(to_f32(src[(long long)r * xs.s2 + (long long)c * xs.s3]));
+    if (split0 && r == 0) m0 = fmaxf(m0, a); else m = fmaxf(m, a);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, o));
+  }
+  if ((threadIdx.x & 31) == 0) { red[0][threadIdx.x >> 5] = m; red[1][threadIdx.x >> 5] = m0; }
+  __syncthreads();
+  m = 0.0f; m0 = 0.0f;
+  for (int w = 0; w < (int)(blockDim.x >> 5); ++w) { m = fmaxf(m, red[0][w]); m0 = fmaxf(m0, red[1][w]); }
+  const int e = pow2_exponent(m, 48);
+  const int ez = split0 ? pow2_exponent(m0, 48) : e;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int r = lo + warp; r < hi; r += (int)(blockDim.x >> 5)) {      // one warp per key row
+    const InT* xr = src + (long long)r * xs.s2;
+    float mr = 0.0f;
+    for (int c = lane; c < dh; c += 32) mr = fmaxf(mr, fabsf(to_f32(xr[(long long)c * xs.s3])));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mr = fmaxf(mr, __shfl_xor_sync(0xffffffffu, mr, o));
+    const int etok = (split0 && r == 0) ? ez : e;
+    const int dj = min(max(pow2_exponent(mr, 48) - etok, 0), dmax);
+    const float sc = pow2f(etok + dj);
+    for (int c = lane; c < dh; c += 32) dst[(long long)r * dh + c] = (int8_t)quant8(to_f32(xr[(long long)c * xs.s3]), sc);
+    if (lane == 0) d8[rowbase + r] = (int8_t)dj;
+  }
+  if (blk == nblk - 1) {                             // padding rows of the last block
+    for (int i = threadIdx.x; i < (Tpad - hi) * dh; i += blockDim.x) dst[(long long)hi * dh + i] = 0;
+    for (int r = hi + threadIdx.x; r < Tpad; r += blockDim.x) d8[rowbase + r] = 0;
+  }
+  if (threadIdx.x == 0) {
+    eblk[(long long)(b * KVH + g) * nblk + blk] = e;
+    if (mode == 2 && blk == 0) e0[b * KVH + g] = ez;
+    if (e < -32 || e > 40) atomicOr(err, kDevEvRange);
+  }
+}
+
 // P2/P3 (reference/lssab_torch.py:62-85; reference/lssab9_torch.py:46-65,121-132,158).
 // One CTA per (key block, kv head, batch).  x [B, KVH, T, dh] -> x8 [B, KVH, Tpad, dh],
 // e [B, KVH, nblk], e0 [B, KVH] (sink mode only).

@@ -104,6 +104,55 @@ def build_paged_kv(keys, values, seq_lens, block_table, num_pages, sink=False, c
                    seq_lens=seq_lens, max_blocks=a["max_blocks"], num_pages=num_pages, sink=bool(sink))
 
 
+def empty_paged_kv(B, KVH, dh, max_len, block_table, num_pages, sink=False):
+    """An empty lattice (every sequence of length 0) with room for max_len tokens per sequence,
+    to be filled by append_kv.  block_table [B, max_pages] int32 (CUDA)."""
+    dev = block_table.device
+    a = alloc_paged(B, KVH, dh, max_len, num_pages, dev, sink)
+    return PagedKV(k8p=a["k8p"], v8p=a["v8p"], ek=a["ek"], ev=a["ev"], ev0=a["ev0"], block_table=block_table,
+                   seq_lens=torch.zeros(B, dtype=torch.int32, device=dev), max_blocks=a["max_blocks"],
+                   num_pages=num_pages, sink=bool(sink))
+
+
+def append_kv(kv, keys, values, new_lens, src_block_table=None, check=True):
+    """Append-only lattice update (lssab8_kv_append): the sequences grew from kv.seq_lens to
+    new_lens [B] int32 tokens.  keys / values hold every token so far, either dense
+    [B, KVH, Lcap, dh] or, with src_block_table [B, max_pages], paged [num_pages, 16, KVH, dh]
+    (the engine's float cache).  Blocks complete before the append are not rewritten; the open
+    block and the new ones are quantised over their present rows, so the lattice equals a fresh
+    build_paged_kv over new_lens bit for bit.  Updates kv.seq_lens in place and returns kv."""
+    dev = _A._require_cuda(keys, values, new_lens, kv.k8p)
+    if keys.dtype != values.dtype or keys.shape != values.shape or keys.stride() != values.stride():
+        raise ValueError("keys and values must share shape, strides and dtype")
+    B = kv.seq_lens.numel()
+    new_lens = new_lens.to(device=dev, dtype=torch.int32).contiguous()
+    if src_block_table is None:
+        if keys.dim() != 4 or keys.shape[0] != B:
+            raise ValueError("dense keys must be [B, KVH, Lcap, dh]")
+        s = keys.stride()
+        seq_off = (torch.arange(B, dtype=torch.int64) * s[0]).to(dev)
+        st, sg, sc, ps, sbt = s[2], s[1], s[3], 0, None
+    else:
+        if keys.dim() != 4 or keys.shape[1] != PAGE:
+            raise ValueError("paged keys must be [num_pages, 16, KVH, dh]")
+        s = keys.stride()
+        seq_off, st, sg, sc, ps, sbt = None, s[1], s[2], s[3], s[0], src_block_table
+    if sc != 1:
+        raise ValueError("the channel dimension must be contiguous")
+    start = kv.seq_lens.clone()
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().lssab8_kv_append(
+            keys.data_ptr(), values.data_ptr(), _A.dtype_code(keys.dtype), B, kv.KVH, kv.dh, new_lens.data_ptr(),
+            start.data_ptr(), None if seq_off is None else seq_off.data_ptr(), st, sg,
+            None if sbt is None else sbt.data_ptr(), ps, kv.block_table.data_ptr(), kv.block_table.shape[1],
+            kv.max_blocks, kv.num_pages, int(kv.sink), kv.k8p.data_ptr(), kv.v8p.data_ptr(), kv.ek.data_ptr(),
+            kv.ev.data_ptr(), kv.ev0.data_ptr(), _A._stream_handle(dev)), "lssab8_kv_append")
+    kv.seq_lens.copy_(new_lens)
+    if check:
+        _A.check_device_errors(dev)
+    return kv
+
+
 def identity_pages(B, L, device):
     """Block table of a contiguous cache: sequence b owns pages [b*P, (b+1)*P), P = ceil(L/16)."""
     P = (L + PAGE - 1) // PAGE

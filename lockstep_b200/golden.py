@@ -56,10 +56,17 @@ def _core(q, k, v, mu, kb, q_exp_mode, causal, key_valid, sink, b9grid, v_keyshi
         k8, ek, _ = A.quant_blocks(kd, 0)
     vmode = (2 if T > 1 else 1) if sink else (1 if b9grid else 0)
     if v_keyshift:
-        raise NotImplementedError("B9.3 v_keyshift has no kernel")
-    v8, ev, ev0 = A.quant_blocks(vd, vmode)
+        if not 1 <= int(v_keyshift) <= 16:
+            raise NotImplementedError("v_keyshift above 16 has no kernel")
+        if not causal or key_valid is not None:
+            raise NotImplementedError("B9.3 runs on the causal form only")
+        v8, ev, ev0, d8 = A.quant_values_keyshift(vd, int(v_keyshift), sink)
+    else:
+        v8, ev, ev0 = A.quant_blocks(vd, vmode)
     ev0 = ev0 if (sink and T > 1) else None
-    if causal and key_valid is None:
+    if v_keyshift:
+        out = A.prefill_lattice_keyshift(q8, eq, k8, ek, v8, ev, ev0, d8, T, out_dtype=torch.float32)
+    elif causal and key_valid is None:
         out = A.prefill_lattice(q8, eq, k8, ek, v8, ev, ev0, T, out_dtype=torch.float32)
     else:
         km = A.key_mask_words(key_valid, 1, T, dev)

@@ -12,8 +12,8 @@ prefill, sm_100a) and is bit-identical to the reference's.
 
 Parameters the reference calls SCHEDULE (head_chunk, qblk, kblk; gate S10) and `skip` (exact,
 gate S6) are accepted and do not change a bit.  Contract parameters must be the contract's
-values (kb=128, bhi=26, n=7, w_loc=9, weight="rn", s_win=32, seg_keys=4096, qexp="row",
-clamp_sh=True): other arms of the reference (L8-RN-W8, L8-TR, L8-RN-n8, L8-RN-KB64, L16) are
+values (kb=128, bhi=26, n=7, w_loc=9, weight="rn", s_win=32, seg_keys=4096, clamp_sh=True;
+qexp "row" or "head", the per-head query exponent): other arms of the reference (L8-RN-W8, L8-TR, L8-RN-n8, L8-RN-KB64, L16) are
 research controls with no B200 kernel and raise NotImplementedError.  A key offset `mu` (a
 sequence indexed by the module's layer_idx, each [KVH, dh]) is subtracted from the keys in binary32
 before the key quantiser, as the reference does (reference/lssab8_torch.py:116-122, 143-144).
@@ -32,8 +32,8 @@ NB_SENT = -(1 << 58)
 def _contract_check(kb, bhi, n, w_loc, weight, s_win, seg_keys, mu, qexp, clamp_sh):
     assert n <= bhi and qexp in ("row", "head")
     assert seg_keys % kb == 0, "a segment must be a whole number of blocks"
-    if (kb, bhi, n, w_loc, weight, s_win, seg_keys, qexp, bool(clamp_sh)) != (KB, BHI, NIDX, W_LOC, "rn", S_WIN,
-                                                                               SEG_KEYS, "row", True):
+    if (kb, bhi, n, w_loc, weight, s_win, seg_keys, bool(clamp_sh)) != (KB, BHI, NIDX, W_LOC, "rn", S_WIN,
+                                                                        SEG_KEYS, True):
         raise NotImplementedError("only the LSSA-B8 contract arm (L8 = L8-RN-W9) has a B200 kernel")
 
 
@@ -53,14 +53,14 @@ def _mu_for(mu, module, device, cache=None):
     return t
 
 
-def _attn_closure(sink, mu=None):
+def _attn_closure(sink, mu=None, qexp="row"):
     mu_cache = {}
 
     def attn(module, query, key, value, attention_mask, *args, **kw):
         Bsz, H, T, dh = query.shape
         assert Bsz == 1, "B=1 windows only"
         out = _A.prefill(query, key, value, sink=sink, out_dtype=query.dtype,
-                         mu=_mu_for(mu, module, query.device, mu_cache))
+                         mu=_mu_for(mu, module, query.device, mu_cache), qexp=qexp)
         return out, None
     return attn
 
@@ -72,7 +72,7 @@ def make_lssab8_long_attn(kb=KB, bhi=BHI, n=NIDX, w_loc=W_LOC, weight="rn", s_wi
 
     `stats` (the reference's debug counters) is not collected by the kernels and stays untouched."""
     _contract_check(kb, bhi, n, w_loc, weight, s_win, seg_keys, mu, qexp, clamp_sh)
-    return _attn_closure(sink=False, mu=mu)
+    return _attn_closure(sink=False, mu=mu, qexp=qexp)
 
 
 def make_lssab8_attn(kb=KB, bhi=BHI, n=NIDX, w_loc=W_LOC, weight="rn", head_chunk=16,

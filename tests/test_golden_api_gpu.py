@@ -44,6 +44,14 @@ def test_general_forms_equal_reference(case):
     kw = dict(causal=c["causal"], key_valid=c["key_valid"], q_exp_mode=c["q_exp_mode"])
     assert FX.digest(_bits(G.lssab8_attention(c["q"], c["k"], c["v"], **kw))) == gold["b8"]
     assert FX.digest(_bits(G.lssab9_attention(c["q"], c["k"], c["v"], sink_alone=True, **kw))) == gold["b9sink"]
+    if c["causal"] and c["key_valid"] is None:          # the torch drop-ins take the same forms
+        from lockstep_b200 import lssab8_torch as L8
+        from lockstep_b200 import lssab9_torch as L9
+        args = [torch.from_numpy(x).cuda()[None] for x in (c["q"], c["k"], c["v"])]
+        o8, _ = L8.make_lssab8_long_attn(qexp=c["q_exp_mode"])(None, *args, None)
+        o9, _ = L9.make_lssab9_long_attn(qexp=c["q_exp_mode"], sink_alone=True)(None, *args, None)
+        assert FX.digest(_bits(o8[0].transpose(0, 1).cpu().numpy())) == gold["b8"]
+        assert FX.digest(_bits(o9[0].transpose(0, 1).cpu().numpy())) == gold["b9sink"]
 
 
 def test_rows_heads_and_torch_inputs():
@@ -59,3 +67,23 @@ def test_rows_heads_and_torch_inputs():
     assert isinstance(t, torch.Tensor) and np.array_equal(_bits(t.cpu().numpy()), _bits(full))
     with pytest.raises(NotImplementedError):
         G.lssab8_attention(c["q"], c["k"], c["v"], kb=64)
+
+
+@pytest.mark.parametrize("case", FX.keyshift_cases(), ids=lambda c: c["tag"])
+@pytest.mark.parametrize("sink", [False, True])
+def test_value_keyshift_equals_reference(case, sink):
+    """B9.3 v_keyshift (reference/lssab9_golden.py:37-70, 179-186) against the reference's recorded
+    d8 shifts and outputs, through the golden entry point and through the torch drop-in."""
+    from lockstep_b200 import attention as A
+    from lockstep_b200 import lssab9_torch as L9
+    rec = json.load(open(os.path.join(HERE, "golden", "golden_keyshift.json")))[case["tag"]]
+    q, k, v, dmax = case["q"], case["k"], case["v"], case["dmax"]
+    name = "sink" if sink else "nosink"
+    _, _, _, d8 = A.quant_values_keyshift(torch.from_numpy(v).cuda()[None], dmax, sink)
+    T = q.shape[1]
+    assert GD.sha(d8[0, :, :T].cpu().numpy()) == rec["d8_" + name]
+    out = G.lssab9_attention(q, k, v, sink_alone=sink, v_keyshift=dmax)
+    assert FX.digest(_bits(out)) == rec["out_" + name]
+    attn = L9.make_lssab9_long_attn(sink_alone=sink, v_keyshift=dmax)
+    o, _ = attn(None, *(torch.from_numpy(x).cuda()[None] for x in (q, k, v)), None)
+    assert np.array_equal(_bits(o[0].transpose(0, 1).cpu().numpy()), _bits(out))
