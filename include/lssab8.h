@@ -211,7 +211,9 @@ int lssab8_decode_prep_kv(const void* k, const void* v, int dtype, int B, int KV
  * bit.  The float cache: token t, kv head g, channel c at k + seq_off[b] + t*st + g*sg + c
  * (src_block_table NULL), or, for a paged cache, at
  * k + src_block_table[b, t / 16] * src_page_stride + (t % 16) * st + g*sg + c
- * (src_block_table [B, max_pages], 16-token pages, e.g. the same table as the lattice's).
+ * (src_block_table [B, max_pages], 16-token pages, e.g. the same table as the lattice's; the
+ * cache holds at least num_pages pages, and a source page id outside [0, num_pages) sets the
+ * bad-page device error and the page is not read).
  * Channels contiguous, every row 16-byte aligned, dh in {64, 128}; lattice arguments as in
  * lssab8_decode_prep_kv. */
 int lssab8_kv_append(const void* k, const void* v, int dtype, int B, int KVH, int dh, const int32_t* seq_lens,

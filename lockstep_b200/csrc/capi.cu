@@ -761,7 +761,8 @@ static int kv_lattice_launch(const void* k, const void* v, int dtype, int B, int
     dim3 grid(max_blocks, KVH, 2 * B);                  // K and V blocks in separate CTAs
     const int vmode = sink ? 2 : 0;
     auto kfn = dh == 128 ? kv_lattice_kernel<InT, 128> : kv_lattice_kernel<InT, 64>;
-    kfn<<<grid, 256, 0, s>>>(static_cast<const InT*>(k), static_cast<const InT*>(v),
+    const int nt = dh == 128 ? KvLattice<InT, 128>::kThreads : KvLattice<InT, 64>::kThreads;
+    kfn<<<grid, nt, 0, s>>>(static_cast<const InT*>(k), static_cast<const InT*>(v),
                              reinterpret_cast<const long long*>(seq_off), st, sg, src_bt, src_ps, B, KVH, seq_lens,
                              start_lens, block_table, max_pages, max_blocks, num_pages, vmode, k8p, v8p, ek, ev, ev0,
                              err);

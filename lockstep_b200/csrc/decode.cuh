@@ -398,28 +398,74 @@ decode_prep_kernel(const InT* __restrict__ ksrc, const InT* __restrict__ vsrc, c
 
 // The paged lattice writer, vectorised, with append-only semantics (the engine's per-step prep,
 // docs/contract/BLOCK_EXPONENT_VARIANT.md:53-55, 212-215: a complete 128-key block never changes;
-// the open block's exponents and values are recomputed from its present rows).  One CTA of 256
-// threads per (128-key block, kv head, sequence, tensor): K and V blocks are separate CTAs (their
-// exponents are independent), which keeps a CTA's registers low enough for several per SM.  Blocks
-// below start_lens[b] / 128 (complete before this append) are left as they are.  The float source
-// is read once in 16-byte vectors (channels contiguous) and kept in registers for the amax and the
-// quantisation; K rows go straight to their pages, V is transposed per page through shared memory,
-// and both are written in 16-byte (K: 8-byte) stores.  Token t of sequence b, kv head g, channel c
-// is read at
+// the open block's exponents and values are recomputed from its present rows).  One CTA per
+// (128-key block, kv head, sequence, tensor): K and V blocks are separate CTAs (their exponents are
+// independent).  Blocks below start_lens[b] / 128 (complete before this append) are left as they
+// are.  Thread (pl, cv) holds page pl of the block (16 keys) x channels [cv EPV, cv EPV + EPV) in
+// registers, read once as 16 16-byte vectors, for the amax and the quantisation; only the block
+// maximum passes through shared memory.  A K page row is 8 (bf16) bytes per thread, stored as it
+// is; a V page is the transposed [channel][16 keys], so each of the thread's channels becomes one
+// 16-byte row packed in registers.  Token t of sequence b, kv head g, channel c is read at
 //   src + seq_off[b] + t * st + g * sg + c                 (src_bt == nullptr), or
-//   src + src_bt[b, t / 16] * src_ps + (t % 16) * st + g * sg + c  (a paged source cache).
+//   src + src_bt[b, t / 16] * src_ps + (t % 16) * st + g * sg + c  (a paged source cache whose
+//                                                           page ids are below num_pages).
 // Rows past the sequence end inside its last page are written as zeros.
 template <typename InT, int DH>
-__global__ void __launch_bounds__(256)
+struct KvLattice {
+  static constexpr int kEpv = 16 / (int)sizeof(InT);        // channels per 16-byte vector
+  static constexpr int kVpr = DH / kEpv;                    // vectors per key row
+  static constexpr int kThreads = 8 * kVpr;                 // 8 pages x kVpr
+};
+
+// four int8 values (clamped to [-127, 127]) packed into one word, lowest first
+__device__ __forceinline__ uint32_t pack4_s8(int a, int b, int c, int d) {
+  return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
+}
+
+// max |x| over a 16-byte vector, on the bit patterns: with the sign cleared a pattern is monotone
+// in |x| (zeros, subnormals and infinity included), and a NaN (a pattern above infinity's) counts
+// as 0, which is fmaxf's rule of ignoring NaN.  acc holds the running maximum pattern(s): two
+// 16-bit lanes for bf16 / fp16, one word for f32; absmax_value turns it into the float.
+template <typename InT>
+__device__ __forceinline__ uint32_t absmax_acc(uint32_t acc, const uint4& v) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  if constexpr (sizeof(InT) == 2) {
+    constexpr uint32_t kInf2 = std::is_same<InT, __half>::value ? 0x7C007C00u : 0x7F807F80u;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t a = w[i] & 0x7FFF7FFFu;
+      acc = __vmaxu2(acc, a & ~__vcmpgtu2(a, kInf2));
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t a = w[i] & 0x7FFFFFFFu;
+      acc = max(acc, a > 0x7F800000u ? 0u : a);
+    }
+  }
+  return acc;
+}
+template <typename InT>
+__device__ __forceinline__ float absmax_value(uint32_t acc) {
+  if constexpr (sizeof(InT) == 2) {
+    const uint32_t h = max(acc & 0xFFFFu, acc >> 16);
+    if constexpr (std::is_same<InT, __half>::value) return __half2float(__ushort_as_half((unsigned short)h));
+    else return __uint_as_float(h << 16);
+  } else {
+    return __uint_as_float(acc);
+  }
+}
+
+template <typename InT, int DH>
+__global__ void __launch_bounds__(KvLattice<InT, DH>::kThreads)
 kv_lattice_kernel(const InT* __restrict__ ksrc, const InT* __restrict__ vsrc, const long long* __restrict__ seq_off,
                   long long st, long long sg, const int32_t* __restrict__ src_bt, long long src_ps, int B, int KVH,
                   const int32_t* __restrict__ seq_lens, const int32_t* __restrict__ start_lens,
                   const int32_t* __restrict__ block_table, int max_pages, int max_blocks, int num_pages, int vmode,
                   int8_t* __restrict__ k8p, int8_t* __restrict__ v8p, int32_t* __restrict__ ek,
                   int32_t* __restrict__ ev, int32_t* __restrict__ ev0, int* __restrict__ err) {
-  constexpr int EPV = 16 / sizeof(InT);                  // elements per 16-byte vector
-  constexpr int VPR = DH / EPV;                          // vectors per row
-  constexpr int NV = 128 * VPR / 256;                    // vectors per thread
+  using K = KvLattice<InT, DH>;
+  constexpr int EPV = K::kEpv, VPR = K::kVpr, NW = K::kThreads / 32;
   const int blk = blockIdx.x, g = blockIdx.y, b = blockIdx.z >> 1;
   const bool isv = (blockIdx.z & 1) != 0;                // this CTA's tensor: K (0) or V (1)
   const int L = seq_lens[b];
@@ -430,35 +476,38 @@ kv_lattice_kernel(const InT* __restrict__ ksrc, const InT* __restrict__ vsrc, co
     return;
   }
   if (start_lens && blk < start_lens[b] / kKB) return;   // complete before this append: unchanged
-  const int lo = blk * kKB;
+  const int pl = threadIdx.x / VPR, cv = threadIdx.x % VPR;
+  const int lo = blk * kKB + pl * 16;                    // this thread's first key
   const int npages = min(8, ((L + 15) / 16) - blk * 8);  // pages of this block that exist
   const int32_t* bt = block_table + (long long)b * max_pages;
   const InT* src = isv ? vsrc : ksrc;
-  __shared__ float red[2][8];
-  __shared__ __align__(16) int8_t vt[DH][128 + 16];      // V^T of the block, one row per channel
-  const bool split0 = isv && (vmode == 2) && (blk == 0) && (L > 1);
-  uint4 x[NV];
-  float m = 0.0f, m0 = 0.0f;
-#pragma unroll
-  for (int i = 0; i < NV; ++i) {
-    const int u = threadIdx.x + 256 * i;
-    const int r = u / VPR, cv = u % VPR;
-    const int t = lo + r;
-    x[i] = make_uint4(0u, 0u, 0u, 0u);
-    if (t < L) {
-      const long long row = src_bt ? (long long)src_bt[(long long)b * max_pages + t / 16] * src_ps + (long long)(t % 16) * st
-                                   : seq_off[b] + (long long)t * st;
-      const long long o = row + (long long)g * sg + cv * EPV;
-      if (o & (EPV - 1)) atomicOr(err, kDevAlign);       // a row off the 16-byte grid: refuse it
-      else x[i] = *reinterpret_cast<const uint4*>(src + o);
+  __shared__ float red[2][NW];
+  const bool split0 = isv && (vmode == 2) && (blk == 0) && (L > 1);   // key 0 alone (B9.1)
+  bool have = lo < L;
+  long long rb = 0;                                      // element offset of key lo, channel cv EPV
+  if (have) {
+    if (src_bt) {
+      const int sp = src_bt[(long long)b * max_pages + blk * 8 + pl];
+      if (sp < 0 || sp >= num_pages) { atomicOr(err, kDevBadPage); have = false; }
+      else rb = (long long)sp * src_ps + g * sg + cv * EPV;
+    } else {
+      rb = seq_off[b] + (long long)lo * st + g * sg + cv * EPV;
     }
-    const InT* xe = reinterpret_cast<const InT*>(&x[i]);
-#pragma unroll
-    for (int e = 0; e < EPV; ++e) {
-      const float a = fabsf(to_f32(xe[e]));
-      if (split0 && t == 0) m0 = fmaxf(m0, a); else m = fmaxf(m, a);
-    }
+    if (rb & (EPV - 1)) { atomicOr(err, kDevAlign); have = false; }   // a row off the 16-byte grid
   }
+  uint4 x[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    x[i] = make_uint4(0u, 0u, 0u, 0u);
+    if (have && lo + i < L) x[i] = __ldg(reinterpret_cast<const uint4*>(src + rb + i * st));
+  }
+  uint32_t am = 0u, am0 = 0u;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    if (i == 0 && split0 && pl == 0) am0 = absmax_acc<InT>(0u, x[0]);
+    else am = absmax_acc<InT>(am, x[i]);
+  }
+  float m = absmax_value<InT>(am), m0 = absmax_value<InT>(am0);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
@@ -467,43 +516,41 @@ kv_lattice_kernel(const InT* __restrict__ ksrc, const InT* __restrict__ vsrc, co
   const int w = threadIdx.x >> 5;
   if ((threadIdx.x & 31) == 0) { red[0][w] = m; red[1][w] = m0; }
   __syncthreads();
-  m = 0.0f; m0 = 0.0f;
+  m = red[0][0]; m0 = red[1][0];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) { m = fmaxf(m, red[0][i]); m0 = fmaxf(m0, red[1][i]); }
+  for (int i = 1; i < NW; ++i) { m = fmaxf(m, red[0][i]); m0 = fmaxf(m0, red[1][i]); }
   const int e1 = pow2_exponent(m, (!isv || vmode == 0) ? 40 : 48);
   const int e0 = split0 ? pow2_exponent(m0, 48) : e1;
   const float s1 = pow2f(e1), s0 = pow2f(e0);
+  if (pl < npages) {                                     // the page exists
+    const int pg = bt[blk * 8 + pl];
+    if (pg < 0 || pg >= num_pages) {
+      atomicOr(err, kDevBadPage);
+    } else if (!isv) {                                   // K page [16 keys][DH]: this thread's EPV channels of each key
+      int8_t* kd = k8p + ((long long)pg * KVH + g) * 16 * DH + cv * EPV;
 #pragma unroll
-  for (int i = 0; i < NV; ++i) {
-    const int u = threadIdx.x + 256 * i;
-    const int r = u / VPR, cv = u % VPR;
-    const int t = lo + r;
-    const InT* xe = reinterpret_cast<const InT*>(&x[i]);
-    if (isv) {                                           // V: into the transposed tile
+      for (int i = 0; i < 16; ++i) {
+        const InT* xe = reinterpret_cast<const InT*>(&x[i]);
+        uint32_t kq[EPV / 4];
 #pragma unroll
-      for (int e = 0; e < EPV; ++e) vt[cv * EPV + e][r] = (int8_t)quant8(to_f32(xe[e]), (split0 && t == 0) ? s0 : s1);
-    } else if (r / 16 < npages) {                        // K: straight to the row's page
-      uint32_t kq[EPV / 4 > 0 ? EPV / 4 : 1] = {};
+        for (int q = 0; q < EPV / 4; ++q)
+          kq[q] = pack4_s8(quant8(to_f32(xe[4 * q]), s1), quant8(to_f32(xe[4 * q + 1]), s1),
+                           quant8(to_f32(xe[4 * q + 2]), s1), quant8(to_f32(xe[4 * q + 3]), s1));
+        if constexpr (EPV == 8) *reinterpret_cast<uint2*>(kd + i * DH) = make_uint2(kq[0], kq[1]);
+        else *reinterpret_cast<uint32_t*>(kd + i * DH) = kq[0];
+      }
+    } else {                                             // V page [DH][16 keys]: one 16-byte row per channel
+      int8_t* vd = v8p + (((long long)pg * KVH + g) * DH + cv * EPV) * 16;
 #pragma unroll
-      for (int e = 0; e < EPV; ++e) kq[e / 4] |= (uint32_t)(uint8_t)(int8_t)quant8(to_f32(xe[e]), s1) << (8 * (e % 4));
-      const int pg = bt[blk * 8 + r / 16];
-      if (pg < 0 || pg >= num_pages) { atomicOr(err, kDevBadPage); continue; }
-      int8_t* kd = k8p + (((long long)pg * KVH + g) * 16 + (r % 16)) * DH + cv * EPV;
-      if constexpr (EPV == 8) *reinterpret_cast<uint2*>(kd) = make_uint2(kq[0], kq[1]);
-      else if constexpr (EPV == 4) *reinterpret_cast<uint32_t*>(kd) = kq[0];
-      else *reinterpret_cast<uint4*>(kd) = make_uint4(kq[0], kq[1], kq[2], kq[3]);
-    }
-  }
-  if (isv) {
-    __syncthreads();
-    // V pages: [page][g][channel][16 keys], one 16-byte store per (page, channel)
-    for (int i = threadIdx.x; i < npages * DH; i += 256) {
-      const int pl = i / DH, c = i % DH;
-      const int pg = bt[blk * 8 + pl];
-      if (pg < 0 || pg >= num_pages) { atomicOr(err, kDevBadPage); continue; }
-      const uint32_t* srow = reinterpret_cast<const uint32_t*>(&vt[c][pl * 16]);
-      *reinterpret_cast<uint4*>(v8p + (((long long)pg * KVH + g) * DH + c) * 16) =
-          make_uint4(srow[0], srow[1], srow[2], srow[3]);
+      for (int e = 0; e < EPV; ++e) {
+        int q[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          q[i] = quant8(to_f32(reinterpret_cast<const InT*>(&x[i])[e]), (i == 0 && split0 && pl == 0) ? s0 : s1);
+        *reinterpret_cast<uint4*>(vd + e * 16) = make_uint4(pack4_s8(q[0], q[1], q[2], q[3]), pack4_s8(q[4], q[5], q[6], q[7]),
+                                                           pack4_s8(q[8], q[9], q[10], q[11]),
+                                                           pack4_s8(q[12], q[13], q[14], q[15]));
+      }
     }
   }
   if (threadIdx.x == 0) {

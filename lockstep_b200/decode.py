@@ -135,6 +135,9 @@ def append_kv(kv, keys, values, new_lens, src_block_table=None, check=True):
     else:
         if keys.dim() != 4 or keys.shape[1] != PAGE:
             raise ValueError("paged keys must be [num_pages, 16, KVH, dh]")
+        if keys.shape[0] < kv.num_pages:
+            raise ValueError("the paged float cache must hold the lattice's num_pages pages (its page ids are "
+                             "checked against num_pages)")
         s = keys.stride()
         seq_off, st, sg, sc, ps, sbt = None, s[1], s[2], s[3], s[0], src_block_table
     if sc != 1:
