@@ -254,7 +254,8 @@ int launch_decode_tc_t(const DecodeArgs& a, int max_splits, int num_sms, cudaStr
   const long long chunks = ((long long)a.B * a.KVH * a.max_blocks + kDecChunk - 1) / kDecChunk;
   const int grid = (int)std::min<long long>(chunks, 2LL * std::max(num_sms, 1));   // two CTAs per SM
   if ((rc = launch_pdl(kfn, dim3(grid), dim3(DecWorkers<GQ>::kThreads), smem, st, tk, tq, a))) return rc;
-  return launch_pdl(decode_merge_kernel<SINK, OutT>, dim3(a.KVH, a.B, a.group), dim3(kMergeThreads), 0, st, a);
+  // heads fastest, then kv heads, then the sequences in the plan's longest-first order
+  return launch_pdl(decode_merge_kernel<SINK, OutT>, dim3(a.group, a.KVH, a.B), dim3(kMergeThreads), 0, st, a);
 }
 
 template <bool SINK>
@@ -305,7 +306,7 @@ PrefillWs prefill_ws(int B, int H, int KVH, int T, int dh) {
 }
 
 struct DecodeWs {
-  size_t q8, eq, partA, partM, tickets, blk_off, total;
+  size_t q8, eq, partA, partM, tickets, blk_off, order, total;
 };
 
 DecodeWs decode_ws(int B, int H, int KVH, int dh, int max_blocks) {
@@ -318,6 +319,7 @@ DecodeWs decode_ws(int B, int H, int KVH, int dh, int max_blocks) {
   w.partM = o; o += align256((size_t)B * KVH * max_blocks * gq * 16);
   w.tickets = o; o += align256((size_t)B * KVH * 4);
   w.blk_off = o; o += align256((size_t)(B + 1) * 4);         // the live-block plan
+  w.order = o; o += align256((size_t)B * 4);                 // the refold's sequence order
   w.total = o + 256;
   return w;
 }
@@ -852,6 +854,7 @@ int lssab8_decode(const void* q, int dtype, const int64_t* qs, int B, int H, int
   if (dh == 128) {                                   // the live-block plan; it also zeroes the tickets
     decode_plan_kernel<<<1, kPlanThreads, 0, s>>>(seq_lens, B, max_blocks, max_pages,
                                                   reinterpret_cast<int*>(base + w.blk_off),
+                                                  reinterpret_cast<int*>(base + w.order),
                                                   reinterpret_cast<unsigned int*>(base + w.tickets), B * KVH, ds->err);
     if ((rc = launch_rc())) return rc;
   } else if (cudaMemsetAsync(base + w.tickets, 0, (size_t)B * KVH * 4, s) != cudaSuccess) {
@@ -866,6 +869,7 @@ int lssab8_decode(const void* q, int dtype, const int64_t* qs, int B, int H, int
   a.partM = reinterpret_cast<int4*>(base + w.partM);
   a.tickets = reinterpret_cast<unsigned int*>(base + w.tickets);
   a.blk_off = reinterpret_cast<int*>(base + w.blk_off);
+  a.order = reinterpret_cast<int*>(base + w.order);
   a.out = out; a.os0 = os[0]; a.os1 = os[1]; a.os2 = os[2];
   a.gbase = gbase_of(dh);
   a.err = ds->err;
@@ -928,6 +932,7 @@ int lssab8_decode_noalloc(const void* q, int dtype, const int64_t* qs, int B, in
   if (dh == 128) {                                   // the live-block plan; it also zeroes the tickets
     decode_plan_kernel<<<1, kPlanThreads, 0, s>>>(seq_lens, B, max_blocks, max_pages,
                                                   reinterpret_cast<int*>(base + w.blk_off),
+                                                  reinterpret_cast<int*>(base + w.order),
                                                   reinterpret_cast<unsigned int*>(base + w.tickets), B * KVH, ds->err);
     if ((rc = launch_rc())) return rc;
   } else if (cudaMemsetAsync(base + w.tickets, 0, (size_t)B * KVH * 4, s) != cudaSuccess) {
@@ -942,6 +947,7 @@ int lssab8_decode_noalloc(const void* q, int dtype, const int64_t* qs, int B, in
   a.partM = reinterpret_cast<int4*>(base + w.partM);
   a.tickets = reinterpret_cast<unsigned int*>(base + w.tickets);
   a.blk_off = reinterpret_cast<int*>(base + w.blk_off);
+  a.order = reinterpret_cast<int*>(base + w.order);
   a.out = out; a.os0 = os[0]; a.os1 = os[1]; a.os2 = os[2];
   a.gbase = gbase_of(dh);
   a.err = ds->err;

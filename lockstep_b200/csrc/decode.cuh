@@ -40,6 +40,7 @@ struct DecodeArgs {
   int4* partM;                        // [B, KVH, max_blocks, group] {nb, l_b, eh0, 0}
   unsigned int* tickets;              // [B, KVH], zero before the launch (dh 64)
   int* blk_off;                       // [B + 1] live blocks of the sequences before b (dh 128)
+  int* order;                         // [B] the refold's sequence order, longest first (dh 128)
   void* out; long long os0, os1, os2; // out[b, h, c]
   uint32_t gbase;
   int* err;

@@ -2,8 +2,8 @@
 //
 // Same contract and workspace as decode_kernel (decode.cuh): every 128-key block of a sequence
 // yields EXACT integer block partials (A_b = eh . v8 per head and channel, NB_b, l_b, eh0), and
-// the last CTA of a (sequence, kv head) refolds all blocks in ascending order
-// (reference/lssab8_golden.py:350-394).  What changes is how the partials are produced:
+// a refold folds all blocks of a (sequence, kv head) in ascending order
+// (reference/lssab8_golden.py:350-394).  What changes is how the partials are produced and refolded:
 //
 //   * persistent CTAs walk the list of LIVE (sequence, kv head, block) triples -- numbered by a
 //     per-sequence prefix sum of block counts (decode_plan_kernel), so ragged lengths leave no
@@ -26,8 +26,8 @@
 //     + one named barrier per warpgroup), NB, the 32-bit chain and the T2 gather from a
 //     zero-padded table indexed by d >> 19, write P^T in the core-matrix layout, sum l_b with
 //     redux.sync and shared atomics, and store the partials.
-//   * the refold of each (sequence, kv head) runs afterwards as its own small kernel
-//     (decode_merge_kernel), so no streaming CTA ever stalls on a merge.
+//   * the refold of each (sequence, kv head, head) runs afterwards as its own small kernel
+//     (decode_merge_kernel), longest sequences first, so no streaming CTA ever stalls on a merge.
 #pragma once
 #include "decode.cuh"
 
@@ -114,11 +114,13 @@ struct DecIter {
 // sequence is live when 0 < L and its blocks and pages fit the lattice arrays; one that does not
 // fit gets no blocks and sets kDevBadPage.
 constexpr int kPlanThreads = 1024;
+constexpr int kPlanSortMax = 1024;                 // batches up to this size get the longest-first order
 __global__ void __launch_bounds__(kPlanThreads) decode_plan_kernel(const int32_t* seq_lens, int B, int max_blocks,
-                                                                    int max_pages, int* blk_off, unsigned int* tickets,
-                                                                    int nticket, int* err) {
+                                                                    int max_pages, int* blk_off, int* order,
+                                                                    unsigned int* tickets, int nticket, int* err) {
   __shared__ int warp_sums[kPlanThreads / 32];
   __shared__ int carry;
+  __shared__ int sl[kPlanSortMax];
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
   for (int i = tid; i < nticket; i += kPlanThreads) tickets[i] = 0u;
   if (tid == 0) carry = 0;
@@ -157,6 +159,20 @@ __global__ void __launch_bounds__(kPlanThreads) decode_plan_kernel(const int32_t
     __syncthreads();
     if (tid == 0) carry += warp_sums[kPlanThreads / 32 - 1];
     __syncthreads();
+  }
+  // the refold's sequence order, longest first (ties by index): order[rank(i)] = i with
+  // rank(i) = #{j : L_j > L_i, or L_j == L_i and j < i}; larger batches keep the index order
+  if (B <= kPlanSortMax) {
+    for (int i = tid; i < B; i += kPlanThreads) sl[i] = seq_lens[i];
+    __syncthreads();
+    for (int i = tid; i < B; i += kPlanThreads) {
+      const int Li = sl[i];
+      int r = 0;
+      for (int j = 0; j < B; ++j) r += (sl[j] > Li || (sl[j] == Li && j < i)) ? 1 : 0;
+      order[r] = i;
+    }
+  } else {
+    for (int i = tid; i < B; i += kPlanThreads) order[i] = i;
   }
   if (tid == 0) blk_off[B] = carry;
 }
@@ -450,60 +466,73 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
   }
 }
 
-// The committed-order refold of every (sequence, kv head, head) from its exact block partials:
-// one CTA per (kv head, sequence, head of the group), one thread per channel plus one warp for
-// l.  Per 32-block segment: the partial rows (32 x 512 contiguous bytes) are staged into shared
-// memory with cp.async; warp 0 derives the segment's fold schedule, which depends on the block
-// and head only (running max by a prefix-max scan, rescale distance D, skip distance s, the
-// scale 2^-(s + e_v), and the segment -> row step); then every channel thread folds its channel
-// with one exact multiply-add per block while lane 0 of warp 4 folds l, in the same order
-// (reference/lssab8_golden.py:257-335, 350-394).  A block past the skip window gets scale +0,
-// which leaves O bit-identical (O is never -0).
-constexpr int kMergeThreads = 160;
+// The committed-order refold of the block partials (reference/lssab8_golden.py:257-335, 350-394):
+// one CTA of 64 threads per (head, kv head, sequence), the sequences in the plan's longest-first
+// order, so the longest refolds start first and the shortest fill the tail of the grid.  Per
+// 32-block segment the partial rows are staged in shared memory with cp.async in one round trip
+// while lane u of warp 0 computes block u's fold schedule (the running maximum by a prefix-max
+// scan, the rescale distance before the block, its skip distance and term scale) from the
+// segment's (NB_b, l_b, e_v) -- prefetched into registers during the previous segment's fold --
+// and then thread t folds channels 2t and 2t + 1 with it, one exact multiply-add per block and
+// channel, while thread 32 also folds l, in the same order.  A block past the skip window gets
+// scale +0, which leaves O bit-identical (O is never -0).
+constexpr int kMergeThreads = 64;
 template <bool SINK, typename OutT>
 __global__ void __launch_bounds__(kMergeThreads) decode_merge_kernel(const DecodeArgs p) {
   constexpr int DH = 128;
   __shared__ __align__(16) int sA[kSEG][DH];
   __shared__ int2 sM[kSEG];
-  __shared__ int sEv[kSEG];
   __shared__ int sD[kSEG];                 // rescale distance before block u (0: none)
   __shared__ int sS[kSEG];                 // skip distance of block u
   __shared__ float sSc[kSEG];              // 2^-(s_u + e_v,u), or +0 past the skip window
-  __shared__ int sSeg[4];                  // segment -> row: D2, s2 (and the segment's NB)
+  __shared__ int sSeg[2];                  // segment -> row: D2, s2
   __shared__ float sLrow;
   pdl_wait();                                          // every block partial is written
-  const int g = blockIdx.x, b = blockIdx.y, h = blockIdx.z, c = threadIdx.x;
-  const int lane = c & 31;
+  const int h = blockIdx.x, g = blockIdx.y;
+  const int b = p.order[blockIdx.z];
+  const int t = threadIdx.x, lane = t & 31, w = t >> 5;
+  const int c0 = 2 * t;                                // this thread's channels c0, c0 + 1
   const int gq = p.group;
   const int L = p.seq_lens[b];
   const int nblk = (L + kKB - 1) / kKB;
   if (L <= 0 || nblk > p.max_blocks || (L + 15) / 16 > p.max_pages) return;   // flagged by the plan
   const long long bg = (long long)b * p.KVH + g;
-  int v0c = 0, evs0 = 0, eh0 = 0;
-  if (SINK && L > 1 && c < DH) {
+  const int4* pm = p.partM + (bg * p.max_blocks) * gq + h;      // block u's {NB, l_b, eh0} at pm[u * gq]
+  const int32_t* evb = p.ev + bg * p.max_blocks;
+  int v0a = 0, v0b = 0, evs0 = 0, eh0 = 0;
+  if (SINK && L > 1) {
     const int pg = p.block_table[(long long)b * p.max_pages];
-    v0c = (int)p.v8p[((long long)pg * p.KVH + g) * (16 * DH) + c * 16 + 0];
+    const int8_t* v0 = p.v8p + ((long long)pg * p.KVH + g) * (16 * DH);
+    v0a = (int)v0[c0 * 16];
+    v0b = (int)v0[(c0 + 1) * 16];
     evs0 = p.ev0[bg];
-    eh0 = __ldcg(&p.partM[(bg * p.max_blocks) * gq + h]).z;
+    eh0 = __ldcg(&pm[0]).z;
   }
-  float Orow = 0.0f, lrow = 0.0f;          // lrow: warp 4 lane 0 only
-  int nbrow = 0;                           // warp 0 lane 0 only
+  float Oa = 0.0f, Ob = 0.0f, lrow = 0.0f;             // lrow: thread 32 only
+  int nbrow = 0;                                       // thread 0 only
+  int2 mn = make_int2(INT32_MIN, 0);                   // warp 0: the segment's schedule inputs, one block per lane
+  int evn = 0;
+  if (w == 0 && lane < min(kSEG, nblk)) {
+    mn = __ldcg(reinterpret_cast<const int2*>(&pm[lane * gq]));
+    evn = evb[lane];
+  }
   for (int s0 = 0; s0 < nblk; s0 += kSEG) {
     const int n = min(kSEG, nblk - s0);
-    for (int i = c; i < n * (DH / 4); i += blockDim.x) {     // 16-byte pieces of the n partial rows
+    for (int i = t; i < n * (DH / 4); i += kMergeThreads) {     // 16-byte pieces of the n partial rows
       const int u = i / (DH / 4), q = i % (DH / 4);
       const int32_t* src = p.partA + ((bg * p.max_blocks + s0 + u) * gq + h) * DH + q * 4;
       asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(&sA[u][q * 4])), "l"(src) : "memory");
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
-    if (c < 32) {
+    if (w == 0) {
       // ---- the segment's schedule: lane u owns block u
       const bool live = lane < n;
-      int2 m = make_int2(INT32_MIN, 0);
-      int ev = 0;
-      if (live) {
-        m = __ldcg(reinterpret_cast<const int2*>(&p.partM[(bg * p.max_blocks + s0 + lane) * gq + h]));
-        ev = p.ev[bg * p.max_blocks + s0 + lane];
+      const int2 m = mn;
+      const int ev = evn;
+      const int s1 = s0 + kSEG;                              // the next segment's inputs, in flight during the fold
+      if (s1 < nblk && lane < min(kSEG, nblk - s1)) {
+        mn = __ldcg(reinterpret_cast<const int2*>(&pm[(s1 + lane) * gq]));
+        evn = evb[s1 + lane];
       }
       int run = m.x;                                         // inclusive prefix max of NB_b
 #pragma unroll
@@ -519,7 +548,6 @@ __global__ void __launch_bounds__(kMergeThreads) decode_merge_kernel(const Decod
       const bool add = sg <= kSWIN;
       if (live) {
         sM[lane] = m;
-        sEv[lane] = ev;
         sD[lane] = D > 0 ? D : 0;
         sS[lane] = sg;
         sSc[lane] = add ? pow2f(-(sg + ev)) : 0.0f;
@@ -537,17 +565,23 @@ __global__ void __launch_bounds__(kMergeThreads) decode_merge_kernel(const Decod
     asm volatile("cp.async.wait_group 0;" ::: "memory");
     __syncthreads();
     const int D2 = sSeg[0], s2 = sSeg[1];
-    if (c < DH) {
-      float O = 0.0f;
-      for (int u = 0; u < n; ++u) {
-        const int Du = sD[u];
-        if (Du > 0) O = rescale(O, Du);                      // block-uniform branch
-        if (SINK && s0 + u == 0 && L > 1) O = fold_term(O, eh0 * v0c, pow2f(-evs0));
-        O = fold_term(O, sA[u][c], sSc[u]);
+    float xa = 0.0f, xb = 0.0f;
+    for (int u = 0; u < n; ++u) {
+      const int Du = sD[u];
+      if (Du > 0) { xa = rescale(xa, Du); xb = rescale(xb, Du); }   // block-uniform branch
+      if (SINK && s0 + u == 0 && L > 1) {
+        const float sc0 = pow2f(-evs0);
+        xa = fold_term(xa, eh0 * v0a, sc0);
+        xb = fold_term(xb, eh0 * v0b, sc0);
       }
-      if (D2 > 0) Orow = rescale(Orow, D2);
-      if (s2 <= kSWIN) Orow = __fadd_rn(Orow, rescale(O, s2));
-    } else if (c == DH) {                                    // l: the same rules, in the same order
+      const int2 av = *reinterpret_cast<const int2*>(&sA[u][c0]);
+      const float sc = sSc[u];
+      xa = fold_term(xa, av.x, sc);
+      xb = fold_term(xb, av.y, sc);
+    }
+    if (D2 > 0) { Oa = rescale(Oa, D2); Ob = rescale(Ob, D2); }
+    if (s2 <= kSWIN) { Oa = __fadd_rn(Oa, rescale(xa, s2)); Ob = __fadd_rn(Ob, rescale(xb, s2)); }
+    if (t == 32) {                                           // l: the same rules, in the same order
       float lseg = 0.0f;
       for (int u = 0; u < n; ++u) {
         const int Du = sD[u];
@@ -560,11 +594,10 @@ __global__ void __launch_bounds__(kMergeThreads) decode_merge_kernel(const Decod
     }
     __syncthreads();                                         // the stage and schedule are refilled next
   }
-  if (c >= DH) return;
   const float lr = sLrow;
-  const float y = (lr != 0.0f) ? __fdiv_rn(Orow, lr) : 0.0f;
-  OutT* dst = reinterpret_cast<OutT*>(p.out) + b * p.os0 + (long long)(g * gq + h) * p.os1 + c * p.os2;
-  *dst = from_f32<OutT>(y);
+  OutT* dst = reinterpret_cast<OutT*>(p.out) + b * p.os0 + (long long)(g * gq + h) * p.os1 + c0 * p.os2;
+  dst[0] = from_f32<OutT>(lr != 0.0f ? __fdiv_rn(Oa, lr) : 0.0f);
+  dst[p.os2] = from_f32<OutT>(lr != 0.0f ? __fdiv_rn(Ob, lr) : 0.0f);
 }
 
 }  // namespace lssab8
