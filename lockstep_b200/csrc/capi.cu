@@ -481,6 +481,28 @@ int lssab8_device_errors(int clear, void* stream, int* bits) {
   return kOk;
 }
 
+// The decode's query quantiser ([B, H, dh] rows): the vector kernel is launched with
+// programmatic dependent launch, so it runs beside the decode plan kernel before it (which it does
+// not read); it waits for the plan before it completes, so the streaming kernel's wait on it
+// covers the plan too.  Other layouts take lssab8_quant_rows.
+static int quant_queries_pdl(const void* q, int dtype, int B, int H, int dh, const int64_t* q4, int8_t* q8,
+                             int32_t* eq, cudaStream_t st) {
+  Strides4 s{q4[0], q4[1], q4[2], q4[3]};
+  return with_in_dtype(dtype, [&](auto tag) -> int {
+    using InT = std::remove_const_t<std::remove_pointer_t<decltype(tag)>>;
+    if (!vec_ok<InT>(q, s, dh)) return lssab8_quant_rows(q, dtype, B, H, 1, dh, q4, 1, q8, eq, st);
+    constexpr int N = Vec16<InT>::kN;
+    const int rpw = 32 / (dh / N);
+    const long long per_cta = 8LL * rpw * kRowsPerLane;
+    const int grid = (int)(((long long)B * H + per_cta - 1) / per_cta);
+    if (dh == 128)
+      return launch_pdl(quant_rows_vec_kernel<InT, 128>, dim3(grid), dim3(256), 0, st, static_cast<const InT*>(q), s, B,
+                        H, 1, 1, q8, eq);
+    return launch_pdl(quant_rows_vec_kernel<InT, 64>, dim3(grid), dim3(256), 0, st, static_cast<const InT*>(q), s, B, H,
+                      1, 1, q8, eq);
+  });
+}
+
 int lssab8_quant_rows(const void* x, int dtype, int B, int H, int T, int dh, const int64_t* xs, int Tpad,
                       int8_t* q8, int32_t* eq, void* stream) {
   if (!x || !q8 || !eq || !shape_ok(B, H, H, T, dh) || Tpad < T || !strides_ok(xs, 4)) return kErrArg;
@@ -860,7 +882,9 @@ int lssab8_decode(const void* q, int dtype, const int64_t* qs, int B, int H, int
   } else if (cudaMemsetAsync(base + w.tickets, 0, (size_t)B * KVH * 4, s) != cudaSuccess) {
     return kErrCuda;
   }
-  if ((rc = lssab8_quant_rows(q, dtype, B, H, 1, dh, q4, 1, q8, eq, stream))) return rc;
+  if ((rc = dh == 128 ? quant_queries_pdl(q, dtype, B, H, dh, q4, q8, eq, s)
+                      : lssab8_quant_rows(q, dtype, B, H, 1, dh, q4, 1, q8, eq, stream)))
+    return rc;
   DecodeArgs a{};
   a.B = B; a.H = H; a.KVH = KVH; a.dh = dh; a.group = H / KVH; a.max_blocks = max_blocks; a.max_pages = max_pages;
   a.split_blocks = split_blocks; a.num_pages = num_pages; a.seq_lens = seq_lens; a.block_table = block_table;
@@ -938,7 +962,9 @@ int lssab8_decode_noalloc(const void* q, int dtype, const int64_t* qs, int B, in
   } else if (cudaMemsetAsync(base + w.tickets, 0, (size_t)B * KVH * 4, s) != cudaSuccess) {
     return kErrCuda;
   }
-  if ((rc = lssab8_quant_rows(q, dtype, B, H, 1, dh, q4, 1, q8, eq, stream))) return rc;
+  if ((rc = dh == 128 ? quant_queries_pdl(q, dtype, B, H, dh, q4, q8, eq, s)
+                      : lssab8_quant_rows(q, dtype, B, H, 1, dh, q4, 1, q8, eq, stream)))
+    return rc;
   DecodeArgs a{};
   a.B = B; a.H = H; a.KVH = KVH; a.dh = dh; a.group = H / KVH; a.max_blocks = max_blocks; a.max_pages = max_pages;
   a.split_blocks = split_blocks; a.num_pages = num_pages; a.seq_lens = seq_lens; a.block_table = block_table;

@@ -121,6 +121,7 @@ __global__ void __launch_bounds__(kPlanThreads) decode_plan_kernel(const int32_t
   __shared__ int warp_sums[kPlanThreads / 32];
   __shared__ int carry;
   __shared__ int sl[kPlanSortMax];
+  pdl_launch_dependents();                         // the query quantiser runs beside the plan
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
   for (int i = tid; i < nticket; i += kPlanThreads) tickets[i] = 0u;
   if (tid == 0) carry = 0;

@@ -319,6 +319,10 @@ quant_rows_vec_kernel(const InT* __restrict__ x, Strides4 xs, int B, int H, int 
                       int8_t* __restrict__ q8, int32_t* __restrict__ eq) {
   pdl_launch_dependents();                             // a PDL-launched consumer may start its setup
   quant_rows_vec<InT, DH>((int)blockIdx.x, x, xs, B, H, T, Tpad, q8, eq);
+  // launched with programmatic dependent launch after a kernel it does not read (the decode
+  // plan), it still completes only after that kernel, so a consumer's wait on this grid covers
+  // both (a no-op otherwise)
+  pdl_wait();
 }
 
 // P2/P3 fast path: one CTA of 256 threads per (block, kv head, batch); the block's 128 x DH
