@@ -60,12 +60,16 @@ def alloc_paged(B, KVH, dh, max_len, num_pages, device, sink=False):
     )
 
 
-def build_paged_kv(keys, values, seq_lens, block_table, num_pages, sink=False, cu_seqlens=None, check=True):
+def build_paged_kv(keys, values, seq_lens, block_table, num_pages, sink=False, cu_seqlens=None, check=True,
+                   out=None):
     """Quantise K/V into a paged lattice.
 
     keys/values: dense [B, KVH, L, dh] (then cu_seqlens is None and seq_lens[b] <= L), or flat
     [N, KVH, dh] with cu_seqlens [B+1] (int64, host or device) giving each sequence's first token.
-    seq_lens [B] int32, block_table [B, max_pages] int32 (CUDA tensors)."""
+    seq_lens [B] int32, block_table [B, max_pages] int32 (CUDA tensors).  out: an existing
+    PagedKV of the same B, KVH, dh, num_pages and sink with room for the longest sequence, whose
+    buffers are rewritten in place (its pages outside the sequences keep their contents) instead of
+    allocating a new lattice; it is returned with the new seq_lens and block_table."""
     dev = _A._require_cuda(keys, values, seq_lens, block_table)
     if keys.dtype != values.dtype or keys.shape != values.shape:
         raise ValueError("keys and values must share shape and dtype")
@@ -90,7 +94,13 @@ def build_paged_kv(keys, values, seq_lens, block_table, num_pages, sink=False, c
         raise ValueError("keys and values must share strides")
     max_pages = block_table.shape[1]
     Lcap = max(int(Lmax), 1)
-    a = alloc_paged(B, KVH, dh, Lcap, num_pages, dev, sink)
+    if out is None:
+        a = alloc_paged(B, KVH, dh, Lcap, num_pages, dev, sink)
+    else:
+        if (out.ek.shape[0] != B or out.KVH != KVH or out.dh != dh or out.num_pages != num_pages or
+                out.sink != bool(sink) or out.max_blocks * KB < Lcap):
+            raise ValueError("out: a lattice of another shape")
+        a = dict(k8p=out.k8p, v8p=out.v8p, ek=out.ek, ev=out.ev, ev0=out.ev0, max_blocks=out.max_blocks)
     seq_off = seq_off.to(dev)
     with torch.cuda.device(dev):
         _lib.check(_lib.load().lssab8_decode_prep_kv(
@@ -163,12 +173,16 @@ def identity_pages(B, L, device):
     return bt, B * P
 
 
-def contiguous_kv(keys, values, sink=False, check=True):
-    """Lattice of a dense cache keys/values [B, KVH, L, dh] (every sequence of length L)."""
+def contiguous_kv(keys, values, sink=False, check=True, out=None):
+    """Lattice of a dense cache keys/values [B, KVH, L, dh] (every sequence of length L); out: a
+    lattice from an earlier call of the same shape, rewritten in place."""
     B, KVH, L, dh = keys.shape
-    bt, npages = identity_pages(B, L, keys.device)
-    seq_lens = torch.full((B,), L, dtype=torch.int32, device=keys.device)
-    return build_paged_kv(keys, values, seq_lens, bt, npages, sink=sink, check=check)
+    if out is not None:
+        bt, npages, seq_lens = out.block_table, out.num_pages, out.seq_lens
+    else:
+        bt, npages = identity_pages(B, L, keys.device)
+        seq_lens = torch.full((B,), L, dtype=torch.int32, device=keys.device)
+    return build_paged_kv(keys, values, seq_lens, bt, npages, sink=sink, check=check, out=out)
 
 
 def decode(q, kv, split_blocks=4, out=None, out_dtype=None, check=True):

@@ -3,7 +3,8 @@ take it for channel-contiguous, 16-byte aligned rows) against the generic per-el
 (decode_prep_kernel, taken for every other layout -- here a channel-strided view of the same
 values): int8 pages, block exponents and the sink exponent bit for bit, for bf16, fp16 and f32
 inputs, dh 64 and 128, sink off and on, ragged lengths over a shuffled page table, and blocks
-holding signed zeros, subnormals, infinities, NaN and values at the int8 clamp."""
+holding signed zeros, subnormals, infinities, NaN and values at the int8 clamp; and the in-place
+rewrite of an existing lattice (build_paged_kv(out=...)) equals a fresh build."""
 import pytest
 import torch
 
@@ -55,3 +56,9 @@ def test_vectorised_writer_equals_generic_writer(dtype, dh, sink):
         assert torch.equal(getattr(a, name), getattr(b, name)), name
     if sink:
         assert torch.equal(a.ev0, b.ev0)
+    # rewriting an existing lattice in place (out=): one built from other values (K and V swapped)
+    c = D.build_paged_kv(v, k, lens, bt, num_pages, sink=sink)
+    c2 = D.build_paged_kv(k, v, lens, bt, num_pages, sink=sink, out=c)
+    assert c2.k8p.data_ptr() == c.k8p.data_ptr()
+    for name in ("k8p", "v8p", "ek", "ev") + (("ev0",) if sink else ()):
+        assert torch.equal(getattr(a, name), getattr(c2, name)), name
