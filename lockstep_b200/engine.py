@@ -20,9 +20,9 @@ this library, in the engine's own terms:
     open block and new blocks are quantised), then runs each prompt chunk through the block-aligned
     chunked prefill and every generated row through one split-KV decode call.
 
-A vLLM attention backend wraps this forward pass: its metadata builder supplies query_start_loc,
-seq_lens, block_table and slot_mapping, and the scheduler hook supplies the prefill flags and the
-128-aligned chunk boundaries.
+lockstep_b200.vllm_backend wraps this forward pass as a vLLM attention backend: its metadata
+builder supplies query_start_loc, seq_lens, block_table, slot_mapping and the scheduler's prefill
+flags; the 128-aligned chunk boundaries are the scheduler's to keep.
 """
 from dataclasses import dataclass
 
@@ -66,21 +66,44 @@ class LatticeLayer:
         self.ev0 = torch.zeros((max_seqs, KVH), dtype=torch.int32, device=device)
         self.lens = [0] * max_seqs
         self.slot_of = {}                                 # first page -> slot
+        self.last_use = [0] * max_seqs                    # step of the slot's last use
+        self.step = 0
 
     def slots(self, first_pages, lens_before):
-        """Slots of the step's sequences; a sequence seen for the first time (its length before
-        the step is 0) takes a free slot."""
+        """Slots of the step's sequences.  A sequence seen for the first time (its length before
+        the step is 0) takes a free slot, or the least recently used one of a sequence not in this
+        step (an engine that never calls release() reuses its finished sequences' slots this way).
+        A sequence that continues (length before > 0) must still hold its slot: if it was taken,
+        its block exponents are gone and the step is refused."""
+        self.step += 1
         out = []
         for fp, l0 in zip(first_pages, lens_before):
             s = self.slot_of.get(fp)
-            if s is None or l0 == 0:
-                if s is None:
-                    used = set(self.slot_of.values())
-                    s = next(i for i in range(len(self.lens)) if i not in used)
-                    self.slot_of[fp] = s
-                self.lens[s] = 0
+            if s is None:
+                if l0 != 0:
+                    raise RuntimeError("the sequence with first page %d continues at length %d, but its lattice "
+                                       "slot was reused (more live sequences than slots)" % (fp, l0))
+                s = self._take_slot()
+                self.slot_of[fp] = s
+            if l0 == 0:
+                self.lens[s] = 0                          # a new sequence (possibly on a reused first page)
+            self.last_use[s] = self.step
             out.append(s)
         return out
+
+    def _take_slot(self):
+        used = set(self.slot_of.values())
+        for i in range(len(self.lens)):
+            if i not in used:
+                return i
+        idle = [i for i in range(len(self.lens)) if self.last_use[i] < self.step]
+        if not idle:
+            raise RuntimeError("more sequences in one step than lattice slots")
+        victim = min(idle, key=lambda i: self.last_use[i])
+        for fp, s in list(self.slot_of.items()):
+            if s == victim:
+                del self.slot_of[fp]
+        return victim
 
     def release(self, first_page):
         """Forget a finished sequence (the engine frees its pages)."""
@@ -104,7 +127,8 @@ class Lssab8Attention:
 
     def forward(self, layer, query, key, value, k_cache, v_cache, meta, out=None):
         """query [ntok, H, dh], key / value [ntok, KVH, dh] (this step's new tokens), k_cache /
-        v_cache [num_pages, 16, KVH, dh] (the engine's float cache) -> out [ntok, H, dh] in
+        v_cache [num_pages, 16, KVH, dh] (the engine's float cache; rows and channels contiguous,
+        any page stride) -> out [ntok, H, dh] in
         query.dtype.  Prompt chunks must start on a multiple of 128 tokens."""
         st = self.layers[layer]
         dev = query.device
@@ -115,11 +139,11 @@ class Lssab8Attention:
         before = [lens[i] - qlen[i] for i in range(nseq)]
         if out is None:
             out = torch.empty_like(query)
-        # 1. the step's keys and values into the engine's float cache
-        kflat = k_cache.view(-1, self.KVH, self.dh)
-        vflat = v_cache.view(-1, self.KVH, self.dh)
-        kflat.index_copy_(0, meta.slot_mapping, key.to(k_cache.dtype))
-        vflat.index_copy_(0, meta.slot_mapping, value.to(v_cache.dtype))
+        # 1. the step's keys and values into the engine's float cache (by page and row, so a cache
+        #    whose pages are strided -- K and V interleaved per page -- is written in place)
+        page, row = meta.slot_mapping // PAGE, meta.slot_mapping % PAGE
+        k_cache[page, row] = key.to(k_cache.dtype)
+        v_cache[page, row] = value.to(v_cache.dtype)
         # 2. the lattice: the open block and new blocks of every sequence, from the float cache
         bt = meta.block_table.to(device=dev, dtype=torch.int32)
         if bt.shape[1] < st.max_pages:
