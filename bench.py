@@ -10,8 +10,8 @@ its heads -- whose epilogue stores each finished output tile into its own [B, T,
 and, over NVLink, into every other rank's (CUDA IPC peer buffers: the gather fused into the
 kernel) -- and a closing barrier; value = 8.797e12 ops / the max-over-ranks step time (strong
 scaling: the total work is fixed).  The NCCL all-gather form of the same step is timed beside
-it.  Inputs are resident in HBM when the timed region starts; L2 is flushed (a 512 MB write)
-before every timed step, outside the timed events.
+it.  Inputs are resident in HBM when the timed region starts; L2 is flushed (a 512 MB write, then a
+512 MB read that evicts the write's dirty lines) before every timed step, outside the timed events.
 
 Also in the line: the compute alone and the gather alone; the prefill kernel's roofline; the
 end-to-end public-API call (pinned host shard -> device -> gathered -> this rank's rows back to
@@ -126,10 +126,15 @@ def load_json(p, key=None):
 
 
 class Timer:
-    """CUDA-event timing on the current stream, L2 flushed before every timed repetition."""
+    """CUDA-event timing on the current stream, L2 flushed before every timed repetition: a 512 MB
+    write, then a 512 MB read of the same buffer.  The read evicts the write's dirty lines (their
+    write-back to HBM happens there, outside the timed events), so the timed step starts with an
+    L2 of clean lines that hold none of its inputs, and pays for no one else's write-backs."""
 
     def __init__(self, flush):
+        import torch
         self.flush = flush
+        self.sink = torch.empty(1, dtype=flush.dtype, device=flush.device)
 
     def __call__(self, fn, reps, warmup=0):
         import torch
@@ -139,6 +144,7 @@ class Timer:
         evs = []
         for i in range(reps):
             self.flush.fill_(float(i))
+            self.sink.copy_(self.flush.sum().view(1))
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record()
             fn()
@@ -370,7 +376,7 @@ def run_gpu(args):
         "config": {"workload": "cfg4 causal GQA prefill (Qwen2.5-72B shape), sharded by kv-head group, every "
                                "rank's output rows stored into every rank's output (fused P2P epilogue over NVLink; "
                                "NCCL all-gather where peers are not reachable)", "B": B, "H": H, "KVH": KVH, "dh": dh, "T": T, "sink": False,
-                   "l2": "flushed (512 MB write) before each timed step; inputs (1.3 GB / N per rank) exceed L2",
+                   "l2": "flushed (512 MB write, then 512 MB read) before each timed step; inputs (1.3 GB / N per rank) exceed L2",
                    "parallelism": "kv-group x%d" % world, "chunk": chunk, "gather": "fused P2P" if peers else "NCCL",
                    "inputs": "numpy PCG64 seed 0, bf16 (generated in %.0f s)" % t_gen},
         "prefill_frac_int8_peak": round(value / world / int8_peak, 4),

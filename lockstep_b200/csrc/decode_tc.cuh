@@ -244,6 +244,7 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
       DecIter itr;
       itr.init(p);
       int jj = 0, run = -1, cur_bg = -1, b, g, blk;
+      const uint64_t once = l2_evict_first_policy();    // the lattice is read once per call
       while (itr.next(p, b, g, blk)) {
         const int bg = b * p.KVH + g;
         if (bg != cur_bg) {                              // a new (sequence, kv head): its Q^T tile
@@ -268,8 +269,8 @@ decode_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant
           int q = pg[i];
           if (q < 0 || q >= p.num_pages) { atomicOr(p.err, kDevBadPage); q = 0; }
           const long long prow = (long long)q * p.KVH + g;
-          tma_load_2d(kdst + i * L::kPage, &tm_k, 0, (int)(prow * 16), &bars[kDFull + st]);
-          bulk_g2s(vdst + i * L::kPage, p.v8p + prow * L::kPage, L::kPage, &bars[kDFull + st]);
+          tma_load_2d_hint(kdst + i * L::kPage, &tm_k, 0, (int)(prow * 16), &bars[kDFull + st], once);
+          bulk_g2s_hint(vdst + i * L::kPage, p.v8p + prow * L::kPage, L::kPage, &bars[kDFull + st], once);
         }
         ++jj;
       }
