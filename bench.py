@@ -172,7 +172,9 @@ def run_gpu(args):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
+        # short enough that ranks waiting on a rank that left end with an error, long enough for
+        # the slowest rank's input generation before the first collective
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
 
     def barrier():
         if world > 1:

@@ -74,7 +74,7 @@ class PeerOutputs:
         off = ctypes.c_uint64(0)
         _lib.check(L.lssab8_peer_export(self.local.data_ptr(), h, ctypes.byref(off)), "lssab8_peer_export")
         infos = [None] * self.world
-        dist.all_gather_object(infos, (bytes(h.raw), int(off.value), int(self.local.device.index)), group=group)
+        dist.all_gather_object(infos, (bytes(h.raw), int(off.value), self.local.get_device()), group=group)
         err = None
         with torch.cuda.device(self.local.device):
             for r, (hb, o, d) in enumerate(infos):
