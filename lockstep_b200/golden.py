@@ -17,6 +17,7 @@ NotImplementedError.  Computation runs on the current CUDA device; there is no C
 import numpy as np
 import torch
 
+from . import lssab8_torch as _B8
 from . import attention as A
 
 KB = 128
@@ -31,6 +32,7 @@ def _to_dev(x):
 
 
 def _core(q, k, v, mu, kb, q_exp_mode, causal, key_valid, sink, b9grid, v_keyshift, rows, heads, kw):
+    _B8.env_contract_check()
     if kb != KB:
         raise NotImplementedError("only the contract's 128-key blocks have a kernel (kb=%r)" % kb)
     if kw.get("weight", "rn") != "rn":

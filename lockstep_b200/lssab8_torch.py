@@ -29,7 +29,25 @@ NIDX = 7
 NB_SENT = -(1 << 58)
 
 
+# The reference selects a different contract version from the environment when it is imported
+# (reference/lssab8_golden.py:57-68, reference/lssab_golden.py:80): LSSAB8_SEG (segment size; 0 =
+# single-level fold), LSSAB8_RESCALE=mul (an RN-multiply rescale), LSSAB_TABLE=frac2 (another T2
+# table).  The kernels implement the filed contract only, so a session that selects another
+# version is refused rather than given the filed function under its name.
+_ENV_CONTRACT = (("LSSAB8_SEG", ("", "32")), ("LSSAB8_RESCALE", ("", "field")), ("LSSAB_TABLE", ("", "frac")))
+
+
+def env_contract_check():
+    import os
+    for var, ok in _ENV_CONTRACT:
+        val = os.environ.get(var, "")
+        if val not in ok:
+            raise NotImplementedError("%s=%s selects a contract variant with no B200 kernel (only the filed "
+                                      "contract: %s unset or %r)" % (var, val, var, ok[1]))
+
+
 def _contract_check(kb, bhi, n, w_loc, weight, s_win, seg_keys, mu, qexp, clamp_sh):
+    env_contract_check()
     assert n <= bhi and qexp in ("row", "head")
     assert seg_keys % kb == 0, "a segment must be a whole number of blocks"
     if (kb, bhi, n, w_loc, weight, s_win, seg_keys, bool(clamp_sh)) != (KB, BHI, NIDX, W_LOC, "rn", S_WIN,
