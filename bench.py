@@ -212,12 +212,25 @@ def run_gpu(args):
             peers = SH.PeerOutputs((B, T, H, dh), torch.bfloat16, dev)
         except Exception as e:                        # GPUs that cannot reach each other: NCCL gather
             peer_note = "peer buffers unavailable (%s); NCCL all-gather" % str(e)[:120]
-    out = peers.local if peers is not None else torch.empty((B, T, H, dh), dtype=torch.bfloat16, device=dev)
-    chunk = B if (world == 1 or peers is not None) else args.chunk
     ops4 = prefill_ops(B, H, T, dh)
+    nccl_out = None if (world > 1 and peers is not None) else torch.empty((B, T, H, dh), dtype=torch.bfloat16,
+                                                                           device=dev)
+    fused_ms = nccl_pick_ms = None
+    if world > 1 and peers is not None:
+        # The gather's form is chosen per run, on all ranks alike (both times are maxima over the
+        # ranks): the fused P2P epilogue stores cost (N - 1) / N of the output over NVLink from the
+        # kernel's own stores, which keep up at small N; the NCCL all-gather, pipelined over batch
+        # chunks, wins when that traffic outruns the stores.  Both give the same bits.
+        nccl_out = torch.empty((B, T, H, dh), dtype=torch.bfloat16, device=dev)
+        fused_ms = max_over_ranks(timer(lambda: SH.prefill_shard_gather(qd, kd, vd, H, peers=peers, chunk=B), 3, 1))
+        nccl_pick_ms = max_over_ranks(timer(lambda: SH.prefill_shard_gather(qd, kd, vd, H, out=nccl_out,
+                                                                           chunk=args.chunk), 3, 1))
+    use_fused = peers is not None and (nccl_pick_ms is None or fused_ms <= nccl_pick_ms)
+    out = peers.local if use_fused else nccl_out
+    chunk = B if (world == 1 or use_fused) else args.chunk
 
     def step4():
-        if peers is not None:
+        if use_fused:
             SH.prefill_shard_gather(qd, kd, vd, H, peers=peers, chunk=chunk)
         else:
             SH.prefill_shard_gather(qd, kd, vd, H, out=out, chunk=chunk)
@@ -254,12 +267,11 @@ def run_gpu(args):
 
     loc = torch.empty((B, T, h1 - h0, dh), dtype=torch.bfloat16, device=dev)
     t_comp = max_over_ranks(timer(lambda: A.prefill(qd, kd, vd, out=loc, check=False), args.steps, 1))
-    t_gath = t_nccl = None
+    t_gath = None
+    t_nccl = t4 if (world > 1 and not use_fused) else nccl_pick_ms     # the NCCL form's step (timed above)
     if world > 1:
-        nout = torch.empty((B, T, H, dh), dtype=torch.bfloat16, device=dev)
+        nout = nccl_out if use_fused else torch.empty((B, T, H, dh), dtype=torch.bfloat16, device=dev)
         t_gath = max_over_ranks(timer(lambda: SH._gather_into(nout, loc, world, None), args.steps, 1))
-        t_nccl = max_over_ranks(timer(lambda: SH.prefill_shard_gather(qd, kd, vd, H, out=nout, chunk=args.chunk),
-                                      args.steps, 1))
         del nout
 
     # the prefill kernel alone on this rank's whole shard (one launch)
@@ -282,7 +294,7 @@ def run_gpu(args):
     # output back to pinned host memory
     r0, r1 = rank * T // world, (rank + 1) * T // world
     hout = torch.empty((B, r1 - r0, H, dh), dtype=torch.bfloat16).pin_memory()
-    if peers is not None:
+    if use_fused:
         e2e_call = lambda: SH.prefill_shard_gather(qh, kh, vh, H, peers=peers, chunk=1, host_out=hout,  # noqa: E731
                                                    host_rows=(r0, r1))
     else:
@@ -369,17 +381,26 @@ def run_gpu(args):
         bit4 = bool(check4["samples"]) and check4.get("ranks_agree", True) is not False and \
             check4["n1_digest"] is not False
     launches = (B // chunk + (B % chunk > 0)) * 3                # Q quantiser, K/V quantiser, prefill per chunk
-    gather = ("fused: epilogue P2P stores into %d peer buffer(s) over NVLink (CUDA IPC), NCCL barriers around "
-              "the kernel" % (world - 1)) if peers is not None else (peer_note or "none (one GPU)")
+    if world == 1:
+        gather = "none (one GPU)"
+    elif use_fused:
+        gather = ("fused: epilogue P2P stores into %d peer buffer(s) over NVLink (CUDA IPC), NCCL barriers around "
+                  "the kernel (chosen: %.3f ms per step against %.3f ms for the NCCL all-gather form)"
+                  % (world - 1, fused_ms, nccl_pick_ms))
+    elif peers is not None:
+        gather = ("NCCL all-gather pipelined over batch chunks of %d (chosen: %.3f ms per step against %.3f ms for "
+                  "the fused P2P epilogue stores)" % (chunk, nccl_pick_ms, fused_ms))
+    else:
+        gather = peer_note or "NCCL all-gather"
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": "TOPS", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(t4, 4), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "int8 (bf16 in/out, int32 accumulate, binary32 fold)", "data": "synthetic",
         "config": {"workload": "cfg4 causal GQA prefill (Qwen2.5-72B shape), sharded by kv-head group, every "
-                               "rank's output rows stored into every rank's output (fused P2P epilogue over NVLink; "
-                               "NCCL all-gather where peers are not reachable)", "B": B, "H": H, "KVH": KVH, "dh": dh, "T": T, "sink": False,
+                               "rank's output rows gathered into every rank's output (the faster of the fused P2P "
+                               "epilogue stores over NVLink and the NCCL all-gather, timed per run)", "B": B, "H": H, "KVH": KVH, "dh": dh, "T": T, "sink": False,
                    "l2": "flushed (512 MB write, then 512 MB read) before each timed step; inputs (1.3 GB / N per rank) exceed L2",
-                   "parallelism": "kv-group x%d" % world, "chunk": chunk, "gather": "fused P2P" if peers else "NCCL",
+                   "parallelism": "kv-group x%d" % world, "chunk": chunk, "gather": "fused P2P" if use_fused else ("NCCL" if world > 1 else "none"),
                    "inputs": "numpy PCG64 seed 0, bf16 (generated in %.0f s)" % t_gen},
         "prefill_frac_int8_peak": round(value / world / int8_peak, 4),
         "bit_exact_vs_reference": bit4,
@@ -388,6 +409,7 @@ def run_gpu(args):
         "compute_ms": round(t_comp, 4), "gather_exposed_ms": round(t4 - t_comp, 4),
         "nccl_allgather_ms": None if t_gath is None else round(t_gath, 4),
         "nccl_step_ms": None if t_nccl is None else round(t_nccl, 4),
+        "fused_step_ms": None if fused_ms is None else round(fused_ms, 4),
         "roofline": roofline,
         "e2e": {"value": round(ops4 / (t_e2e * 1e-3) / 1e12, 3), "unit": "TOPS", "ms_per_step": round(t_e2e, 4),
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "host_rows_match": e2e_ok,
