@@ -215,7 +215,7 @@ def run_gpu(args):
     ops4 = prefill_ops(B, H, T, dh)
     nccl_out = None if (world > 1 and peers is not None) else torch.empty((B, T, H, dh), dtype=torch.bfloat16,
                                                                            device=dev)
-    fused_ms = nccl_pick_ms = None
+    fused_ms = copy_ms = nccl_pick_ms = None
     if world > 1 and peers is not None:
         # The gather's form is chosen per run, on all ranks alike (both times are maxima over the
         # ranks): the fused P2P epilogue stores cost (N - 1) / N of the output over NVLink from the
@@ -223,15 +223,19 @@ def run_gpu(args):
         # chunks, wins when that traffic outruns the stores.  Both give the same bits.
         nccl_out = torch.empty((B, T, H, dh), dtype=torch.bfloat16, device=dev)
         fused_ms = max_over_ranks(timer(lambda: SH.prefill_shard_gather(qd, kd, vd, H, peers=peers, chunk=B), 3, 1))
+        copy_ms = max_over_ranks(timer(lambda: SH.prefill_shard_gather(qd, kd, vd, H, peers=peers, chunk=1,
+                                                                      peer_copy=True), 3, 1))
         nccl_pick_ms = max_over_ranks(timer(lambda: SH.prefill_shard_gather(qd, kd, vd, H, out=nccl_out,
                                                                            chunk=args.chunk), 3, 1))
-    use_fused = peers is not None and (nccl_pick_ms is None or fused_ms <= nccl_pick_ms)
+    forms = {"fused": fused_ms, "copy": copy_ms, "nccl": nccl_pick_ms} if (world > 1 and peers is not None) else {}
+    mode = min(forms, key=forms.get) if forms else ("single" if world == 1 else "nccl")
+    use_fused = mode in ("fused", "copy")            # the result lives in the mapped peer buffers
     out = peers.local if use_fused else nccl_out
-    chunk = B if (world == 1 or use_fused) else args.chunk
+    chunk = {"fused": B, "copy": 1, "single": B}.get(mode, args.chunk)
 
     def step4():
         if use_fused:
-            SH.prefill_shard_gather(qd, kd, vd, H, peers=peers, chunk=chunk)
+            SH.prefill_shard_gather(qd, kd, vd, H, peers=peers, chunk=chunk, peer_copy=(mode == "copy"))
         else:
             SH.prefill_shard_gather(qd, kd, vd, H, out=out, chunk=chunk)
 
@@ -296,7 +300,7 @@ def run_gpu(args):
     hout = torch.empty((B, r1 - r0, H, dh), dtype=torch.bfloat16).pin_memory()
     if use_fused:
         e2e_call = lambda: SH.prefill_shard_gather(qh, kh, vh, H, peers=peers, chunk=1, host_out=hout,  # noqa: E731
-                                                   host_rows=(r0, r1))
+                                                   host_rows=(r0, r1), peer_copy=(mode == "copy"))
     else:
         e2e_call = lambda: SH.prefill_shard_gather(qh, kh, vh, H, out=out, chunk=1, host_out=hout,  # noqa: E731
                                                    host_rows=(r0, r1))
@@ -381,26 +385,31 @@ def run_gpu(args):
         bit4 = bool(check4["samples"]) and check4.get("ranks_agree", True) is not False and \
             check4["n1_digest"] is not False
     launches = (B // chunk + (B % chunk > 0)) * 3                # Q quantiser, K/V quantiser, prefill per chunk
+    forms_note = ("; per step, fused epilogue stores %.3f ms, copy engines %.3f ms, NCCL all-gather %.3f ms"
+                  % (fused_ms, copy_ms, nccl_pick_ms)) if forms else ""
     if world == 1:
         gather = "none (one GPU)"
-    elif use_fused:
+    elif mode == "fused":
         gather = ("fused: epilogue P2P stores into %d peer buffer(s) over NVLink (CUDA IPC), NCCL barriers around "
-                  "the kernel (chosen: %.3f ms per step against %.3f ms for the NCCL all-gather form)"
-                  % (world - 1, fused_ms, nccl_pick_ms))
-    elif peers is not None:
-        gather = ("NCCL all-gather pipelined over batch chunks of %d (chosen: %.3f ms per step against %.3f ms for "
-                  "the fused P2P epilogue stores)" % (chunk, nccl_pick_ms, fused_ms))
+                  "the kernel (the fastest form%s)" % (world - 1, forms_note))
+    elif mode == "copy":
+        gather = ("copy engines: after each batch element's compute, one 2D copy of this rank's head slab into each "
+                  "of %d peer buffer(s) over NVLink (CUDA IPC), under the next element's compute; NCCL barriers "
+                  "around the step (the fastest form%s)" % (world - 1, forms_note))
     else:
-        gather = peer_note or "NCCL all-gather"
+        gather = ("NCCL all-gather pipelined over batch chunks of %d%s" % (chunk, forms_note)) if forms else \
+            (peer_note or "NCCL all-gather")
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": "TOPS", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(t4, 4), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "int8 (bf16 in/out, int32 accumulate, binary32 fold)", "data": "synthetic",
         "config": {"workload": "cfg4 causal GQA prefill (Qwen2.5-72B shape), sharded by kv-head group, every "
-                               "rank's output rows gathered into every rank's output (the faster of the fused P2P "
-                               "epilogue stores over NVLink and the NCCL all-gather, timed per run)", "B": B, "H": H, "KVH": KVH, "dh": dh, "T": T, "sink": False,
+                               "rank's output rows gathered into every rank's output (the fastest of three forms, timed per run: "
+                               "P2P stores from the kernel's epilogue, P2P copy-engine copies per batch element, the "
+                               "NCCL all-gather)", "B": B, "H": H, "KVH": KVH, "dh": dh, "T": T, "sink": False,
                    "l2": "flushed (512 MB write, then 512 MB read) before each timed step; inputs (1.3 GB / N per rank) exceed L2",
-                   "parallelism": "kv-group x%d" % world, "chunk": chunk, "gather": "fused P2P" if use_fused else ("NCCL" if world > 1 else "none"),
+                   "parallelism": "kv-group x%d" % world, "chunk": chunk, "gather": {"fused": "fused P2P", "copy": "P2P copy engines", "nccl": "NCCL",
+                                                   "single": "none"}[mode],
                    "inputs": "numpy PCG64 seed 0, bf16 (generated in %.0f s)" % t_gen},
         "prefill_frac_int8_peak": round(value / world / int8_peak, 4),
         "bit_exact_vs_reference": bit4,
@@ -410,6 +419,7 @@ def run_gpu(args):
         "nccl_allgather_ms": None if t_gath is None else round(t_gath, 4),
         "nccl_step_ms": None if t_nccl is None else round(t_nccl, 4),
         "fused_step_ms": None if fused_ms is None else round(fused_ms, 4),
+        "copy_step_ms": None if copy_ms is None else round(copy_ms, 4),
         "roofline": roofline,
         "e2e": {"value": round(ops4 / (t_e2e * 1e-3) / 1e12, 3), "unit": "TOPS", "ms_per_step": round(t_e2e, 4),
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "host_rows_match": e2e_ok,

@@ -188,6 +188,13 @@ int lssab8_peer_export(const void* ptr, void* handle, uint64_t* offset);
 int lssab8_peer_import(const void* handle, uint64_t offset, int owner_device, void** ptr);
 int lssab8_peer_close(void* ptr, uint64_t offset);
 
+/* The sharded prefill's gather on the copy engines (no SM time): copies a height x width-byte
+ * slab, rows dpitch / spitch bytes apart, from this GPU's output to a peer's buffer mapped by
+ * lssab8_peer_import (cudaMemcpy2DAsync on `stream`, device to device over NVLink).  A rank's
+ * head slice of out [B, T, H, dh] is such a slab: width h*dh*e bytes, pitch H*dh*e, B*T rows. */
+int lssab8_peer_copy2d(void* dst, size_t dpitch, const void* src, size_t spitch, size_t width, size_t height,
+                       void* stream);
+
 /* ---------------------------------------------------------------------------- decode */
 
 /* Paged int8 lattice writer.  Sequence b has seq_lens[b] tokens; token t, kv head g, channel c

@@ -19,7 +19,7 @@ SYMBOLS = (
     "lssab8_quant_values_keyshift",
     "lssab8_prefill_lattice", "lssab8_prefill_lattice_general", "lssab8_prefill_lattice_keyshift",
     "lssab8_prefill_chunk_lattice", "lssab8_prefill_workspace_size", "lssab8_prefill",
-    "lssab8_prefill_peers", "lssab8_peer_export", "lssab8_peer_import", "lssab8_peer_close",
+    "lssab8_prefill_peers", "lssab8_peer_export", "lssab8_peer_import", "lssab8_peer_close", "lssab8_peer_copy2d",
     "lssab8_decode_prep_kv", "lssab8_kv_append", "lssab8_decode_workspace_size", "lssab8_decode",
     "lssab8_decode_noalloc", "lssab8_selftest_div", "lssab8_selftest_rescale", "lssab8_selftest_timeout",
 )
@@ -63,6 +63,7 @@ def load():
     L.lssab8_peer_export.argtypes = [P, P, ctypes.POINTER(ctypes.c_uint64)]
     L.lssab8_peer_import.argtypes = [P, ctypes.c_uint64, I, ctypes.POINTER(P)]
     L.lssab8_peer_close.argtypes = [P, ctypes.c_uint64]
+    L.lssab8_peer_copy2d.argtypes = [P, SZ, P, SZ, SZ, SZ, P]
     L.lssab8_decode_prep_kv.argtypes = [P, P, I, I, I, I, P, P, I64, I64, I64, P, I, I, I, I, P, P, P, P, P, P]
     L.lssab8_kv_append.argtypes = [P, P, I, I, I, I, P, P, P, I64, I64, P, I64, P, I, I, I, I, P, P, P, P, P, P]
     L.lssab8_decode_workspace_size.argtypes = [I] * 5

@@ -763,6 +763,14 @@ int lssab8_peer_close(void* ptr, uint64_t offset) {
   return cuda_rc(cudaIpcCloseMemHandle(static_cast<uint8_t*>(ptr) - offset));
 }
 
+int lssab8_peer_copy2d(void* dst, size_t dpitch, const void* src, size_t spitch, size_t width, size_t height,
+                       void* stream) {
+  if (!dst || !src || width == 0 || width > dpitch || width > spitch) return kErrArg;
+  if (height == 0) return kOk;
+  return cuda_rc(cudaMemcpy2DAsync(dst, dpitch, src, spitch, width, height, cudaMemcpyDeviceToDevice,
+                                   static_cast<cudaStream_t>(stream)));
+}
+
 }  // extern "C"
 
 // the vectorised lattice writer applies when channels are contiguous, dh is 64 or 128, and every

@@ -121,7 +121,7 @@ def _kernel_compute(q, k, v, sink, out):
 
 
 def prefill_shard_gather(q, k, v, H, sink=False, out=None, chunk=1, group=None, compute=None,
-                         host_out=None, host_rows=None, peers=None):
+                         host_out=None, host_rows=None, peers=None, peer_copy=False):
     """Sharded causal GQA prefill, gathered: every rank returns the whole out [B, T, H, dh].
 
     q [B, h, T, dh], k / v [B, kvh, T, dh]: this rank's shard, query heads [r*h, (r+1)*h) and kv
@@ -130,14 +130,17 @@ def prefill_shard_gather(q, k, v, H, sink=False, out=None, chunk=1, group=None, 
     elements per pipeline step.  compute(q, k, v, sink, out) -> out [b, T, h, dh] defaults to the
     B200 kernel (attention.prefill).  host_out [B, T1 - T0, H, dh] (pinned) receives rows
     host_rows = (T0, T1) of every gathered batch element.  The result's dtype is q's.
-    peers: a PeerOutputs of shape [B, T, H, dh]: the gather is fused into the kernel (the result
-    is peers.local; `out` and `compute` must be None)."""
+    peers: a PeerOutputs of shape [B, T, H, dh] (the result is peers.local; `out` must be None):
+    every rank's rows reach every rank's buffer over NVLink, stored by the prefill kernel's epilogue
+    (peer_copy=False; `compute` must be None), or copied by the copy engines after each chunk's
+    compute (peer_copy=True: one 2D copy of the chunk's head slice per peer, no SM time, under the
+    next chunk's compute)."""
     world, rank = _world(group)
     B, h, T, dh = q.shape
     if H != h * world:
         raise ValueError("H = %d query heads cannot be %d ranks x %d" % (H, world, h))
     if peers is not None:
-        if out is not None or compute is not None:
+        if out is not None or (compute is not None and not peer_copy):
             raise ValueError("with peers the result is peers.local and the kernel computes it")
         if tuple(peers.local.shape) != (B, T, H, dh) or peers.world != world:
             raise ValueError("the peer buffers do not match this call")
@@ -160,7 +163,8 @@ def prefill_shard_gather(q, k, v, H, sink=False, out=None, chunk=1, group=None, 
         return out
 
     cur = torch.cuda.current_stream(dev)
-    fused = peers is not None and world > 1
+    fused = peers is not None and world > 1 and not peer_copy
+    copying = peers is not None and world > 1 and peer_copy
     s_in = torch.cuda.Stream(dev) if not q.is_cuda else None
     s_comm = torch.cuda.Stream(dev) if world > 1 and not fused else None
     s_out = torch.cuda.Stream(dev) if host_out is not None else None
@@ -182,7 +186,7 @@ def prefill_shard_gather(q, k, v, H, sink=False, out=None, chunk=1, group=None, 
                 ev.record(s_in)
             loaded[c] = (t, ev)
         load(0)
-    if fused:
+    if fused or copying:
         peers.barrier()                               # every owner is done reading its buffer
     for c, (b0, b1) in enumerate(chunks):
         if loaded is not None:
@@ -196,6 +200,22 @@ def prefill_shard_gather(q, k, v, H, sink=False, out=None, chunk=1, group=None, 
             qc, kc, vc = q[b0:b1], k[b0:b1], v[b0:b1]
         if world == 1:
             compute(qc, kc, vc, sink, out[b0:b1])
+            done = out[b0:b1]
+        elif copying:
+            from . import _lib
+            mine = out[b0:b1, :, rank * h:(rank + 1) * h]
+            compute(qc, kc, vc, sink, mine)
+            ev = torch.cuda.Event()
+            ev.record(cur)
+            s_comm.wait_event(ev)
+            es = out.element_size()
+            L = _lib.load()
+            for a in peers.addresses(mine):           # the chunk's head slab: (b1 - b0) * T rows of h * dh
+                _lib.check(L.lssab8_peer_copy2d(a, H * dh * es, mine.data_ptr(), H * dh * es, h * dh * es,
+                                                (b1 - b0) * T, s_comm.cuda_stream), "lssab8_peer_copy2d")
+            if s_out is not None:
+                with torch.cuda.stream(s_comm):
+                    peers.barrier()                   # this chunk is complete on every rank
             done = out[b0:b1]
         elif fused:
             from . import attention as A
@@ -223,6 +243,8 @@ def prefill_shard_gather(q, k, v, H, sink=False, out=None, chunk=1, group=None, 
     for s in (s_comm, s_out):                         # the caller's stream sees the whole result
         if s is not None:
             cur.wait_stream(s)
+    if copying:
+        peers.barrier()                               # every rank's copies into every buffer have landed
     del keep
     return out
 

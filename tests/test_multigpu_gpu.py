@@ -1,6 +1,7 @@
 """The sharded path on two GPUs, on the real kernels: kv-head-group prefill with the pipelined
-NCCL output all-gather and with the gather fused into the kernel (epilogue P2P stores into the
-other rank's buffer, CUDA IPC), each from device inputs and from pinned host inputs with this
+NCCL output all-gather, with the gather fused into the kernel (epilogue P2P stores into the
+other rank's buffer, CUDA IPC) and with it on the copy engines (a 2D copy of each chunk's head slab
+into the other rank's buffer), each from device inputs and from pinned host inputs with this
 rank's rows read back; and sequence-partitioned paged decode.  Every rank's gathered output must equal the
 pinned oracle bit for bit, which is also the single-GPU result: no arithmetic crosses a rank.
 
@@ -66,6 +67,15 @@ def _worker(rank, world, port, ret):
         SH.prefill_shard_gather(qh, kh, vh, H, peers=peers, chunk=1, host_out=host3, host_rows=rows)
         torch.cuda.synchronize()
         out4 = peers.local.clone()
+        # the gather on the copy engines: each chunk's head slab copied into the other buffer
+        peers.local.fill_(float("nan"))
+        SH.prefill_shard_gather(qd, kd, vd, H, peers=peers, chunk=1, peer_copy=True)
+        out5 = peers.local.clone()
+        host5 = torch.empty_like(host).pin_memory()
+        peers.local.fill_(float("nan"))
+        SH.prefill_shard_gather(qh, kh, vh, H, peers=peers, chunk=2, host_out=host5, host_rows=rows, peer_copy=True)
+        torch.cuda.synchronize()
+        out6 = peers.local.clone()
         peers.close()
         # decode: sequences partitioned over the ranks, each rank quantises only its own
         lens = [700, 1, 130, 511, 256]
@@ -85,8 +95,9 @@ def _worker(rank, world, port, ret):
         dec = SH.decode_sharded(dq, lens, local)
         torch.cuda.synchronize()
         dig = lambda t: hashlib.sha256(t.cpu().view(torch.int16).numpy().tobytes()).hexdigest()
-        ret[rank] = dict(out1=dig(out1), out2=dig(out2), out3=dig(out3), out4=dig(out4),
-                         host=host.view(torch.int16).numpy().copy(), host3=host3.view(torch.int16).numpy().copy(),
+        ret[rank] = dict(out1=dig(out1), out2=dig(out2), out3=dig(out3), out4=dig(out4), out5=dig(out5),
+                         out6=dig(out6), host=host.view(torch.int16).numpy().copy(),
+                         host3=host3.view(torch.int16).numpy().copy(), host5=host5.view(torch.int16).numpy().copy(),
                          rows=rows, dec=dec.cpu().view(torch.int16).numpy().copy())
         if rank == 0:
             ret["full"] = out1.cpu().view(torch.int16).numpy().copy()
@@ -107,11 +118,11 @@ def test_two_nccl_ranks_equal_oracle():
     full = ret["full"].view(np.uint16)
     assert np.array_equal(full, ref)
     for r in range(2):
-        for key in ("out1", "out2", "out3", "out4"):
+        for key in ("out1", "out2", "out3", "out4", "out5", "out6"):
             assert ret[r][key] == ret[0]["out1"], (r, key)
         t0, t1 = ret[r]["rows"]
-        assert np.array_equal(ret[r]["host"].view(np.uint16), ref[:, t0:t1]), r
-        assert np.array_equal(ret[r]["host3"].view(np.uint16), ref[:, t0:t1]), r
+        for key in ("host", "host3", "host5"):
+            assert np.array_equal(ret[r][key].view(np.uint16), ref[:, t0:t1]), (r, key)
         assert np.array_equal(ret[r]["dec"], ret[0]["dec"]), r
     dq, dk, dv, lens = ret["dq"], ret["dk"], ret["dv"], ret["lens"]
     dec = ret[0]["dec"].view(np.uint16)
