@@ -167,10 +167,12 @@ def prefill_shard_gather(q, k, v, H, sink=False, out=None, chunk=1, group=None, 
     copying = peers is not None and world > 1 and peer_copy
     s_in = torch.cuda.Stream(dev) if not q.is_cuda else None
     s_comm = torch.cuda.Stream(dev) if world > 1 and not fused else None
+    # copy mode: one stream per peer, so the copies to different peers run on different copy engines
+    s_peer = [torch.cuda.Stream(dev) for _ in range(world - 1)] if copying else []
     s_out = torch.cuda.Stream(dev) if host_out is not None else None
     start = torch.cuda.Event()
     start.record(cur)
-    for s in (s_in, s_comm, s_out):
+    for s in [s_in, s_comm, s_out] + s_peer:
         if s is not None:
             s.wait_event(start)
     keep = []                                         # buffers used on the side streams
@@ -207,13 +209,15 @@ def prefill_shard_gather(q, k, v, H, sink=False, out=None, chunk=1, group=None, 
             compute(qc, kc, vc, sink, mine)
             ev = torch.cuda.Event()
             ev.record(cur)
-            s_comm.wait_event(ev)
             es = out.element_size()
             L = _lib.load()
-            for a in peers.addresses(mine):           # the chunk's head slab: (b1 - b0) * T rows of h * dh
+            for sp, a in zip(s_peer, peers.addresses(mine)):   # the chunk's head slab: (b1 - b0) T rows of h dh
+                sp.wait_event(ev)
                 _lib.check(L.lssab8_peer_copy2d(a, H * dh * es, mine.data_ptr(), H * dh * es, h * dh * es,
-                                                (b1 - b0) * T, s_comm.cuda_stream), "lssab8_peer_copy2d")
+                                                (b1 - b0) * T, sp.cuda_stream), "lssab8_peer_copy2d")
             if s_out is not None:
+                for sp in s_peer:
+                    s_comm.wait_stream(sp)
                 with torch.cuda.stream(s_comm):
                     peers.barrier()                   # this chunk is complete on every rank
             done = out[b0:b1]
@@ -240,7 +244,7 @@ def prefill_shard_gather(q, k, v, H, sink=False, out=None, chunk=1, group=None, 
             s_out.wait_event(ev)
             with torch.cuda.stream(s_out):
                 host_out[b0:b1].copy_(done[:, T0:T1], non_blocking=True)
-    for s in (s_comm, s_out):                         # the caller's stream sees the whole result
+    for s in [s_comm, s_out] + s_peer:               # the caller's stream sees the whole result
         if s is not None:
             cur.wait_stream(s)
     if copying:
