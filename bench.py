@@ -5,13 +5,15 @@ Headline workload (BASELINE.json configs[3] = config 4, the configuration the no
 Qwen2.5-72B-shaped causal GQA prefill, B=8, 64 query / 8 kv heads, dh 128, T 8192, bf16 inputs
 N(0,1) from seed 0, sink off, sharded over the N ranks by kv-head group (rank r owns kv heads
 [r*8/N, (r+1)*8/N) and their query heads) with the outputs gathered on every rank.  One step =
-the whole job: a barrier, every rank's PREP quantisers and persistent tcgen05 prefill kernel over
-its heads -- whose epilogue stores each finished output tile into its own [B, T, H, dh] buffer
-and, over NVLink, into every other rank's (CUDA IPC peer buffers: the gather fused into the
-kernel) -- and a closing barrier; value = 8.797e12 ops / the max-over-ranks step time (strong
-scaling: the total work is fixed).  The NCCL all-gather form of the same step is timed beside
-it.  Inputs are resident in HBM when the timed region starts; L2 is flushed (a 512 MB write, then a
-512 MB read that evicts the write's dirty lines) before every timed step, outside the timed events.
+the whole job: every rank's PREP quantisers and persistent tcgen05 prefill kernel over its heads,
+and the gather of every rank's rows into every rank's [B, T, H, dh] buffer in the fastest of three
+forms, each timed for a few steps first (maxima over the ranks, so that all ranks choose alike):
+the kernel's epilogue storing each finished tile into the peers' buffers over NVLink (CUDA IPC),
+the copy engines copying each batch element's head slab into them under the next element's
+compute, or the NCCL all-gather pipelined over batch chunks; value = 8.797e12 ops / the
+max-over-ranks step time (strong scaling: the total work is fixed).  Inputs are resident in HBM
+when the timed region starts; L2 is flushed (a 512 MB write, then a 512 MB read that evicts the
+write's dirty lines) before every timed step, outside the timed events.
 
 Also in the line: the compute alone and the gather alone; the prefill kernel's roofline; the
 end-to-end public-API call (pinned host shard -> device -> gathered -> this rank's rows back to
